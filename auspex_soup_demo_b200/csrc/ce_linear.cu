@@ -1,0 +1,609 @@
+// Fused lm_head cross-entropy on tcgen05, and the plain GEMM entry point.
+//
+// One soup_ce_linear call over `rows` tokens runs:
+//   1. logits GEMM  L = H W^T  (M=rows, N=vocab, K=dim; A, B K-major) whose
+//      epilogue, per row and 256-column vocab tile, keeps the online-softmax
+//      state (max, sum exp, sum z*exp, first argmax), captures the target
+//      logit, and stores the logits as bf16 into the workspace;
+//   2. ce_finalize: per row, merges the tile states (ties keep the smaller
+//      index), writes loss / entropy / hit, and rewrites the row's logits in
+//      place as dlogits = (softmax - onehot) / denominator (0 for ignored rows);
+//   3. ce_sums: fixed-order sums of the per-row losses and hits;
+//   4. dX GEMM  dH = dL W  (A = dL K-major, B = W MN-major), split along the
+//      vocab into fp32 partials, then a fixed-order reduce to bf16;
+//   5. dW GEMM  dW = dL^T H  (A = dL MN-major, B = H MN-major).
+// This follows the semantics of chunk_cross_entropy_triton and its kernel in
+// the reference (solution/kernels/chunked_ce.py:32-128, 183-264).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <stdio.h>
+
+#include "soup_common.cuh"
+#include "tc_gemm.cuh"
+
+namespace soup {
+namespace tc {
+
+using bf16 = __nv_bfloat16;
+
+// ------------------------------------------------------------- epilogues ---
+// Plain store: C = alpha * acc (+ C). `split_stride` > 0 writes k-split
+// partial slices (fp32) at C + ks * split_stride.
+template <int BN>
+struct EpiStore {
+  struct Params {
+    void* c;
+    int64_t ldc;
+    int64_t split_stride;
+    float alpha;
+    int c_bf16;
+    int accumulate;
+    int vec_ok;  // 16-byte aligned rows
+    int M, N;
+  };
+  static __device__ __forceinline__ void tile(const Params& p, int mt, int nt, int ks, int quarter,
+                                              int lane, uint32_t taddr) {
+    const int row = mt * BM + quarter * 32 + lane;
+    const bool row_ok = row < p.M;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      tmem_ld32(taddr + c * 32, v);
+      const int col0 = nt * BN + c * 32;
+      if (!row_ok || col0 >= p.N) continue;
+      const bool full = (col0 + 32 <= p.N) && p.vec_ok;
+      if (p.c_bf16) {
+        bf16* dst = reinterpret_cast<bf16*>(p.c) + ks * p.split_stride + (int64_t)row * p.ldc + col0;
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            Vec16<bf16> o;
+            if (p.accumulate) o = ld16(dst + q * 8);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float x = p.alpha * v[q * 8 + j];
+              if (p.accumulate) x += __bfloat162float(o.v[j]);
+              o.v[j] = __float2bfloat16_rn(x);
+            }
+            st16(dst + q * 8, o);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < p.N) {
+              float x = p.alpha * v[j];
+              if (p.accumulate) x += __bfloat162float(dst[j]);
+              dst[j] = __float2bfloat16_rn(x);
+            }
+          }
+        }
+      } else {
+        float* dst = reinterpret_cast<float*>(p.c) + ks * p.split_stride + (int64_t)row * p.ldc + col0;
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (p.accumulate) o = *reinterpret_cast<const float4*>(dst + q * 4);
+            o.x += p.alpha * v[q * 4 + 0];
+            o.y += p.alpha * v[q * 4 + 1];
+            o.z += p.alpha * v[q * 4 + 2];
+            o.w += p.alpha * v[q * 4 + 3];
+            *reinterpret_cast<float4*>(dst + q * 4) = o;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < p.N) {
+              float x = p.alpha * v[j];
+              if (p.accumulate) x += dst[j];
+              dst[j] = x;
+            }
+          }
+        }
+      }
+    }
+  }
+};
+
+// Logits epilogue of the CE forward: online-softmax state per (row, tile),
+// target logit capture, bf16 logits store.
+template <int BN>
+struct EpiCE {
+  struct Params {
+    const int64_t* targets;
+    float4* partials;  // [n_tiles][M]: (max, sum exp, sum z*exp, argmax bits)
+    float* zt;         // [M] target logit (written by the tile holding it)
+    bf16* logits;      // [M][ld_logits] or nullptr
+    int64_t ld_logits;
+    int M, N;
+  };
+  static __device__ __forceinline__ void tile(const Params& p, int mt, int nt, int ks, int quarter,
+                                              int lane, uint32_t taddr) {
+    const int row = mt * BM + quarter * 32 + lane;
+    const bool row_ok = row < p.M;
+    const int64_t t = row_ok ? p.targets[row] : -1;
+    float m = -INFINITY, s = 0.f, w = 0.f;
+    int bidx = 0x7fffffff;
+    float ztv = 0.f;
+    bool found = false;
+    bf16* lrow = (row_ok && p.logits) ? p.logits + (int64_t)row * p.ld_logits : nullptr;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      tmem_ld32(taddr + c * 32, v);
+      const int col0 = nt * BN + c * 32;
+      const int nvalid = p.N - col0;
+      if (nvalid <= 0) continue;
+      if (nvalid < 32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j >= nvalid) v[j] = -INFINITY;
+      }
+      // chunk maximum with its first index
+      float cm = v[0];
+      int ci = 0;
+#pragma unroll
+      for (int j = 1; j < 32; ++j)
+        if (v[j] > cm) {
+          cm = v[j];
+          ci = j;
+        }
+      if (cm > m) {
+        const float f = fast_exp2((m - cm) * kLog2e);  // 0 when m = -inf
+        s *= f;
+        w *= f;
+        m = cm;
+        bidx = col0 + ci;
+      }
+      const float mb = m * kLog2e;
+      if (nvalid >= 32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float e = fast_exp2(fmaf(v[j], kLog2e, -mb));
+          s += e;
+          w = fmaf(v[j], e, w);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (j < nvalid) {
+            const float e = fast_exp2(fmaf(v[j], kLog2e, -mb));
+            s += e;
+            w = fmaf(v[j], e, w);
+          }
+        }
+      }
+      if (t >= col0 && t < col0 + 32 && t < p.N) {
+        const int tj = static_cast<int>(t - col0);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j == tj) ztv = v[j];
+        found = true;
+      }
+      if (lrow) {
+        bf16* dst = lrow + col0;
+        if (nvalid >= 32) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            Vec16<bf16> o;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o.v[j] = __float2bfloat16_rn(v[q * 8 + j]);
+            st16(dst + q * 8, o);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < nvalid) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+    if (row_ok) {
+      p.partials[(int64_t)nt * p.M + row] = make_float4(m, s, w, __int_as_float(bidx));
+      if (found) p.zt[row] = ztv;
+    }
+  }
+};
+
+// ------------------------------------------------------- tensor maps -------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 map over a row-major matrix [outer, inner] with row stride ld
+// (elements), box {64, box_outer}, 128-byte swizzle, zero fill out of bounds.
+static int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                    uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_last_error("cuTensorMapEncodeTiled is not available from the driver");
+    return SOUP_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char msg[160];
+    snprintf(msg, sizeof(msg), "cuTensorMapEncodeTiled failed (%d): inner=%llu outer=%llu ld=%llu",
+             static_cast<int>(r), (unsigned long long)inner, (unsigned long long)outer,
+             (unsigned long long)ld);
+    set_last_error(msg);
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  return SOUP_OK;
+}
+
+// Operand map: K-major operand stored [rows, K]: box {64 (K), rows_box};
+// MN-major operand stored [K, rows]: box {64 (MN), 64 (K)}.
+static int make_operand_map(CUtensorMap* map, const void* ptr, bool mn_major, int64_t rows, int64_t k,
+                            int64_t ld, int rows_box) {
+  if (mn_major) return make_map(map, ptr, rows, k, ld, 64);
+  return make_map(map, ptr, k, rows, ld, rows_box);
+}
+
+static bool tma_ok(const void* p, int64_t ld) {
+  return aligned16(p) && ((ld * 2) % 16 == 0) && ld > 0;
+}
+
+constexpr int kBN = 256;
+constexpr int kStages = 4;
+
+template <bool A_MN, bool B_MN, class Epi>
+static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
+                       const typename Epi::Params& ep, cudaStream_t stream) {
+  using L = SmemLayout<kBN, kStages>;
+  auto kern = gemm_kernel<kBN, kStages, A_MN, B_MN, Epi>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    attr_set[dev] = true;
+  }
+  const int units = sched.m_tiles * sched.n_tiles * sched.splits;
+  if (units <= 0) return SOUP_OK;
+  int* err = device_err_ptr();
+  if (!err) {
+    set_last_error("device error word unavailable");
+    return SOUP_ERR_CUDA;
+  }
+  const int grid = units < num_sms() ? units : num_sms();
+  kern<<<grid, kThreads, L::kBytes, stream>>>(ma, mb, sched, ep, err);
+  return launch_status();
+}
+
+// ------------------------------------------------------ CE row kernels -----
+// Per row: merge the tile states, metrics, then dlogits in place.
+__global__ void __launch_bounds__(512) ce_finalize_kernel(
+    const float4* __restrict__ partials, int n_tiles, const float* __restrict__ zt,
+    const int64_t* __restrict__ targets, bf16* __restrict__ logits, int64_t ld_logits, int rows,
+    int vocab, float inv_den, int64_t ignore_index, float* __restrict__ losses,
+    float* __restrict__ entropies, int32_t* __restrict__ correct, int write_grad) {
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  __shared__ SoftmaxState red[16];
+  __shared__ float s_lse;
+  SoftmaxState st = sm_init();
+  for (int j = threadIdx.x; j < n_tiles; j += blockDim.x) {
+    float4 p = partials[(int64_t)j * rows + row];
+    SoftmaxState b{p.x, p.y, p.z, __float_as_int(p.w)};
+    st = sm_merge(st, b);
+  }
+  st = sm_warp_reduce(st);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = st;
+  __syncthreads();
+  const int64_t t = targets[row];
+  const bool ignored = (t == ignore_index);
+  if (threadIdx.x == 0) {
+    SoftmaxState r = red[0];
+    const int nw = blockDim.x >> 5;
+    for (int i = 1; i < nw; ++i) r = sm_merge(r, red[i]);
+    const float safe_s = fmaxf(r.s, 1e-12f);
+    const float lse = r.m + logf(safe_s);
+    const bool in_range = (t >= 0 && t < vocab);
+    const float z_t = in_range ? zt[row] : 0.f;
+    float loss = ignored ? 0.f : (lse - z_t);
+    float ent = fmaxf(0.f, lse - r.w / safe_s);
+    if (!isfinite(loss)) loss = 0.f;
+    if (!isfinite(ent)) ent = 0.f;
+    losses[row] = loss;
+    entropies[row] = ent;
+    correct[row] = (!ignored && in_range && r.idx == static_cast<int>(t)) ? 1 : 0;
+    s_lse = lse;
+  }
+  if (!write_grad) return;
+  __syncthreads();
+  bf16* lrow = logits + (int64_t)row * ld_logits;
+  const int nvec = vocab / 8;
+  if (ignored) {
+    Vec16<bf16> zero;
+    zero.u = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) st16(lrow + i * 8, zero);
+    for (int c = nvec * 8 + threadIdx.x; c < vocab; c += blockDim.x) lrow[c] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  const float lb = s_lse * kLog2e;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    Vec16<bf16> z = ld16(lrow + i * 8);
+    Vec16<bf16> o;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float p = fast_exp2(fmaf(__bfloat162float(z.v[j]), kLog2e, -lb));
+      if (i * 8 + j == t) p -= 1.f;
+      o.v[j] = __float2bfloat16_rn(p * inv_den);
+    }
+    st16(lrow + i * 8, o);
+  }
+  for (int c = nvec * 8 + threadIdx.x; c < vocab; c += blockDim.x) {
+    float p = fast_exp2(fmaf(__bfloat162float(lrow[c]), kLog2e, -lb));
+    if (c == t) p -= 1.f;
+    lrow[c] = __float2bfloat16_rn(p * inv_den);
+  }
+}
+
+// sums[0] = sum of losses, sums[1] = number of hits; one block, fixed order.
+__global__ void __launch_bounds__(1024) ce_sums_kernel(const float* __restrict__ losses,
+                                                       const int32_t* __restrict__ correct,
+                                                       int rows, float* __restrict__ sums) {
+  __shared__ float sl[32], sc[32];
+  float a = 0.f, b = 0.f;
+  for (int i = threadIdx.x; i < rows; i += blockDim.x) {
+    a += losses[i];
+    b += static_cast<float>(correct[i]);
+  }
+  a = warp_sum(a);
+  b = warp_sum(b);
+  if ((threadIdx.x & 31) == 0) {
+    sl[threadIdx.x >> 5] = a;
+    sc[threadIdx.x >> 5] = b;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float ta = 0.f, tb = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) {
+      ta += sl[i];
+      tb += sc[i];
+    }
+    sums[0] = ta;
+    sums[1] = tb;
+  }
+}
+
+// out[m, n] = bf16(sum_s ws[s][m][n]), fixed order over s.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t slice,
+                                     int rows, int cols, bf16* __restrict__ out, int64_t ldo) {
+  const int64_t n4 = (int64_t)rows * cols / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i * 4;
+    float4 acc = *reinterpret_cast<const float4*>(ws + e);
+    for (int s = 1; s < splits; ++s) {
+      float4 v = *reinterpret_cast<const float4*>(ws + s * slice + e);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const int64_t r = e / cols, c = e % cols;
+    bf16* o = out + r * ldo + c;
+    o[0] = __float2bfloat16_rn(acc.x);
+    o[1] = __float2bfloat16_rn(acc.y);
+    o[2] = __float2bfloat16_rn(acc.z);
+    o[3] = __float2bfloat16_rn(acc.w);
+  }
+}
+
+// ------------------------------------------------------- stage events ------
+static thread_local cudaEvent_t g_stage_events[8];
+static thread_local int g_n_stage_events = 0;
+
+static void mark_stage(int i, cudaStream_t s) {
+  if (i < g_n_stage_events && g_stage_events[i]) cudaEventRecord(g_stage_events[i], s);
+}
+
+// ---------------------------------------------------- workspace layout -----
+struct CEWorkspace {
+  int64_t ld_logits;
+  int n_vtiles;
+  int splits;
+  size_t off_logits, off_partials, off_zt, off_splitk, total;
+};
+
+static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+static int choose_splits(int64_t rows, int64_t dim, int64_t vocab, int sms) {
+  const int64_t tiles = ((rows + BM - 1) / BM) * ((dim + kBN - 1) / kBN);
+  int64_t s = (2 * sms + tiles - 1) / tiles;  // about two waves of work units
+  const int64_t kb = (vocab + BK - 1) / BK;
+  if (s > kb / 16) s = kb / 16;              // keep >= 16 k-blocks per unit
+  if (s < 1) s = 1;
+  if (s > 16) s = 16;
+  return static_cast<int>(s);
+}
+
+static CEWorkspace ce_layout(int64_t rows, int64_t vocab, int64_t dim) {
+  CEWorkspace w;
+  w.ld_logits = (vocab + 7) / 8 * 8;
+  w.n_vtiles = static_cast<int>((vocab + kBN - 1) / kBN);
+  w.splits = choose_splits(rows, dim, vocab, num_sms());
+  size_t off = 0;
+  w.off_logits = off;
+  off = align_up(off + (size_t)rows * w.ld_logits * 2, 256);
+  w.off_partials = off;
+  off = align_up(off + (size_t)w.n_vtiles * rows * 16, 256);
+  w.off_zt = off;
+  off = align_up(off + (size_t)rows * 4, 256);
+  w.off_splitk = off;
+  off = align_up(off + (size_t)w.splits * rows * dim * 4, 256);
+  w.total = off;
+  return w;
+}
+
+}  // namespace tc
+}  // namespace soup
+
+using namespace soup;
+using namespace soup::tc;
+
+extern "C" {
+
+size_t soup_ce_linear_workspace_bytes(int64_t rows, int64_t vocab, int64_t dim) {
+  if (rows <= 0 || vocab <= 0 || dim <= 0) return 0;
+  return ce_layout(rows, vocab, dim).total;
+}
+
+int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t w_ld,
+                   const int64_t* targets, int64_t rows, int64_t vocab, int64_t dim,
+                   float denominator, int64_t ignore_index, float* losses, float* entropies,
+                   int32_t* correct, float* sums, void* dhidden, void* dweight, int dw_dtype,
+                   int accumulate_dw, void* workspace, size_t workspace_bytes, void* stream_) {
+  if (!hidden || !weight || !targets || !losses || !entropies || !correct || !workspace) {
+    set_last_error("soup_ce_linear: null pointer argument");
+    return SOUP_ERR_INVALID;
+  }
+  if (rows <= 0 || vocab <= 0 || dim <= 0 || rows > (1 << 30) || vocab > (1 << 30) ||
+      h_ld < dim || w_ld < dim) {
+    set_last_error("soup_ce_linear: bad sizes");
+    return SOUP_ERR_INVALID;
+  }
+  if (dweight && dw_dtype != SOUP_F32 && dw_dtype != SOUP_BF16) {
+    set_last_error("soup_ce_linear: dweight dtype must be F32 or BF16");
+    return SOUP_ERR_INVALID;
+  }
+  if (!tma_ok(hidden, h_ld) || !tma_ok(weight, w_ld) || (dim % 8) != 0) {
+    set_last_error("soup_ce_linear: hidden/weight need 16-byte aligned rows and dim % 8 == 0");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  CEWorkspace w = ce_layout(rows, vocab, dim);
+  if (workspace_bytes < w.total || !aligned16(workspace)) {
+    set_last_error("soup_ce_linear: workspace too small or misaligned");
+    return SOUP_ERR_WORKSPACE;
+  }
+  cudaStream_t stream = as_stream(stream_);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  bf16* L = reinterpret_cast<bf16*>(ws + w.off_logits);
+  float4* partials = reinterpret_cast<float4*>(ws + w.off_partials);
+  float* zt = reinterpret_cast<float*>(ws + w.off_zt);
+  float* splitk = reinterpret_cast<float*>(ws + w.off_splitk);
+  const bool need_grad = dhidden || dweight;
+  const int M = static_cast<int>(rows), V = static_cast<int>(vocab), D = static_cast<int>(dim);
+  int rc;
+
+  // 1. logits GEMM + online-softmax epilogue
+  {
+    CUtensorMap ma, mb;
+    if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
+    if ((rc = make_operand_map(&mb, weight, false, vocab, dim, w_ld, kBN))) return rc;
+    Sched sc{(M + BM - 1) / BM, w.n_vtiles, 1, (D + BK - 1) / BK, 0};
+    EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, M, V};
+    if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, sc, ep, stream))) return rc;
+    mark_stage(0, stream);
+  }
+  // 2. metrics + dlogits
+  {
+    const float den = denominator > 0.f ? denominator : 1.f;
+    ce_finalize_kernel<<<M, 512, 0, stream>>>(partials, w.n_vtiles, zt, targets, L, w.ld_logits, M,
+                                               V, 1.f / den, ignore_index, losses, entropies,
+                                               correct, need_grad ? 1 : 0);
+    if ((rc = launch_status())) return rc;
+    mark_stage(1, stream);
+  }
+  if (sums) {
+    ce_sums_kernel<<<1, 1024, 0, stream>>>(losses, correct, M, sums);
+    if ((rc = launch_status())) return rc;
+    mark_stage(2, stream);
+  }
+  // 4. dH = dL W  (split along the vocab)
+  if (dhidden) {
+    CUtensorMap ma, mb;
+    if ((rc = make_operand_map(&ma, L, false, rows, vocab, w.ld_logits, BM))) return rc;
+    if ((rc = make_operand_map(&mb, weight, true, dim, vocab, w_ld, 64))) return rc;
+    Sched sc{(M + BM - 1) / BM, (D + kBN - 1) / kBN, w.splits, (V + BK - 1) / BK, 1};
+    EpiStore<kBN>::Params ep{splitk, dim, (int64_t)rows * dim, 1.f, 0, 0, 1, M, D};
+    if ((rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, sc, ep, stream))) return rc;
+    mark_stage(3, stream);
+    const int64_t n4 = (int64_t)rows * dim / 4;
+    int blocks = static_cast<int>((n4 + 255) / 256);
+    if (blocks > 4 * num_sms()) blocks = 4 * num_sms();
+    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(splitk, w.splits, (int64_t)rows * dim, M, D,
+                                                    static_cast<bf16*>(dhidden), dim);
+    if ((rc = launch_status())) return rc;
+    mark_stage(4, stream);
+  }
+  // 5. dW = dL^T H
+  if (dweight) {
+    CUtensorMap ma, mb;
+    if ((rc = make_operand_map(&ma, L, true, vocab, rows, w.ld_logits, 64))) return rc;
+    if ((rc = make_operand_map(&mb, hidden, true, dim, rows, h_ld, 64))) return rc;
+    Sched sc{(V + BM - 1) / BM, (D + kBN - 1) / kBN, 1, (M + BK - 1) / BK, 1};
+    const int es = dw_dtype == SOUP_BF16 ? 2 : 4;
+    EpiStore<kBN>::Params ep{dweight, dim, 0, 1.f, dw_dtype == SOUP_BF16 ? 1 : 0,
+                             accumulate_dw ? 1 : 0,
+                             (aligned16(dweight) && (dim * es) % 16 == 0) ? 1 : 0, V, D};
+    if ((rc = launch_gemm<true, true, EpiStore<kBN>>(ma, mb, sc, ep, stream))) return rc;
+    mark_stage(5, stream);
+  }
+  return SOUP_OK;
+}
+
+int soup_set_stage_events(void** events, int n) {
+  if (n < 0 || n > 8 || (n > 0 && !events)) {
+    set_last_error("soup_set_stage_events: n must be 0..8");
+    return SOUP_ERR_INVALID;
+  }
+  for (int i = 0; i < 8; ++i) g_stage_events[i] = (i < n) ? static_cast<cudaEvent_t>(events[i]) : nullptr;
+  g_n_stage_events = n;
+  return SOUP_OK;
+}
+
+int soup_gemm_bf16(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb,
+                   int b_mn_major, void* c, int64_t ldc, int c_dtype, int64_t m, int64_t n,
+                   int64_t k, float alpha, int accumulate, void* stream_) {
+  if (!a || !b || !c || m <= 0 || n <= 0 || k <= 0 || m > (1 << 30) || n > (1 << 30)) {
+    set_last_error("soup_gemm_bf16: bad arguments");
+    return SOUP_ERR_INVALID;
+  }
+  if (c_dtype != SOUP_F32 && c_dtype != SOUP_BF16) {
+    set_last_error("soup_gemm_bf16: C dtype must be F32 or BF16");
+    return SOUP_ERR_INVALID;
+  }
+  if ((a_mn_major ? lda < m : lda < k) || (b_mn_major ? ldb < n : ldb < k) || ldc < n) {
+    set_last_error("soup_gemm_bf16: leading dimension too small");
+    return SOUP_ERR_INVALID;
+  }
+  if (!tma_ok(a, lda) || !tma_ok(b, ldb)) {
+    set_last_error("soup_gemm_bf16: operands need 16-byte aligned rows");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_operand_map(&ma, a, a_mn_major != 0, m, k, lda, BM))) return rc;
+  if ((rc = make_operand_map(&mb, b, b_mn_major != 0, n, k, ldb, kBN))) return rc;
+  const int es = c_dtype == SOUP_BF16 ? 2 : 4;
+  EpiStore<kBN>::Params ep{c, ldc, 0, alpha, c_dtype == SOUP_BF16 ? 1 : 0, accumulate ? 1 : 0,
+                           (aligned16(c) && (ldc * es) % 16 == 0) ? 1 : 0, (int)m, (int)n};
+  const int mt = (int)((m + BM - 1) / BM), nt = (int)((n + kBN - 1) / kBN);
+  Sched sc{mt, nt, 1, (int)((k + BK - 1) / BK), nt > mt ? 0 : 1};
+  cudaStream_t stream = as_stream(stream_);
+  if (!a_mn_major && !b_mn_major) return launch_gemm<false, false, EpiStore<kBN>>(ma, mb, sc, ep, stream);
+  if (!a_mn_major && b_mn_major) return launch_gemm<false, true, EpiStore<kBN>>(ma, mb, sc, ep, stream);
+  if (a_mn_major && !b_mn_major) return launch_gemm<true, false, EpiStore<kBN>>(ma, mb, sc, ep, stream);
+  return launch_gemm<true, true, EpiStore<kBN>>(ma, mb, sc, ep, stream);
+}
+
+}  // extern "C"

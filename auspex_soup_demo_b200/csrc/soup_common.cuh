@@ -1,0 +1,135 @@
+// Shared helpers for the sm_100a kernels: dtype traits, 128-bit vector
+// access, warp/block reductions, status handling.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "../../include/soupb200.h"
+
+namespace soup {
+
+// ---------------------------------------------------------------- status ----
+void set_last_error(const char* msg);
+int cuda_status(cudaError_t e);                      // records the text, maps to SOUP_ERR_CUDA
+inline int launch_status() { return cuda_status(cudaGetLastError()); }
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int num_sms();                                       // of the current device (cached)
+int* device_err_ptr();                               // device error word of the current device
+
+// ---------------------------------------------------------------- dtypes ----
+template <typename T> struct Cvt;
+template <> struct Cvt<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Cvt<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <> struct Cvt<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// A 16-byte vector of T: 4 floats or 8 halves.
+template <typename T> struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  union {
+    uint4 u;
+    T v[N];
+  };
+};
+
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld16(const T* p) {
+  Vec16<T> r;
+  r.u = *reinterpret_cast<const uint4*>(p);
+  return r;
+}
+// Streaming load: data read once, keep it out of L1.
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld16_stream(const T* p) {
+  Vec16<T> r;
+  r.u = __ldcs(reinterpret_cast<const uint4*>(p));
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ void st16(T* p, const Vec16<T>& r) {
+  *reinterpret_cast<uint4*>(p) = r.u;
+}
+template <typename T>
+__device__ __forceinline__ void st16_stream(T* p, const Vec16<T>& r) {
+  __stcs(reinterpret_cast<uint4*>(p), r.u);
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// ------------------------------------------------------------ reductions ----
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// exp(x) through the hardware base-2 exponential: exp(x) = 2^(x*log2(e)).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Online-softmax state of one row segment: running max m, s = sum exp(z-m),
+// w = sum z*exp(z-m), first index of the maximum.
+struct SoftmaxState {
+  float m, s, w;
+  int idx;
+};
+
+__device__ __forceinline__ SoftmaxState sm_init() { return SoftmaxState{-INFINITY, 0.f, 0.f, 0x7fffffff}; }
+
+// Merge b into a. Ties of the maximum keep the smaller index.
+__device__ __forceinline__ SoftmaxState sm_merge(SoftmaxState a, SoftmaxState b) {
+  if (b.m == -INFINITY) return a;
+  if (a.m == -INFINITY) return b;
+  float m = fmaxf(a.m, b.m);
+  float ea = fast_exp2((a.m - m) * kLog2e);
+  float eb = fast_exp2((b.m - m) * kLog2e);
+  SoftmaxState r;
+  r.m = m;
+  r.s = a.s * ea + b.s * eb;
+  r.w = a.w * ea + b.w * eb;
+  if (a.m > b.m) r.idx = a.idx;
+  else if (b.m > a.m) r.idx = b.idx;
+  else r.idx = min(a.idx, b.idx);
+  return r;
+}
+
+__device__ __forceinline__ SoftmaxState sm_shfl_xor(const SoftmaxState& a, int o) {
+  SoftmaxState b;
+  b.m = __shfl_xor_sync(0xffffffffu, a.m, o);
+  b.s = __shfl_xor_sync(0xffffffffu, a.s, o);
+  b.w = __shfl_xor_sync(0xffffffffu, a.w, o);
+  b.idx = __shfl_xor_sync(0xffffffffu, a.idx, o);
+  return b;
+}
+
+__device__ __forceinline__ SoftmaxState sm_warp_reduce(SoftmaxState a) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = sm_merge(a, sm_shfl_xor(a, o));
+  return a;
+}
+
+}  // namespace soup

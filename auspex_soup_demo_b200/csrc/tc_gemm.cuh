@@ -1,0 +1,397 @@
+// Persistent, warp-specialised bf16 GEMM for sm_100a on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in TMEM, operands staged by TMA).
+//
+//   C[m, n] = sum_k A(m, k) * B(n, k)
+//
+// A and B are each either K-major (stored [rows, K], K contiguous) or
+// MN-major (stored [K, rows], rows contiguous); both are loaded by 2-D TMA
+// with the 128-byte swizzle and described to the MMA with matching shared
+// memory descriptors. One CTA per SM (grid <= #SMs) walks a static tile list:
+//
+//   warp 0      TMA producer (one elected lane)      smem ring of STAGES
+//   warp 1      TMEM allocator + MMA issuer (lane 0)  2 accumulators in TMEM
+//   warps 2..5  epilogue: tcgen05.ld -> registers -> Epi::tile(...)
+//
+// Each tile is BM=128 rows x BN columns with BK=64 per stage; the MMA shape
+// is 128 x BN x 16. The TMEM accumulators are double buffered (2 x BN fp32
+// columns), so the epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Every mbarrier wait is bounded (kWaitNs of wall time). On expiry the
+// waiting role records an error code in the device error word (`err`),
+// raises a CTA-wide abort flag, the producer waits (bounded) for its copies
+// still in flight, the MMA warp drains its MMAs, and the CTA frees its TMEM
+// and exits. No TMA multicast is used anywhere.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "soup_common.cuh"
+
+namespace soup {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+
+// error codes written to the device error word
+constexpr int kErrWaitProducer = 0x101;
+constexpr int kErrWaitMma = 0x102;
+constexpr int kErrWaitEpilogue = 0x103;
+
+// ------------------------------------------------------------ PTX wrappers --
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+// 2-D TMA tile load into this CTA's shared memory (no multicast).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// MMA completion -> mbarrier arrive (tracks all prior tcgen05 ops of this thread).
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+// D(tmem) (+)= A(smem desc) * B(smem desc), kind::f16 (bf16 in, fp32 acc).
+__device__ __forceinline__ void tc_mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns: thread t of the warp receives
+// row (lane base + t), columns [col, col+32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  __syncwarp();  // .sync.aligned: the whole warp executes the load converged
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor (sm_100 format): start address, leading
+// and stride byte offsets (16-byte units), version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // descriptor version for sm_100
+  d |= 2ull << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: fp32 accumulate, bf16 A and B, M=128, N=bn.
+__host__ __device__ constexpr uint32_t idesc_bf16(int bn, bool a_mn, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
+         (static_cast<uint32_t>(BM >> 4) << 24);
+}
+
+// ---------------------------------------------------------- tile schedule --
+// A work unit is (m tile, n tile, k split). order 0: m fastest (operand B
+// streamed once while A stays hot in L2); order 1: n fastest (A streamed).
+// The k split is the slowest index so concurrently running units share k.
+struct Sched {
+  int m_tiles, n_tiles, splits;
+  int kb_total;  // number of BK blocks along K
+  int order;
+  __device__ __forceinline__ int units() const { return m_tiles * n_tiles * splits; }
+  __device__ __forceinline__ void decode(int u, int& mt, int& nt, int& ks) const {
+    int mn = m_tiles * n_tiles;
+    ks = u / mn;
+    int r = u - ks * mn;
+    if (order == 0) {
+      mt = r % m_tiles;
+      nt = r / m_tiles;
+    } else {
+      nt = r % n_tiles;
+      mt = r / n_tiles;
+    }
+  }
+  __device__ __forceinline__ void k_range(int ks, int& kb0, int& kb1) const {
+    int base = kb_total / splits, rem = kb_total % splits;
+    kb0 = ks * base + min(ks, rem);
+    kb1 = kb0 + base + (ks < rem ? 1 : 0);
+  }
+};
+
+template <int BN, int STAGES>
+struct SmemLayout {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOff = STAGES * kStageBytes;
+  // full[S], empty[S], tfull[2], tempty[2], drain, then tmem base + abort flag
+  static constexpr int kNumBars = 2 * STAGES + 5;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kBytes = kMiscOff + 16 + 1024;  // + alignment slack
+};
+
+// Bounded wait. Returns false when the CTA is aborting (timeout here or
+// elsewhere); on a local timeout it records `code` and raises the flag.
+__device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity,
+                                             volatile int* abort_flag, int* err, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+// Epi must provide:
+//   struct Params;
+//   static __device__ void tile(const Params&, int mt, int nt, int ks, int quarter,
+//                               int lane, uint32_t tmem_acc /* lane base applied */);
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                Sched sched, typename Epi::Params ep, int* err) {
+  using L = SmemLayout<BN, STAGES>;
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, multiple of 64");
+  static_assert(2 * BN <= 512, "two accumulators must fit in 512 TMEM columns");
+  constexpr int kTmemCols = (2 * BN <= 128) ? 128 : ((2 * BN <= 256) ? 256 : 512);
+  constexpr uint32_t kIdesc = idesc_bf16(BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::kBarOff;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int n_units = sched.units();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer ----
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        int mt, nt, ks, kb0, kb1;
+        sched.decode(u, mt, nt, ks);
+        sched.k_range(ks, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!bounded_wait(empty_bar(s), ph ^ 1u, abort_flag, err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t a_dst = sbase + s * L::kStageBytes;
+          const uint32_t b_dst = a_dst + L::kABytes;
+          mbar_arrive_expect_tx(full_bar(s), L::kStageBytes);
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(a_dst + j * 8192, &tma_a, full_bar(s), mt * BM + j * 64, k0);
+          } else {
+            tma_load_2d(a_dst, &tma_a, full_bar(s), k0, mt * BM);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b_dst + j * 8192, &tma_b, full_bar(s), nt * BN + j * 64, k0);
+          } else {
+            tma_load_2d(b_dst, &tma_b, full_bar(s), k0, nt * BN);
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA leaves: wait for
+        // the last min(it, STAGES) stages' full barriers (bounded).
+        int n = it < (uint32_t)STAGES ? (int)it : STAGES;
+        for (int i = 1; i <= n; ++i) {
+          uint32_t j = it - i;
+          uint32_t bar = full_bar(j % STAGES), ph = (j / STAGES) & 1u;
+          uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(bar, ph) && globaltimer() - t0 < kWaitNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // --------------------------------------------------- MMA issuer ----
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++lt) {
+        int mt, nt, ks, kb0, kb1;
+        sched.decode(u, mt, nt, ks);
+        sched.k_range(ks, kb0, kb1);
+        const uint32_t acc = lt & 1u;
+        const uint32_t acc_ph = (lt >> 1) & 1u;
+        if (!bounded_wait(tempty_bar(acc), acc_ph ^ 1u, abort_flag, err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!bounded_wait(full_bar(s), ph, abort_flag, err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sbase + s * L::kStageBytes;
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t ad, bd;
+            if (A_MN) ad = smem_desc_sw128(a_addr + k * 2048, 8192, 1024);
+            else ad = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            if (B_MN) bd = smem_desc_sw128(b_addr + k * 2048, 8192, 1024);
+            else bd = smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            tc_mma_bf16(tmem_d, ad, bd, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(empty_bar(s));  // frees the stage once these MMAs finish
+        }
+        if (!ok) break;
+        tc_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+      }
+      if (!ok) {
+        tc_commit(drain_bar);
+        uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain_bar, 0) && globaltimer() - t0 < kWaitNs) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------ epilogue ----
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    uint32_t lt = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++lt) {
+      int mt, nt, ks;
+      sched.decode(u, mt, nt, ks);
+      const uint32_t acc = lt & 1u;
+      const uint32_t acc_ph = (lt >> 1) & 1u;
+      bool ok = true;
+      if (lane == 0) ok = bounded_wait(tfull_bar(acc), acc_ph, abort_flag, err, kErrWaitEpilogue);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+      Epi::tile(ep, mt, nt, ks, quarter, lane, taddr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+}  // namespace tc
+}  // namespace soup

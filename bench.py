@@ -1,0 +1,383 @@
+"""Benchmark of the fused lm_head cross-entropy (forward + backward) on B200.
+
+Workload (default): hidden [2048, 1536] bf16 ~N(0,1), lm_head W [151936, 1536]
+bf16 ~N(0, 0.02), labels uniform in [0, 151936) with 10 % set to -100, chunk 32;
+outputs mean loss, entropy, top-1 hits, dhidden and dW. One step = one pass of
+the fused path over the 2048 tokens. Algorithmic work: 3 GEMMs x 2*N*V*D =
+2.868 TFLOP per step (logits, dX, dW). Metric: TFLOP/s, higher is better.
+
+* ``value``: device-resident inputs, the tensor-level fused call, CUDA events
+  around exactly K steps (barrier + synchronize on both sides, max over ranks).
+* ``e2e``: the reference-facing autograd Function
+  (``make_triton_chunked_loss_function``) with the hidden states and labels
+  copied host->device (pinned) each step and loss + hit count read back.
+* ``roofline``: the tcgen05 GEMM kernel (three launches per step, 2*N*V*D
+  FLOP each) timed by CUDA events the library records between its stages.
+* ``cpu_baseline``: the same computation in PyTorch eager on the host cores
+  (the oracle restatement), on one 128-token chunk, all threads.
+
+``--impl reference`` times only that CPU path (the reference's PyTorch eager
+formulation of the op) and prints its own line. With N > 1 GPUs (torchrun),
+every rank runs the same per-GPU workload on its own tokens (weak scaling,
+no collective on the data path).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+N_TOK, DIM, VOCAB, CHUNK = 2048, 1536, 151936, 32
+FLOP_PER_GEMM = 2.0 * N_TOK * DIM * VOCAB
+FLOP_PER_STEP = 3 * FLOP_PER_GEMM
+METRIC = "fused-CE TFLOP/s (fwd+bwd, logits+dX+dW GEMMs)"
+WORKLOAD = "chunked lm_head cross-entropy fwd+bwd, hidden [2048,1536] bf16, W [151936,1536] bf16"
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi SM clock / throttle samples while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                     "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                parts = [p.strip() for p in out.stdout.strip().split(",")]
+                if len(parts) >= 9:
+                    self.samples.append(parts)
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for name, val in zip(names, s[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------- inputs ---
+def make_inputs(seed: int, device):
+    g = torch.Generator().manual_seed(seed)
+    hidden = torch.randn(N_TOK, DIM, generator=g).to(torch.bfloat16)
+    labels = torch.randint(0, VOCAB, (N_TOK,), generator=g)
+    labels[torch.rand(N_TOK, generator=g) < 0.1] = -100
+    gw = torch.Generator(device=device).manual_seed(1000 + seed)
+    weight = (0.02 * torch.randn(VOCAB, DIM, device=device, generator=gw)).to(torch.bfloat16)
+    return hidden, labels, weight
+
+
+# ----------------------------------------------------------- CPU baseline ---
+def cpu_eager_chunk(hidden_chunk, weight_cpu, labels_chunk, den):
+    """One chunk of the reference's eager formulation: h@W^T, fp32 CE, autograd for dh and dW."""
+    h = hidden_chunk.clone().requires_grad_(True)
+    w = weight_cpu.detach().requires_grad_(True)
+    logits = (h @ w.t()).float()
+    loss = torch.nn.functional.cross_entropy(logits, labels_chunk, ignore_index=-100,
+                                             reduction="sum") / den
+    with torch.no_grad():
+        logp = torch.log_softmax(logits, -1)
+        _ = -(logp.exp() * logp).sum(-1)
+        _ = (logits.argmax(-1) == labels_chunk).sum()
+    loss.backward()
+    return float(loss)
+
+
+def cpu_baseline(seconds: float = 8.0, rows: int = 4 * CHUNK):
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(7)
+    weight = (0.02 * torch.randn(VOCAB, DIM, generator=g)).to(torch.bfloat16)
+    hidden = torch.randn(rows, DIM, generator=g).to(torch.bfloat16)
+    labels = torch.randint(0, VOCAB, (rows,), generator=g)
+    den = float(rows)
+    cpu_eager_chunk(hidden, weight, labels, den)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_eager_chunk(hidden, weight, labels, den)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 50:
+            break
+    per = el / n
+    flop = 3 * 2.0 * rows * DIM * VOCAB
+    return {"value": flop / per / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{n} x one {rows}-token chunk (B=4 x chunk {CHUNK}) of the same workload, "
+                      f"PyTorch eager bf16 GEMMs + fp32 CE + autograd dh/dW, {per * 1e3:.1f} ms/chunk"}
+
+
+# ------------------------------------------------------------------- runs ---
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = 4 * CHUNK
+    g = torch.Generator().manual_seed(7)
+    weight = (0.02 * torch.randn(VOCAB, DIM, generator=g)).to(torch.bfloat16)
+    hidden = torch.randn(rows, DIM, generator=g).to(torch.bfloat16)
+    labels = torch.randint(0, VOCAB, (rows,), generator=g)
+    labels[torch.rand(rows, generator=g) < 0.1] = -100
+    den = float((labels != -100).sum())
+    for _ in range(args.warmup):
+        cpu_eager_chunk(hidden, weight, labels, den)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_eager_chunk(hidden, weight, labels, den)
+    el = time.perf_counter() - t0
+    per = el / args.steps
+    flop = 3 * 2.0 * rows * DIM * VOCAB
+    val = flop / per / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": f"{rows}-token chunk per step",
+                   "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": round(val, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"one {rows}-token chunk per step, PyTorch eager on the host"},
+        "e2e": {"value": round(val, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    import torch.distributed as dist
+
+    from auspex_soup_demo_b200 import _lib
+    from auspex_soup_demo_b200.kernels import make_triton_chunked_loss_function
+    from auspex_soup_demo_b200.kernels.chunked_ce import fused_linear_cross_entropy
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    hidden_cpu, labels_cpu, weight = make_inputs(rank, dev)
+    hidden = hidden_cpu.to(dev)
+    labels = labels_cpu.to(dev)
+    den = float((labels_cpu != -100).sum())
+    stream = torch.cuda.current_stream(dev)
+
+    # stage events recorded by the library inside each fused call
+    start_ev = torch.cuda.Event(enable_timing=True)
+    stage_ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for e in [start_ev, *stage_ev]:
+        e.record(stream)  # materialise the handles
+    torch.cuda.synchronize()
+
+    def step():
+        return fused_linear_cross_entropy(hidden, weight, labels, den, -100, True, compute_dw=True,
+                                          dw_dtype=torch.bfloat16)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    assert _lib.device_error(dev) == 0
+
+    # ---- per-stage timing (one extra pass per step, outside the timed loop) ----
+    handles = (ctypes_void_p_array([e.cuda_event for e in stage_ev]))
+    _lib.lib().soup_set_stage_events(handles, 6)
+    stage_ms = [[] for _ in range(6)]
+    for _ in range(max(3, min(args.steps, 10))):
+        start_ev.record(stream)
+        step()
+        torch.cuda.synchronize()
+        prev = start_ev
+        for i, e in enumerate(stage_ev):
+            stage_ms[i].append(prev.elapsed_time(e))
+            prev = e
+    _lib.lib().soup_set_stage_events(None, 0)
+    st = [statistics.median(v) for v in stage_ms]
+
+    # ---- timed region: device-resident inputs ----
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            out = step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ms_all = ms
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_all = float(t)
+    value = world * FLOP_PER_STEP / (ms_all * 1e-3) / 1e12
+
+    # ---- e2e through the reference-facing autograd Function, host buffers ----
+    head = torch.nn.Linear(DIM, VOCAB, bias=False, dtype=torch.bfloat16, device=dev)
+    with torch.no_grad():
+        head.weight.copy_(weight)
+    Fn = make_triton_chunked_loss_function()
+    h_pin = hidden_cpu.view(1, N_TOK, DIM).pin_memory()
+    l_pin = labels_cpu.view(1, N_TOK).pin_memory()
+    res_pin = torch.empty(2, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        h = h_pin.to(dev, non_blocking=True).requires_grad_(True)
+        lab = l_pin.to(dev, non_blocking=True)
+        head.weight.grad = None
+        loss, ent, tok, corr = Fn.apply(h, head, lab, CHUNK, den, -100, True)
+        loss.backward()
+        res = torch.stack([loss.detach().float(), corr.float()])
+        res_pin.copy_(res, non_blocking=True)
+        return res
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t)
+    e2e_val = world * FLOP_PER_STEP / (e2e_ms * 1e-3) / 1e12
+    assert _lib.device_error(dev) == 0
+
+    peak_tf, peak_hbm, peak_src = _peaks()
+    gemm_ms = [st[0], st[3], st[5]]
+    achieved = FLOP_PER_GEMM / (statistics.mean(gemm_ms) * 1e-3) / 1e12
+    traffic = _committed_traffic()
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_all, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "tokens_per_gpu": N_TOK, "chunk": CHUNK,
+                   "ignore_frac": 0.1, "parallelism": f"dp{world} (tokens sharded, no collective)",
+                   "l2": "inputs larger than L2 (W 467 MB, logits buffer 622 MB)"},
+        "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": N_TOK * DIM * 2 + N_TOK * 8, "d2h_bytes_per_step": 8,
+                "ms_per_step": round(e2e_ms, 4),
+                "api": "make_triton_chunked_loss_function().apply + backward (head weight trainable)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf,
+                     "unit": "TFLOP/s", "frac": round(achieved / peak_tf, 4), "traffic": traffic,
+                     "kernel": "soup::tc::gemm_kernel (logits / dX / dW launches, 2*N*V*D each)",
+                     "peak_source": f"{peak_src} bf16_tflops (burst)"},
+        "stages_ms": {"logits_gemm": round(st[0], 4), "finalize": round(st[1], 4),
+                      "sums": round(st[2], 4), "dx_gemm": round(st[3], 4),
+                      "dx_reduce": round(st[4], 4), "dw_gemm": round(st[5], 4)},
+        "gpu_launches": 6 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _committed_traffic():
+    """DRAM bytes per launch of the logits GEMM from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get("gemm_kernel_bytes_per_launch")
+    except Exception:
+        return None
+
+
+def ctypes_void_p_array(values):
+    import ctypes
+
+    return (ctypes.c_void_p * len(values))(*values)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

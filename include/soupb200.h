@@ -1,0 +1,144 @@
+/*
+ * soupb200.h — C ABI of the B200 (sm_100a) fused QLoRA ops.
+ *
+ * Every entry point takes plain device pointers, element counts and strides
+ * (in elements), a dtype code and a cudaStream_t (passed as void*), launches
+ * asynchronously on that stream and returns a status code. Nothing allocates:
+ * outputs and scratch buffers are the caller's. No entry point synchronises
+ * the stream.
+ *
+ * The reference (Python + Triton) exposes these ops through its autograd
+ * Functions; each declaration below names the reference interface it
+ * replaces (paths relative to the reference project root).
+ */
+#ifndef SOUPB200_H
+#define SOUPB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define SOUP_OK 0
+#define SOUP_ERR_INVALID 1      /* bad pointer, size, stride or dtype            */
+#define SOUP_ERR_UNSUPPORTED 2  /* valid but not handled (alignment, dtype mix)  */
+#define SOUP_ERR_CUDA 3         /* a CUDA runtime call or launch failed          */
+#define SOUP_ERR_WORKSPACE 4    /* workspace too small                           */
+#define SOUP_ERR_DEVICE 5       /* a device-side bounded wait timed out          */
+
+/* ---- dtype codes --------------------------------------------------------- */
+#define SOUP_F32 0
+#define SOUP_F16 1
+#define SOUP_BF16 2
+
+/* Library version and the last CUDA error text seen by this thread. */
+int soup_version(void);
+const char* soup_last_error(void);
+
+/* Device error word written by bounded waits in the GEMM kernels (0 = none).
+ * Reading it synchronises the given stream. */
+int soup_device_error(void* stream, int* out_code);
+
+/* ---- RMSNorm -------------------------------------------------------------
+ * Replaces solution/kernels/rmsnorm.py:22-57 (_rms_norm_fwd_kernel) and the
+ * launch in FastRMSNormFunction.forward (rmsnorm.py:102-134).
+ * x, y: [rows, cols] with row strides; weight: [cols]; rstd: [rows] fp32 out.
+ * y = (x * rstd) * w, rstd = 1/sqrt(mean(x^2) + eps), fp32 math. */
+int soup_rmsnorm_fwd(const void* x, int64_t x_row_stride, const void* weight, void* y,
+                     int64_t y_row_stride, float* rstd, int64_t rows, int64_t cols, float eps,
+                     int x_dtype, int w_dtype, void* stream);
+
+/* Replaces solution/kernels/rmsnorm.py:60-96 (_rms_norm_bwd_dx_kernel) and
+ * the eager dw reduction at rmsnorm.py:161-167, fused into one launch.
+ * dx = rstd*(dy*w - (x/cols)*rstd^2*sum(dy*w*x)); dw = sum_rows dy*x*rstd.
+ * dw may be NULL (weight frozen). When dw is given, workspace must hold
+ * soup_rmsnorm_bwd_workspace_bytes(rows, cols) bytes; the dw reduction is
+ * deterministic (fixed-order per-block partials, no data atomics). */
+size_t soup_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t cols);
+int soup_rmsnorm_bwd(const void* dy, int64_t dy_row_stride, const void* x, int64_t x_row_stride,
+                     const void* weight, const float* rstd, void* dx, int64_t dx_row_stride,
+                     void* dw, void* workspace, size_t workspace_bytes, int64_t rows,
+                     int64_t cols, int x_dtype, int w_dtype, void* stream);
+
+/* ---- SwiGLU --------------------------------------------------------------
+ * Replaces solution/kernels/swiglu.py:20-50 (_custom_swiglu_fwd_kernel).
+ * out = g*sigmoid(g)*u on [rows, cols] with independent row strides. */
+int soup_swiglu_fwd(const void* gate, int64_t gate_row_stride, const void* up,
+                    int64_t up_row_stride, void* out, int64_t out_row_stride, int64_t rows,
+                    int64_t cols, int dtype, void* stream);
+
+/* Replaces solution/kernels/swiglu.py:53-95 (_custom_swiglu_bwd_kernel);
+ * sigmoid is recomputed from gate. dgate/dup may alias gate/up (in place). */
+int soup_swiglu_bwd(const void* dy, int64_t dy_row_stride, const void* gate,
+                    int64_t gate_row_stride, const void* up, int64_t up_row_stride, void* dgate,
+                    int64_t dgate_row_stride, void* dup, int64_t dup_row_stride, int64_t rows,
+                    int64_t cols, int dtype, void* stream);
+
+/* ---- RoPE (rotate-half) ----------------------------------------------------
+ * Replaces solution/kernels/rope.py:20-67 (_fused_rope_2d_fwd_kernel) and the
+ * two launches of patch_qwen2_rope (rope.py:217-218): Q and K in one launch.
+ * Tensors are [B, H, S, D] with strides {b, h, s} (last dim contiguous);
+ * cos/sin are indexed [b*cos_sb + s*cos_ss + d] for d < D/2 (the reference
+ * reads the first half only). k/k_out may be NULL with hk = 0. inverse != 0
+ * applies the transpose rotation (backward, rope.py:70-117). */
+int soup_rope(const void* q, const int64_t* q_strides, void* q_out, const int64_t* q_out_strides,
+              int64_t hq, const void* k, const int64_t* k_strides, void* k_out,
+              const int64_t* k_out_strides, int64_t hk, const void* cos, const void* sin,
+              int64_t cos_sb, int64_t cos_ss, int64_t batch, int64_t seq, int64_t head_dim,
+              int dtype, int cos_dtype, int inverse, void* stream);
+
+/* ---- Cross-entropy on a logits buffer ------------------------------------
+ * Replaces solution/kernels/chunked_ce.py:32-128
+ * (_chunked_cross_entropy_fused_kernel): per-row loss, entropy, top-1 hit,
+ * and (write_grad != 0) the in-place overwrite of the logits with
+ * (softmax - onehot)/denominator (0 for ignored rows). */
+int soup_ce_rows(void* logits, int64_t row_stride, const int64_t* targets, float* losses,
+                 float* entropies, int32_t* correct, int64_t rows, int64_t vocab,
+                 float denominator, int64_t ignore_index, int dtype, int write_grad,
+                 void* stream);
+
+/* ---- Fused lm_head cross-entropy (tcgen05 GEMMs) -------------------------
+ * Replaces chunk_cross_entropy_triton (chunked_ce.py:183-264) driven by
+ * TritonChunkedHeadLoss.forward (chunked_ce.py:271-304): the logits GEMM with
+ * an online-softmax epilogue, the per-row metrics, dlogits, the input
+ * gradient and (new, no reference counterpart) the lm_head gradient.
+ * hidden [rows, dim] bf16 (row stride h_ld), weight [vocab, dim] bf16
+ * (row stride w_ld), targets [rows] int64.
+ * Outputs: losses/entropies [rows] fp32, correct [rows] int32,
+ * sums[2] fp32 = {sum of losses, sum of hits} (may be NULL),
+ * dhidden [rows, dim] bf16 (NULL: no input gradient), dweight [vocab, dim]
+ * (NULL: no lm_head gradient; dtype dw_dtype F32 or BF16; accumulate_dw != 0
+ * adds to its contents). Gradients are scaled by 1/denominator (the caller's
+ * grad_output scale is applied outside). workspace: see
+ * soup_ce_linear_workspace_bytes. */
+size_t soup_ce_linear_workspace_bytes(int64_t rows, int64_t vocab, int64_t dim);
+int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t w_ld,
+                   const int64_t* targets, int64_t rows, int64_t vocab, int64_t dim,
+                   float denominator, int64_t ignore_index, float* losses, float* entropies,
+                   int32_t* correct, float* sums, void* dhidden, void* dweight, int dw_dtype,
+                   int accumulate_dw, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Stage timing for measurement: while set (n > 0), each soup_ce_linear call on
+ * this host thread records events[i] on its stream after stage i:
+ * 0 logits GEMM, 1 finalize, 2 sums, 3 dX GEMM, 4 dX reduce, 5 dW GEMM
+ * (a stage that does not run records nothing). n = 0 clears. The events are
+ * cudaEvent_t handles owned by the caller. */
+int soup_set_stage_events(void** events, int n);
+
+/* ---- Plain tcgen05 GEMM (building block, exposed for tests) ---------------
+ * C[m, n] = alpha * sum_k A(m, k) * B(n, k) (+ C if accumulate), bf16 inputs,
+ * fp32 accumulation. a_mn_major = 0: A stored [M, K] (lda >= K); 1: stored
+ * [K, M] (lda >= M). b_mn_major = 0: B stored [N, K]; 1: stored [K, N].
+ * c_dtype F32 or BF16, C stored [M, N] with row stride ldc. */
+int soup_gemm_bf16(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb,
+                   int b_mn_major, void* c, int64_t ldc, int c_dtype, int64_t m, int64_t n,
+                   int64_t k, float alpha, int accumulate, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SOUPB200_H */

@@ -1,0 +1,95 @@
+"""CPU checks of the C ABI: the library loads, exports every declared symbol,
+validates arguments before touching the GPU, and sizes its workspaces."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from auspex_soup_demo_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "soupb200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(soup_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads():
+    lib = _lib.lib()
+    assert lib.soup_version() >= 1
+
+
+def test_every_declared_symbol_is_exported():
+    lib = _lib.lib()
+    names = declared_symbols()
+    assert len(names) >= 12
+    for name in names:
+        assert hasattr(lib, name), f"{name} declared in soupb200.h but not exported"
+
+
+def test_binding_covers_the_header():
+    assert sorted(_lib.exported_symbols()) == declared_symbols()
+
+
+def test_null_pointers_are_rejected_without_a_gpu():
+    lib = _lib.lib()
+    st = lib.soup_rmsnorm_fwd(None, 8, None, None, 8, None, 4, 8, 1e-6, 0, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    assert b"rmsnorm" in lib.soup_last_error()
+    st = lib.soup_swiglu_fwd(None, 8, None, 8, None, 8, 4, 8, 2, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    st = lib.soup_ce_rows(None, 8, None, None, None, None, 4, 8, 1.0, -100, 2, 1, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    st = lib.soup_ce_linear(None, 8, None, 8, None, 4, 8, 8, 1.0, -100, None, None, None, None,
+                            None, None, 0, 0, None, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    st = lib.soup_gemm_bf16(None, 8, 0, None, 8, 0, None, 8, 0, 4, 4, 4, 1.0, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    strides = _lib.i64_array([1, 1, 1])
+    st = lib.soup_rope(None, strides, None, strides, 1, None, None, None, None, 0, None, None, 0, 0,
+                       1, 1, 128, 2, 2, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID
+
+
+def test_bad_sizes_are_rejected():
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    # row stride smaller than the row
+    st = lib.soup_rmsnorm_fwd(fake, 4, fake, fake, 8, fake, 4, 8, 1e-6, 0, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    # odd head_dim
+    strides = _lib.i64_array([1, 1, 1])
+    st = lib.soup_rope(fake, strides, fake, strides, 1, None, None, None, None, 0, fake, fake, 0, 0,
+                       1, 1, 127, 2, 2, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    # unsupported dtype code
+    st = lib.soup_swiglu_fwd(fake, 8, fake, 8, fake, 8, 0, 8, 7, None)
+    assert st == _lib.SOUP_OK  # zero rows: nothing to do, accepted before dtype dispatch
+    st = lib.soup_swiglu_fwd(fake, 8, fake, 8, fake, 8, 1, 8, 7, None)
+    assert st == _lib.SOUP_ERR_INVALID
+
+
+def test_workspace_sizes():
+    lib = _lib.lib()
+    n, v, d = 2048, 151936, 1536
+    ws = lib.soup_ce_linear_workspace_bytes(n, v, d)
+    logits = n * v * 2
+    assert logits < ws < logits + 200 * 2 ** 20  # logits + partials + split-K slices
+    assert lib.soup_ce_linear_workspace_bytes(0, v, d) == 0
+    assert lib.soup_rmsnorm_bwd_workspace_bytes(2048, 1536) >= 1536 * 4
+    # workspace grows linearly with rows
+    assert lib.soup_ce_linear_workspace_bytes(4096, v, d) > 1.9 * ws
+
+
+def test_dtype_codes():
+    import torch
+    assert _lib.dtype_code(torch.float32) == _lib.F32
+    assert _lib.dtype_code(torch.float16) == _lib.F16
+    assert _lib.dtype_code(torch.bfloat16) == _lib.BF16
+    with pytest.raises(TypeError):
+        _lib.dtype_code(torch.int32)

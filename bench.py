@@ -349,6 +349,125 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------- memory-bound op workloads ---
+def run_memory_op(args):
+    """HBM GB/s of one memory-bound fused op (fwd + bwd) at its benchmark shape.
+
+    Inputs rotate over enough buffer sets to exceed twice the L2 (126 MB);
+    `graph_steps` steps are captured once in a CUDA graph and replayed, so
+    host launch overhead stays out of the device time. Algorithmic bytes:
+    rmsnorm 5*N*D*4 (x, y; dy, x, dx) fp32 [2048, 1536]; swiglu 8*N*I*2
+    (g, u, out; dy, g, u, dg, du) bf16 [2048, 8960]; rope 2 passes x (read +
+    write of Q and K + cos/sin reads) bf16 Q [4,12,512,128], K [4,2,512,128].
+    """
+    from auspex_soup_demo_b200.kernels.rmsnorm import rmsnorm_backward, rmsnorm_forward
+    from auspex_soup_demo_b200.kernels.rope import rope_apply
+    from auspex_soup_demo_b200.kernels.swiglu import swiglu_backward, swiglu_forward
+
+    import oracle
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    wl = args.workload
+    l2 = 126 * 2 ** 20
+    if wl == "rmsnorm":
+        N, D = 2048, 1536
+        per_set = 4 * N * D * 4
+        nsets = max(2, -(-2 * l2 // per_set))
+        w = (1 + 0.1 * torch.randn(D, device=dev, generator=g))
+        sets = [dict(x=torch.randn(N, D, device=dev, generator=g),
+                     dy=torch.randn(N, D, device=dev, generator=g),
+                     y=torch.empty(N, D, device=dev), dx=torch.empty(N, D, device=dev),
+                     rstd=torch.empty(N, device=dev)) for _ in range(nsets)]
+        algo = 5 * N * D * 4 + 3 * D * 4 + 2 * N * 4
+        launches = 3
+
+        def one(s):
+            rmsnorm_forward(s["x"], w, 1e-6, out=s["y"], rstd=s["rstd"])
+            rmsnorm_backward(s["dy"], s["x"], w, s["rstd"], True, dx=s["dx"])
+        shape = "x [2048,1536] fp32, dw included"
+    elif wl == "swiglu":
+        N, I = 2048, 8960
+        per_set = 7 * N * I * 2
+        nsets = max(2, -(-2 * l2 // per_set))
+        sets = [dict(g=torch.randn(N, I, device=dev, generator=g).to(torch.bfloat16),
+                     u=torch.randn(N, I, device=dev, generator=g).to(torch.bfloat16),
+                     dy=torch.randn(N, I, device=dev, generator=g).to(torch.bfloat16),
+                     o=torch.empty(N, I, device=dev, dtype=torch.bfloat16),
+                     dg=torch.empty(N, I, device=dev, dtype=torch.bfloat16),
+                     du=torch.empty(N, I, device=dev, dtype=torch.bfloat16)) for _ in range(nsets)]
+        algo = 8 * N * I * 2
+        launches = 2
+
+        def one(s):
+            swiglu_forward(s["g"], s["u"], out=s["o"])
+            swiglu_backward(s["dy"], s["g"], s["u"], dg=s["dg"], du=s["du"])
+        shape = "gate/up [2048,8960] bf16"
+    elif wl == "rope":
+        B, S, Hq, Hk, D = 4, 512, 12, 2, 128
+        qk_bytes = (Hq + Hk) * B * S * D * 2
+        per_set = 4 * qk_bytes
+        nsets = max(2, -(-2 * l2 // per_set))
+        cos, sin = oracle.rope_cos_sin(S, D, 1e6, torch.bfloat16)
+        cos = cos[None, None].to(dev)
+        sin = sin[None, None].to(dev)
+        sets = [dict(q=torch.randn(B, Hq, S, D, device=dev, generator=g).to(torch.bfloat16),
+                     k=torch.randn(B, Hk, S, D, device=dev, generator=g).to(torch.bfloat16),
+                     qo=torch.empty(B, Hq, S, D, device=dev, dtype=torch.bfloat16),
+                     ko=torch.empty(B, Hk, S, D, device=dev, dtype=torch.bfloat16))
+                for _ in range(nsets)]
+        algo = 2 * (2 * qk_bytes + 2 * S * (D // 2) * 2)
+        launches = 2
+
+        def one(s):
+            rope_apply(s["q"], s["k"], cos, sin, False, q_out=s["qo"], k_out=s["ko"])
+            rope_apply(s["qo"], s["ko"], cos, sin, True, q_out=s["q"], k_out=s["k"])
+        shape = "Q [4,12,512,128] + K [4,2,512,128] bf16, theta 1e6, fwd + inverse"
+    else:
+        raise SystemExit(f"unknown workload {wl}")
+
+    graph_steps = max(nsets, 16)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(3):  # warm-up (also sizes the dw scratch before capture)
+            one(sets[i % nsets])
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(graph_steps):
+            one(sets[i % nsets])
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    reps = max(1, args.steps)
+    with ClockSampler(dev.index) as clocks:
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / (reps * graph_steps)
+    gbs = algo / (ms * 1e-3) / 1e9
+    _, peak_hbm, src = _peaks()
+    line = {"metric": f"{wl} fwd+bwd HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
+            "n_gpus": 1, "steps": reps * graph_steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 5), "higher_is_better": True, "dtype": "bf16" if wl != "rmsnorm" else "f32",
+            "data": "synthetic",
+            "config": {"workload": f"{wl}: {shape}", "buffer_sets": nsets,
+                       "l2": f"rotating {nsets} input sets, {nsets * per_set / 2**20:.0f} MiB > 2x L2",
+                       "timing": f"CUDA graph of {graph_steps} steps, replayed {reps}x"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak_hbm, "unit": "GB/s",
+                         "frac": round(gbs / peak_hbm, 4), "traffic": None,
+                         "algorithmic_bytes_per_step": algo, "peak_source": f"{src} hbm_gbs"},
+            "gpu_launches": launches * reps * graph_steps, "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def _committed_traffic():
     """DRAM bytes per launch of the logits GEMM from the committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
@@ -372,9 +491,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", default="ce", choices=["ce", "rmsnorm", "swiglu", "rope"],
+                    help="ce (default): the fused head CE; others: one memory-bound op's HBM GB/s")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "ce":
+        run_memory_op(args)
     else:
         run_b200(args)
 

@@ -56,6 +56,8 @@ _SIGNATURES = {
     "soup_rmsnorm_bwd_workspace_bytes": (c_sz, [c_i64, c_i64]),
     "soup_rmsnorm_bwd": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp,
                                  c_sz, c_i64, c_i64, c_int, c_int, c_vp]),
+    "soup_rmsnorm_bwd_noalloc": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp,
+                                         c_i64, c_i64, c_int, c_int, c_vp]),
     "soup_swiglu_fwd": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_int, c_vp]),
     "soup_swiglu_bwd": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
                                 c_i64, c_i64, c_int, c_vp]),

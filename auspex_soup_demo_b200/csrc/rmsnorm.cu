@@ -9,6 +9,7 @@
 //
 // Semantics: solution/kernels/rmsnorm.py:22-57 (forward), :60-96 (dx) and
 // :161-167 (dw, fp32, cast to the weight dtype).
+#include <cstdio>
 #include <initializer_list>
 #include <utility>
 
@@ -398,6 +399,119 @@ int soup_rmsnorm_bwd(const void* dy, int64_t dy_row_stride, const void* x, int64
   SOUP_DISPATCH_XW(x_dtype, w_dtype, CALL);
 #undef CALL
   set_last_error("soup_rmsnorm_bwd: unsupported dtype");
+  return SOUP_ERR_INVALID;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// RMSNorm backward that allocates nothing.
+//
+// For callers that cannot hand the library a scratch buffer: code that runs
+// under an allocator owning all device memory (a framework's caching pool that
+// has reserved the GPU, a fixed-budget serving process), or host code that
+// must not call cudaMalloc because cudaMalloc may synchronise the device. The
+// dw reduction's per-CTA partial rows live in the file-scope array below
+// instead; every GPU that loads this library holds it until the process exits.
+// ---------------------------------------------------------------------------
+namespace soup {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB
+__device__ __align__(256) float g_rms_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// Device address of the array, looked up once per device with that device
+// current. In host code the array's name is only a host-side stand-in, so the
+// kernels must receive this address instead.
+float* noalloc_scratch(int* status) {
+  static float* addr[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *status = cuda_status(e);
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    set_last_error("soup_rmsnorm_bwd_noalloc: device index out of range");
+    *status = SOUP_ERR_UNSUPPORTED;
+    return nullptr;
+  }
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_rms_noalloc_scratch);
+    if (e != cudaSuccess) {
+      *status = cuda_status(e);
+      return nullptr;
+    }
+    addr[dev] = static_cast<float*>(p);
+  }
+  *status = SOUP_OK;
+  return addr[dev];
+}
+
+// Bytes of dw partial rows the backward writes for these operands.
+template <typename T, typename W>
+size_t bwd_partial_bytes(const void* dy, int64_t dys, const void* x, int64_t xs, const void* w,
+                         const void* dx, int64_t dxs, int64_t rows, int64_t cols) {
+  const bool vec = vec_ok<T, W>(cols, {{dy, dys}, {x, xs}, {dx, dxs}}, w);
+  const size_t prows = static_cast<size_t>(vec ? bwd_grid(rows) : bwd_grid(rows) * kWarps);
+  return prows * static_cast<size_t>(cols) * sizeof(float);
+}
+
+size_t bwd_partial_bytes_any(int xd, int wd, const void* dy, int64_t dys, const void* x,
+                             int64_t xs, const void* w, const void* dx, int64_t dxs, int64_t rows,
+                             int64_t cols) {
+#define NEED(T, W) bwd_partial_bytes<T, W>(dy, dys, x, xs, w, dx, dxs, rows, cols)
+  SOUP_DISPATCH_XW(xd, wd, NEED);
+#undef NEED
+  return 0;  // unsupported dtype pair
+}
+
+}  // namespace
+}  // namespace soup
+
+extern "C" {
+
+int soup_rmsnorm_bwd_noalloc(const void* dy, int64_t dy_row_stride, const void* x,
+                             int64_t x_row_stride, const void* weight, const float* rstd,
+                             void* dx, int64_t dx_row_stride, void* dw, int64_t rows,
+                             int64_t cols, int x_dtype, int w_dtype, void* stream) {
+  if (!dy || !x || !weight || !rstd || !dx || rows < 0 || cols <= 0 || cols > (1 << 20) ||
+      dy_row_stride < cols || x_row_stride < cols || dx_row_stride < cols) {
+    set_last_error("soup_rmsnorm_bwd_noalloc: bad arguments");
+    return SOUP_ERR_INVALID;
+  }
+  if (rows == 0) return SOUP_OK;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  if (dw) {
+    const size_t need = bwd_partial_bytes_any(x_dtype, w_dtype, dy, dy_row_stride, x, x_row_stride,
+                                              weight, dx, dx_row_stride, rows, cols);
+    if (need == 0) {
+      set_last_error("soup_rmsnorm_bwd_noalloc: unsupported dtype");
+      return SOUP_ERR_INVALID;
+    }
+    if (need > kNoAllocScratchBytes) {
+      char msg[200];
+      snprintf(msg, sizeof(msg),
+               "soup_rmsnorm_bwd_noalloc: dw needs %zu bytes of scratch, the built-in buffer holds "
+               "%zu; pass a workspace to soup_rmsnorm_bwd instead",
+               need, kNoAllocScratchBytes);
+      set_last_error(msg);
+      return SOUP_ERR_WORKSPACE;
+    }
+    int status = SOUP_OK;
+    ws = noalloc_scratch(&status);
+    if (!ws) return status;
+    ws_bytes = kNoAllocScratchBytes;
+  }
+  cudaStream_t st = as_stream(stream);
+#define CALL(T, W)                                                                        \
+  bwd_impl<T, W>(dy, dy_row_stride, x, x_row_stride, weight, rstd, dx, dx_row_stride, dw, \
+                 ws, ws_bytes, rows, cols, st)
+  SOUP_DISPATCH_XW(x_dtype, w_dtype, CALL);
+#undef CALL
+  set_last_error("soup_rmsnorm_bwd_noalloc: unsupported dtype");
   return SOUP_ERR_INVALID;
 }
 

@@ -63,6 +63,24 @@ int soup_rmsnorm_bwd(const void* dy, int64_t dy_row_stride, const void* x, int64
                      void* dw, void* workspace, size_t workspace_bytes, int64_t rows,
                      int64_t cols, int x_dtype, int w_dtype, void* stream);
 
+/* RMSNorm backward that allocates nothing. No counterpart in the reference:
+ * it exists for callers that cannot give the library a scratch buffer, such as
+ * code running under an allocator that already owns all device memory, or host
+ * code that must avoid cudaMalloc because it can synchronise the device.
+ * Same arguments and results as soup_rmsnorm_bwd without the workspace: the dw
+ * partial rows go to a 4 MiB array built into the library (every GPU that
+ * loads the library holds it until exit). Calls needing more than 4 MiB of
+ * partials (about rows-independent: one fp32 row of `cols` per CTA, at most
+ * one CTA per SM, so cols up to ~7000 on 148 SMs on the vector path) return
+ * SOUP_ERR_WORKSPACE. The first call on a device looks up the array's device
+ * address; make that first call before any stream capture. All calls share
+ * the array, so calls whose kernels overlap on the GPU (other streams, other
+ * host threads) race: serialise them. */
+int soup_rmsnorm_bwd_noalloc(const void* dy, int64_t dy_row_stride, const void* x,
+                             int64_t x_row_stride, const void* weight, const float* rstd,
+                             void* dx, int64_t dx_row_stride, void* dw, int64_t rows,
+                             int64_t cols, int x_dtype, int w_dtype, void* stream);
+
 /* ---- SwiGLU --------------------------------------------------------------
  * Replaces solution/kernels/swiglu.py:20-50 (_custom_swiglu_fwd_kernel).
  * out = g*sigmoid(g)*u on [rows, cols] with independent row strides. */

@@ -27,14 +27,93 @@ namespace tc {
 using bf16 = __nv_bfloat16;
 
 // ------------------------------------------------------------- epilogues ---
-// Plain store: C = alpha * acc (+ C). `split_stride` > 0 writes k-split
-// partial slices (fp32) at C + ks * split_stride.
+// Each epilogue thread owns one accumulator row (TMEM lane). Stores go through
+// the warp's shared-memory staging block (32 rows x 32 fp32): a thread writes
+// its row's 32 values, then the warp writes the block out row by row, 8 lanes
+// per row, so each global store covers a contiguous 64 B (bf16) or 128 B (fp32)
+// row segment instead of scattered 16 B pieces.
+
+__device__ __forceinline__ void stage_row(uint8_t* stage, int lane, const float (&v)[32], float a) {
+  float4* dst = reinterpret_cast<float4*>(stage + lane * kStageRowBytes);
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    dst[q] = make_float4(a * v[4 * q], a * v[4 * q + 1], a * v[4 * q + 2], a * v[4 * q + 3]);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Write the staged block to C rows [row0, row0+32) x cols [col0, col0+32),
+// clipped to M x N. `vec`: rows are 16-byte aligned (vector stores allowed).
+template <bool BF16>
+__device__ __forceinline__ void write_block(const uint8_t* stage, int lane, void* C, int64_t ldc,
+                                            int row0, int M, int col0, int N, bool vec,
+                                            bool accumulate) {
+  const int cv = lane & 7;
+  const int rsub = lane >> 3;
+  const int gcol = col0 + cv * 4;
+#pragma unroll 2
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + rsub;
+    const int grow = row0 + r;
+    if (grow >= M) continue;
+    float4 x = *reinterpret_cast<const float4*>(stage + r * kStageRowBytes + cv * 16);
+    if (vec && gcol + 4 <= N) {
+      if constexpr (BF16) {
+        bf16* dst = reinterpret_cast<bf16*>(C) + (int64_t)grow * ldc + gcol;
+        if (accumulate) {
+          uint2 o = *reinterpret_cast<const uint2*>(dst);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&o);
+          float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+          x.x += a.x;
+          x.y += a.y;
+          x.z += b.x;
+          x.w += b.y;
+        }
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(x.x, x.y), pack_bf16x2(x.z, x.w));
+      } else {
+        float* dst = reinterpret_cast<float*>(C) + (int64_t)grow * ldc + gcol;
+        if (accumulate) {
+          float4 o = *reinterpret_cast<const float4*>(dst);
+          x.x += o.x;
+          x.y += o.y;
+          x.z += o.z;
+          x.w += o.w;
+        }
+        *reinterpret_cast<float4*>(dst) = x;
+      }
+    } else {
+      const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (gcol + e < N) {
+          if constexpr (BF16) {
+            bf16* dst = reinterpret_cast<bf16*>(C) + (int64_t)grow * ldc + gcol + e;
+            float y = xs[e];
+            if (accumulate) y += __bfloat162float(*dst);
+            *dst = __float2bfloat16_rn(y);
+          } else {
+            float* dst = reinterpret_cast<float*>(C) + (int64_t)grow * ldc + gcol + e;
+            *dst = accumulate ? *dst + xs[e] : xs[e];
+          }
+        }
+      }
+    }
+  }
+}
+
+// Plain store: C = alpha * scale * acc (+ C). `scale` is an optional device
+// scalar (e.g. the upstream gradient of the loss). `split_stride` > 0 writes
+// k-split partial slices (fp32) at C + ks * split_stride.
 template <int BN>
 struct EpiStore {
   struct Params {
     void* c;
     int64_t ldc;
     int64_t split_stride;
+    const float* scale;
     float alpha;
     int c_bf16;
     int accumulate;
@@ -42,65 +121,24 @@ struct EpiStore {
     int M, N;
   };
   static __device__ __forceinline__ void tile(const Params& p, int mt, int nt, int ks, int quarter,
-                                              int lane, uint32_t taddr) {
-    const int row = mt * BM + quarter * 32 + lane;
-    const bool row_ok = row < p.M;
+                                              int lane, uint32_t taddr, uint8_t* stage) {
+    const int row0 = mt * BM + quarter * 32;
+    const float a = p.alpha * (p.scale ? *p.scale : 1.f);
+    const size_t es = p.c_bf16 ? 2 : 4;
+    void* C = static_cast<uint8_t*>(p.c) + (size_t)ks * p.split_stride * es;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       float v[32];
       tmem_ld32(taddr + c * 32, v);
       const int col0 = nt * BN + c * 32;
-      if (!row_ok || col0 >= p.N) continue;
-      const bool full = (col0 + 32 <= p.N) && p.vec_ok;
-      if (p.c_bf16) {
-        bf16* dst = reinterpret_cast<bf16*>(p.c) + ks * p.split_stride + (int64_t)row * p.ldc + col0;
-        if (full) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            Vec16<bf16> o;
-            if (p.accumulate) o = ld16(dst + q * 8);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float x = p.alpha * v[q * 8 + j];
-              if (p.accumulate) x += __bfloat162float(o.v[j]);
-              o.v[j] = __float2bfloat16_rn(x);
-            }
-            st16(dst + q * 8, o);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (col0 + j < p.N) {
-              float x = p.alpha * v[j];
-              if (p.accumulate) x += __bfloat162float(dst[j]);
-              dst[j] = __float2bfloat16_rn(x);
-            }
-          }
-        }
-      } else {
-        float* dst = reinterpret_cast<float*>(p.c) + ks * p.split_stride + (int64_t)row * p.ldc + col0;
-        if (full) {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (p.accumulate) o = *reinterpret_cast<const float4*>(dst + q * 4);
-            o.x += p.alpha * v[q * 4 + 0];
-            o.y += p.alpha * v[q * 4 + 1];
-            o.z += p.alpha * v[q * 4 + 2];
-            o.w += p.alpha * v[q * 4 + 3];
-            *reinterpret_cast<float4*>(dst + q * 4) = o;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (col0 + j < p.N) {
-              float x = p.alpha * v[j];
-              if (p.accumulate) x += dst[j];
-              dst[j] = x;
-            }
-          }
-        }
-      }
+      if (col0 >= p.N) continue;
+      stage_row(stage, lane, v, a);
+      __syncwarp();
+      if (p.c_bf16)
+        write_block<true>(stage, lane, C, p.ldc, row0, p.M, col0, p.N, p.vec_ok, p.accumulate);
+      else
+        write_block<false>(stage, lane, C, p.ldc, row0, p.M, col0, p.N, p.vec_ok, p.accumulate);
+      __syncwarp();
     }
   }
 };
@@ -118,15 +156,15 @@ struct EpiCE {
     int M, N;
   };
   static __device__ __forceinline__ void tile(const Params& p, int mt, int nt, int ks, int quarter,
-                                              int lane, uint32_t taddr) {
-    const int row = mt * BM + quarter * 32 + lane;
+                                              int lane, uint32_t taddr, uint8_t* stage) {
+    const int row0 = mt * BM + quarter * 32;
+    const int row = row0 + lane;
     const bool row_ok = row < p.M;
     const int64_t t = row_ok ? p.targets[row] : -1;
     float m = -INFINITY, s = 0.f, w = 0.f;
     int bidx = 0x7fffffff;
     float ztv = 0.f;
     bool found = false;
-    bf16* lrow = (row_ok && p.logits) ? p.logits + (int64_t)row * p.ld_logits : nullptr;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       float v[32];
@@ -138,6 +176,12 @@ struct EpiCE {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (j >= nvalid) v[j] = -INFINITY;
+      }
+      if (p.logits) {
+        stage_row(stage, lane, v, 1.f);
+        __syncwarp();
+        write_block<true>(stage, lane, p.logits, p.ld_logits, row0, p.M, col0, p.N, true, false);
+        __syncwarp();
       }
       // chunk maximum with its first index
       float cm = v[0];
@@ -179,22 +223,6 @@ struct EpiCE {
         for (int j = 0; j < 32; ++j)
           if (j == tj) ztv = v[j];
         found = true;
-      }
-      if (lrow) {
-        bf16* dst = lrow + col0;
-        if (nvalid >= 32) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            Vec16<bf16> o;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) o.v[j] = __float2bfloat16_rn(v[q * 8 + j]);
-            st16(dst + q * 8, o);
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < nvalid) dst[j] = __float2bfloat16_rn(v[j]);
-        }
       }
     }
     if (row_ok) {
@@ -454,6 +482,22 @@ static CEWorkspace ce_layout(int64_t rows, int64_t vocab, int64_t dim) {
   return w;
 }
 
+// dW[V, D] (+)= scale * dL^T H: A = dlogits read MN-major, B = hidden MN-major.
+static int dweight_gemm(const bf16* L, int64_t ld_logits, const void* hidden, int64_t h_ld, int M,
+                        int V, int D, const float* scale, void* dweight, int dw_dtype,
+                        int accumulate, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_operand_map(&ma, L, true, V, M, ld_logits, 64))) return rc;
+  if ((rc = make_operand_map(&mb, hidden, true, D, M, h_ld, 64))) return rc;
+  Sched sc{(V + BM - 1) / BM, (D + kBN - 1) / kBN, 1, (M + BK - 1) / BK, 1};
+  const int es = dw_dtype == SOUP_BF16 ? 2 : 4;
+  EpiStore<kBN>::Params ep{dweight, D, 0, scale, 1.f, dw_dtype == SOUP_BF16 ? 1 : 0,
+                           accumulate ? 1 : 0,
+                           (aligned16(dweight) && (D * es) % 16 == 0) ? 1 : 0, V, D};
+  return launch_gemm<true, true, EpiStore<kBN>>(ma, mb, sc, ep, stream);
+}
+
 }  // namespace tc
 }  // namespace soup
 
@@ -534,7 +578,7 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
     if ((rc = make_operand_map(&ma, L, false, rows, vocab, w.ld_logits, BM))) return rc;
     if ((rc = make_operand_map(&mb, weight, true, dim, vocab, w_ld, 64))) return rc;
     Sched sc{(M + BM - 1) / BM, (D + kBN - 1) / kBN, w.splits, (V + BK - 1) / BK, 1};
-    EpiStore<kBN>::Params ep{splitk, dim, (int64_t)rows * dim, 1.f, 0, 0, 1, M, D};
+    EpiStore<kBN>::Params ep{splitk, dim, (int64_t)rows * dim, nullptr, 1.f, 0, 0, 1, M, D};
     if ((rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, sc, ep, stream))) return rc;
     mark_stage(3, stream);
     const int64_t n4 = (int64_t)rows * dim / 4;
@@ -547,18 +591,40 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   }
   // 5. dW = dL^T H
   if (dweight) {
-    CUtensorMap ma, mb;
-    if ((rc = make_operand_map(&ma, L, true, vocab, rows, w.ld_logits, 64))) return rc;
-    if ((rc = make_operand_map(&mb, hidden, true, dim, rows, h_ld, 64))) return rc;
-    Sched sc{(V + BM - 1) / BM, (D + kBN - 1) / kBN, 1, (M + BK - 1) / BK, 1};
-    const int es = dw_dtype == SOUP_BF16 ? 2 : 4;
-    EpiStore<kBN>::Params ep{dweight, dim, 0, 1.f, dw_dtype == SOUP_BF16 ? 1 : 0,
-                             accumulate_dw ? 1 : 0,
-                             (aligned16(dweight) && (dim * es) % 16 == 0) ? 1 : 0, V, D};
-    if ((rc = launch_gemm<true, true, EpiStore<kBN>>(ma, mb, sc, ep, stream))) return rc;
+    if ((rc = dweight_gemm(L, w.ld_logits, hidden, h_ld, M, V, D, nullptr, dweight, dw_dtype,
+                           accumulate_dw, stream)))
+      return rc;
     mark_stage(5, stream);
   }
   return SOUP_OK;
+}
+
+int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const void* hidden,
+                           int64_t h_ld, int64_t rows, int64_t vocab, int64_t dim,
+                           const float* grad_scale, void* dweight, int dw_dtype, int accumulate_dw,
+                           void* stream) {
+  if (!workspace || !hidden || !dweight || rows <= 0 || vocab <= 0 || dim <= 0 ||
+      rows > (1 << 30) || vocab > (1 << 30) || h_ld < dim) {
+    set_last_error("soup_ce_linear_dweight: bad arguments");
+    return SOUP_ERR_INVALID;
+  }
+  if (dw_dtype != SOUP_F32 && dw_dtype != SOUP_BF16) {
+    set_last_error("soup_ce_linear_dweight: dweight dtype must be F32 or BF16");
+    return SOUP_ERR_INVALID;
+  }
+  if (!tma_ok(hidden, h_ld) || (dim % 8) != 0) {
+    set_last_error("soup_ce_linear_dweight: hidden needs 16-byte aligned rows and dim % 8 == 0");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  CEWorkspace w = ce_layout(rows, vocab, dim);
+  if (workspace_bytes < w.total || !aligned16(workspace)) {
+    set_last_error("soup_ce_linear_dweight: workspace too small or misaligned");
+    return SOUP_ERR_WORKSPACE;
+  }
+  const bf16* L = reinterpret_cast<const bf16*>(static_cast<const uint8_t*>(workspace) + w.off_logits);
+  return dweight_gemm(L, w.ld_logits, hidden, h_ld, static_cast<int>(rows), static_cast<int>(vocab),
+                      static_cast<int>(dim), grad_scale, dweight, dw_dtype, accumulate_dw,
+                      as_stream(stream));
 }
 
 int soup_set_stage_events(void** events, int n) {
@@ -595,7 +661,7 @@ int soup_gemm_bf16(const void* a, int64_t lda, int a_mn_major, const void* b, in
   if ((rc = make_operand_map(&ma, a, a_mn_major != 0, m, k, lda, BM))) return rc;
   if ((rc = make_operand_map(&mb, b, b_mn_major != 0, n, k, ldb, kBN))) return rc;
   const int es = c_dtype == SOUP_BF16 ? 2 : 4;
-  EpiStore<kBN>::Params ep{c, ldc, 0, alpha, c_dtype == SOUP_BF16 ? 1 : 0, accumulate ? 1 : 0,
+  EpiStore<kBN>::Params ep{c, ldc, 0, nullptr, alpha, c_dtype == SOUP_BF16 ? 1 : 0, accumulate ? 1 : 0,
                            (aligned16(c) && (ldc * es) % 16 == 0) ? 1 : 0, (int)m, (int)n};
   const int mt = (int)((m + BM - 1) / BM), nt = (int)((n + kBN - 1) / kBN);
   Sched sc{mt, nt, 1, (int)((k + BK - 1) / BK), nt > mt ? 0 : 1};

@@ -176,12 +176,17 @@ struct Sched {
   }
 };
 
+// Per-epilogue-warp staging buffer: 32 rows x 32 fp32 (128 B) + 16 B pad.
+constexpr int kStageRowBytes = 144;
+constexpr int kEpiWarpBytes = 32 * kStageRowBytes;
+
 template <int BN, int STAGES>
 struct SmemLayout {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOff = STAGES * kStageBytes;
+  static constexpr int kEpiOff = STAGES * kStageBytes;
+  static constexpr int kBarOff = kEpiOff + 4 * kEpiWarpBytes;
   // full[S], empty[S], tfull[2], tempty[2], drain, then tmem base + abort flag
   static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
@@ -208,7 +213,8 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity,
 // Epi must provide:
 //   struct Params;
 //   static __device__ void tile(const Params&, int mt, int nt, int ks, int quarter,
-//                               int lane, uint32_t tmem_acc /* lane base applied */);
+//                               int lane, uint32_t tmem_acc /* lane base applied */,
+//                               uint8_t* stage /* this warp's kEpiWarpBytes of smem */);
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
@@ -364,6 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------ epilogue ----
     const int quarter = warp & 3;  // TMEM lanes this warp may access
+    uint8_t* stage = smem + L::kEpiOff + (warp - 2) * kEpiWarpBytes;
     uint32_t lt = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++lt) {
       int mt, nt, ks;
@@ -376,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      Epi::tile(ep, mt, nt, ks, quarter, lane, taddr);
+      Epi::tile(ep, mt, nt, ks, quarter, lane, taddr, stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));

@@ -15,8 +15,10 @@ through one ``soup_ce_linear`` launch sequence (tcgen05 logits GEMM with the
 online-softmax epilogue, per-row finalize writing dlogits in place, split-K
 dX GEMM, dW GEMM) in bf16 with fp32 accumulation and fp32 metrics. ``chunk``
 stays in the signature; token rows are processed in blocks sized by
-``CONFIG["ce_workspace_bytes"]`` instead, which bounds the logits buffer the
-way ``chunk`` bounds it in the reference.
+``CE_WORKSPACE_BYTES`` instead, which bounds the logits buffer the way
+``chunk`` bounds it in the reference. With a trainable head the lm_head
+gradient GEMM runs in backward, scaled by the upstream gradient inside its
+epilogue, and accumulates into ``weight.grad`` in the weight's dtype.
 """
 
 from __future__ import annotations
@@ -152,6 +154,63 @@ def fused_linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, targe
     return losses, ents, corr, total, dh, dw
 
 
+def _fused_forward_keep_dlogits(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
+                                denominator: float, ignore_index: int):
+    """Forward + dhidden in one pass, leaving the dlogits in a workspace owned by the caller.
+
+    Returns ``(losses, ents, corr, sums, dh, state)`` where ``state`` holds the
+    workspace and the bf16 hidden rows needed by :func:`_dweight_from_state`.
+    """
+    n, d = hidden.shape
+    v = weight.shape[0]
+    h = hidden.detach()
+    if h.dtype != torch.bfloat16 or not _tma_rows_ok(h):
+        h = h.to(torch.bfloat16).contiguous()
+    w = _bf16_weight(weight)
+    t = targets.reshape(-1)
+    if t.dtype != torch.int64 or not t.is_contiguous():
+        t = t.to(torch.int64).contiguous()
+    dev = hidden.device
+    lib = _lib.lib()
+    ws_bytes = lib.soup_ce_linear_workspace_bytes(n, v, d)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    losses = torch.empty(n, dtype=torch.float32, device=dev)
+    ents = torch.empty(n, dtype=torch.float32, device=dev)
+    corr = torch.empty(n, dtype=torch.int32, device=dev)
+    sums = torch.empty(2, dtype=torch.float32, device=dev)
+    dh = torch.empty(n, d, dtype=torch.bfloat16, device=dev)
+    _lib.call("soup_ce_linear", dev, h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
+              t.data_ptr(), n, v, d, float(denominator), int(ignore_index), losses.data_ptr(),
+              ents.data_ptr(), corr.data_ptr(), sums.data_ptr(), dh.data_ptr(), 0, _lib.F32, 0,
+              ws.data_ptr(), ws_bytes, _lib.stream_of(hidden))
+    return losses, ents, corr, sums, dh, {"ws": ws, "h": h, "rows": n, "vocab": v, "dim": d}
+
+
+def _dweight_from_state(state, weight: torch.Tensor, grad_scale: torch.Tensor) -> None:
+    """weight.grad (+)= grad_scale * dL^T H, in the weight's dtype, one GEMM launch."""
+    scale = grad_scale.detach().to(torch.float32).reshape(1).contiguous()
+    dev = weight.device
+    if weight.dtype in (torch.bfloat16, torch.float32):
+        target = weight.grad
+        accumulate = 1
+        if target is None:
+            target = torch.empty_like(weight)
+            accumulate = 0
+        _lib.call("soup_ce_linear_dweight", dev, state["ws"].data_ptr(), state["ws"].numel(),
+                  state["h"].data_ptr(), state["h"].stride(0), state["rows"], state["vocab"],
+                  state["dim"], scale.data_ptr(), target.data_ptr(), _lib.dtype_code(weight.dtype),
+                  accumulate, _lib.stream_of(weight))
+        if weight.grad is None:
+            weight.grad = target
+        return
+    tmp = torch.empty(weight.shape, dtype=torch.float32, device=dev)
+    _lib.call("soup_ce_linear_dweight", dev, state["ws"].data_ptr(), state["ws"].numel(),
+              state["h"].data_ptr(), state["h"].stride(0), state["rows"], state["vocab"],
+              state["dim"], scale.data_ptr(), tmp.data_ptr(), _lib.F32, 0, _lib.stream_of(weight))
+    g = tmp.to(weight.dtype)
+    weight.grad = g if weight.grad is None else weight.grad.add_(g)
+
+
 def chunk_cross_entropy_triton(head: Any, piece: torch.Tensor, target: torch.Tensor,
                                ignore_index: int = IGNORE_INDEX, denominator: float = 1.0,
                                with_grad: bool = True
@@ -222,12 +281,22 @@ def make_triton_chunked_loss_function():
             weight = _extract_head_weight(head)
             ctx.with_grad = with_grad
             ctx.weight = None
+            ctx.dw_state = None
             if weight is not None and hidden.is_cuda:
                 B, S, D = hidden.shape
                 want_dw = bool(with_grad and weight.requires_grad)
-                losses, ents, corr, sums, dh, dw = fused_linear_cross_entropy(
-                    hidden.reshape(-1, D), weight, target.reshape(-1), den, ignore_index,
-                    with_grad, compute_dw=want_dw)
+                h2 = hidden.reshape(-1, D)
+                state = None
+                if want_dw and _rows_per_block(h2.shape[0], weight.shape[0], D,
+                                               CE_WORKSPACE_BYTES) == h2.shape[0]:
+                    # dW is deferred to backward, where grad_loss scales it in the epilogue
+                    losses, ents, corr, sums, dh, state = _fused_forward_keep_dlogits(
+                        h2, weight, target.reshape(-1), den, ignore_index)
+                    dw = None
+                else:
+                    losses, ents, corr, sums, dh, dw = fused_linear_cross_entropy(
+                        h2, weight, target.reshape(-1), den, ignore_index, with_grad,
+                        compute_dw=want_dw)
                 token_entropy = ents.view(B, S)
                 token_loss = losses.view(B, S)
                 correct = corr.sum()
@@ -237,9 +306,10 @@ def make_triton_chunked_loss_function():
                     if grad.dtype != hidden.dtype:
                         grad = grad.to(hidden.dtype)
                     ctx.save_for_backward(grad)
-                    if dw is not None:
+                    if want_dw:
                         ctx.weight = weight
                         ctx.dw = dw
+                        ctx.dw_state = state
             else:
                 grad = torch.zeros_like(hidden) if with_grad else None
                 total = torch.zeros((), dtype=torch.float32, device=hidden.device)
@@ -270,12 +340,16 @@ def make_triton_chunked_loss_function():
             (grad,) = ctx.saved_tensors
             if ctx.weight is not None:
                 w = ctx.weight
-                g = (ctx.dw * grad_loss).to(w.dtype)
-                if w.grad is None:
-                    w.grad = g
+                if ctx.dw_state is not None:
+                    _dweight_from_state(ctx.dw_state, w, grad_loss)
                 else:
-                    w.grad.add_(g)
+                    g = (ctx.dw * grad_loss).to(w.dtype)
+                    if w.grad is None:
+                        w.grad = g
+                    else:
+                        w.grad.add_(g)
                 ctx.dw = None
+                ctx.dw_state = None
             return ((grad * grad_loss).to(grad.dtype), None, None, None, None, None, None)
 
     return B200ChunkedHeadLoss

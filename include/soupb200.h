@@ -139,6 +139,18 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
                    int32_t* correct, float* sums, void* dhidden, void* dweight, int dw_dtype,
                    int accumulate_dw, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The lm_head gradient from the dlogits that a preceding soup_ce_linear call
+ * with a non-NULL dhidden left in `workspace` (same rows/vocab/dim/hidden):
+ * dweight (+)= grad_scale[0] * dL^T H, where grad_scale is an optional device
+ * fp32 scalar (the upstream gradient of the loss; NULL = 1). Lets an autograd
+ * backward apply its upstream gradient inside the GEMM epilogue instead of in a
+ * separate pass over the [vocab, dim] gradient. Extends chunked_ce.py:307-311
+ * (the reference's head is frozen and has no gradient). */
+int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const void* hidden,
+                           int64_t h_ld, int64_t rows, int64_t vocab, int64_t dim,
+                           const float* grad_scale, void* dweight, int dw_dtype, int accumulate_dw,
+                           void* stream);
+
 /* Stage timing for measurement: while set (n > 0), each soup_ce_linear call on
  * this host thread records events[i] on its stream after stage i:
  * 0 logits GEMM, 1 finalize, 2 sums, 3 dX GEMM, 4 dX reduce, 5 dW GEMM

@@ -186,9 +186,19 @@ def test_autograd_function_trainable_head_accumulates_weight_grad():
     Fn = make_triton_chunked_loss_function()
     h = hidden.cuda().requires_grad_(True)
     loss, *_ = Fn.apply(h, head, target.cuda(), 64, den, -100, True)
-    loss.backward()
-    assert head.weight.grad is not None
+    (3.0 * loss).backward()  # upstream gradient 3 is applied inside the dW GEMM epilogue
+    assert head.weight.grad is not None and head.weight.grad.dtype == torch.bfloat16
     assert cosine(head.weight.grad, ref[5]) >= 0.999  # bf16-stored weight grad
+    g1 = head.weight.grad.float().cpu()
+    ratio = float((g1 * ref[5]).sum() / (ref[5] * ref[5]).sum())
+    assert abs(ratio - 3.0) < 0.02, ratio
+    # a second backward accumulates into the existing gradient
+    h2 = hidden.cuda().requires_grad_(True)
+    loss2, *_ = Fn.apply(h2, head, target.cuda(), 64, den, -100, True)
+    loss2.backward()
+    g2 = head.weight.grad.float().cpu()
+    ratio2 = float((g2 * ref[5]).sum() / (ref[5] * ref[5]).sum())
+    assert abs(ratio2 - 4.0) < 0.03, ratio2
 
 
 def test_autograd_function_callable_head_path():

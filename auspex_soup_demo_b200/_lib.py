@@ -72,6 +72,8 @@ _SIGNATURES = {
     "soup_ce_linear_dweight": (c_int, [c_vp, c_sz, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,
                                        c_int, c_int, c_vp]),
     "soup_set_stage_events": (c_int, [ctypes.POINTER(c_vp), c_int]),
+    "soup_nf4_quantize": (c_int, [c_vp, c_i64, c_int, c_int, ctypes.POINTER(c_f), c_vp, c_vp, c_vp]),
+    "soup_nf4_dequant": (c_int, [c_vp, c_vp, c_i64, c_int, ctypes.POINTER(c_f), c_vp, c_int, c_vp]),
     "soup_gemm_bf16": (c_int, [c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_i64,
                                c_i64, c_i64, c_f, c_int, c_vp]),
 }

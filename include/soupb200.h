@@ -158,6 +158,19 @@ int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const 
  * cudaEvent_t handles owned by the caller. */
 int soup_set_stage_events(void** events, int n);
 
+/* ---- NF4 base weights for the QLoRA step ------------------------------------
+ * No kernel in the reference: there the 4-bit base layers come from
+ * bitsandbytes (Linear4bit, blocksize 64; harness/eval_adapter.py:26-28 loads
+ * them). Blockwise absmax quantisation to the nearest of 16 code values
+ * (code16: host array, sorted ascending, normalised to [-1, 1]); packed[n/2],
+ * two 4-bit indices per byte, the earlier element in the high nibble;
+ * absmax[n/64] fp32. Ties between two codes pick the lower index. */
+int soup_nf4_quantize(const void* weight, int64_t n, int dtype, int blocksize, const float* code16,
+                      uint8_t* packed, float* absmax, void* stream);
+/* out[i] = code16[index_i] * absmax[i / 64] in dtype (16-byte aligned buffers). */
+int soup_nf4_dequant(const uint8_t* packed, const float* absmax, int64_t n, int blocksize,
+                     const float* code16, void* out, int dtype, void* stream);
+
 /* ---- Plain tcgen05 GEMM (building block, exposed for tests) ---------------
  * C[m, n] = alpha * sum_k A(m, k) * B(n, k) (+ C if accumulate), bf16 inputs,
  * fp32 accumulation. a_mn_major = 0: A stored [M, K] (lda >= K); 1: stored

@@ -468,6 +468,105 @@ def run_memory_op(args):
     print(json.dumps(line), flush=True)
 
 
+def run_qlora(args):
+    """Qwen2.5-1.5B-architecture QLoRA train step: tokens/s (whole job).
+
+    Random-init model (28 layers, NF4 blocksize 64, LoRA r16/a32 on
+    q/k/v/o/gate/up/down), uniform random token ids, AdamW 2e-4, the fused
+    patches installed. One step = forward + backward + optimiser step on
+    `batch` x `seq` tokens per GPU. N > 1: DDP over NCCL, LoRA grads only.
+    """
+    import torch.distributed as dist
+
+    from auspex_soup_demo_b200 import _lib, apply, qlora
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    apply()
+    B, S = args.batch, args.seq
+    model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=args.layers), device=dev,
+                                    seed=0)
+    trainer = qlora.QLoRATrainer(model, lr=2e-4, ddp=world > 1)
+    g = torch.Generator().manual_seed(1234 + rank)
+    ids_cpu = torch.randint(0, 151936, (B, S), generator=g)
+    labels_cpu = qlora.causal_labels(ids_cpu)
+    ids, labels = ids_cpu.to(dev), labels_cpu.to(dev)
+    den = float((labels_cpu != -100).sum())
+    for _ in range(max(args.warmup, 3)):
+        trainer.step(ids, labels, den)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            loss, _ = trainer.step(ids, labels, den)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t)
+    tok_s = world * B * S / (ms * 1e-3)
+    # e2e: token ids from pinned host memory each step, loss read back
+    ids_pin = ids_cpu.pin_memory()
+    lab_pin = labels_cpu.pin_memory()
+    out_pin = torch.empty(1, dtype=torch.float32).pin_memory()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e2.record(stream)
+    for _ in range(args.steps):
+        i_d = ids_pin.to(dev, non_blocking=True)
+        l_d = lab_pin.to(dev, non_blocking=True)
+        loss, _ = trainer.step(i_d, l_d, den)
+        out_pin.copy_(loss.view(1), non_blocking=True)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e2.elapsed_time(e3) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t)
+    assert _lib.device_error(dev) == 0
+    n_lora = sum(p.numel() for p in qlora.lora_parameters(model))
+    line = {"metric": "QLoRA train tokens/s", "value": round(tok_s, 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids)",
+            "config": {"workload": "Qwen2.5-1.5B-architecture QLoRA step",
+                       "layers": args.layers, "batch_per_gpu": B, "seq_len": S,
+                       "lora": "r16 a32 q/k/v/o/gate/up/down", "lora_params": n_lora,
+                       "base": "NF4 blocksize 64, dequantised per use", "optimizer": "AdamW 2e-4",
+                       "parallelism": f"dp{world}" + (" (DDP, NCCL allreduce of LoRA grads)"
+                                                      if world > 1 else ""),
+                       "l2": "weights and activations far larger than L2"},
+            "e2e": {"value": round(world * B * S / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 2 * B * S * 8, "d2h_bytes_per_step": 4,
+                    "ms_per_step": round(e2e_ms, 3)},
+            "final_loss": float(loss), "clocks": clocks.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def _committed_traffic():
     """DRAM bytes per launch of the logits GEMM from the committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
@@ -491,11 +590,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", default="ce", choices=["ce", "rmsnorm", "swiglu", "rope"],
-                    help="ce (default): the fused head CE; others: one memory-bound op's HBM GB/s")
+    ap.add_argument("--workload", default="ce", choices=["ce", "rmsnorm", "swiglu", "rope", "qlora"],
+                    help="ce (default): the fused head CE; rmsnorm/swiglu/rope: one memory-bound "
+                         "op's HBM GB/s; qlora: the Qwen2.5-1.5B QLoRA train step's tokens/s")
+    ap.add_argument("--batch", type=int, default=4, help="qlora: sequences per GPU")
+    ap.add_argument("--seq", type=int, default=512, help="qlora: tokens per sequence")
+    ap.add_argument("--layers", type=int, default=28, help="qlora: decoder layers")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "qlora":
+        run_qlora(args)
     elif args.workload != "ce":
         run_memory_op(args)
     else:

@@ -1,0 +1,141 @@
+"""GPU checks of the QLoRA step: NF4 kernels vs the oracle (bit-exact), the
+NF4 + LoRA linear vs a dense reference, and a small Qwen2 model trained with
+the fused patches vs the same model on the original transformers code."""
+
+import contextlib
+
+import pytest
+import torch
+
+import oracle.nf4 as onf4
+from auspex_soup_demo_b200 import apply, qlora
+from helpers import cosine
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("shape,dtype", [((1536, 256), torch.bfloat16), ((8960, 64), torch.float32),
+                                         ((64, 64), torch.float16)])
+def test_nf4_quantize_dequantize_bit_exact(shape, dtype):
+    g = torch.Generator().manual_seed(1)
+    w = (0.02 * torch.randn(shape, generator=g)).to(dtype)
+    w[0, :64] = 0.0  # an all-zero block
+    code = onf4.nf4_code()
+    p_ref, a_ref = onf4.nf4_quantize(w, code)
+    p, a = qlora.nf4_quantize(w.cuda())
+    assert torch.equal(a.cpu(), a_ref)
+    assert torch.equal(p.cpu(), p_ref)
+    d = qlora.nf4_dequantize(p, a, shape, dtype=torch.bfloat16)
+    d_ref = onf4.nf4_dequantize(p_ref, a_ref, code, dtype=torch.bfloat16).view(shape)
+    assert torch.equal(d.cpu(), d_ref)
+    d32 = qlora.nf4_dequantize(p, a, shape, dtype=torch.float32)
+    assert torch.equal(d32.cpu(), onf4.nf4_dequantize(p_ref, a_ref, code, dtype=torch.float32).view(shape))
+
+
+def test_lora_nf4_linear_forward_backward():
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(512, 384, bias=True, device="cuda", dtype=torch.bfloat16)
+    mod = qlora.LoRANF4Linear(lin, r=16, alpha=32)
+    torch.nn.init.normal_(mod.lora_B, std=0.05)
+    x = torch.randn(3, 40, 512, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = mod(x)
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    # dense fp32 reference on the dequantised base weight
+    wq = mod.dequantized_weight(torch.float32)
+    xr = x.detach().float().requires_grad_(True)
+    A = mod.lora_A.detach().clone().requires_grad_(True)
+    B = mod.lora_B.detach().clone().requires_grad_(True)
+    yr = xr @ wq.t() + mod.bias.float() + (xr @ A.t() @ B.t()) * mod.scaling
+    yr.backward(dy.float())
+    assert cosine(y, yr) > 0.9999
+    assert cosine(x.grad, xr.grad) > 0.999
+    assert cosine(mod.lora_A.grad, A.grad) > 0.999
+    assert cosine(mod.lora_B.grad, B.grad) > 0.999
+
+
+@contextlib.contextmanager
+def original_transformers_code():
+    """Temporarily restore the unpatched Qwen2 functions."""
+    from transformers.models.qwen2 import modeling_qwen2 as m
+
+    saved = (m.Qwen2RMSNorm.forward, m.Qwen2MLP.forward, m.apply_rotary_pos_emb)
+    m.Qwen2RMSNorm.forward = getattr(saved[0], "_soup_original", saved[0])
+    m.Qwen2MLP.forward = getattr(saved[1], "_soup_original", saved[1])
+    m.apply_rotary_pos_emb = getattr(saved[2], "_soup_original", saved[2])
+    try:
+        yield
+    finally:
+        m.Qwen2RMSNorm.forward, m.Qwen2MLP.forward, m.apply_rotary_pos_emb = saved
+
+
+class EagerHeadLoss(torch.autograd.Function):
+    """Unfused head CE with the reference's chunked-loss signature (fp32 logits)."""
+
+    @staticmethod
+    def forward(ctx, hidden, head, target, chunk, denominator, ignore_index, with_grad):
+        with torch.enable_grad():
+            h = hidden.detach().requires_grad_(True)
+            logits = (h @ head.weight.t()).float()
+            loss = torch.nn.functional.cross_entropy(
+                logits.view(-1, logits.shape[-1]), target.view(-1), ignore_index=ignore_index,
+                reduction="sum") / denominator
+            (g,) = torch.autograd.grad(loss, h)
+        ctx.save_for_backward(g)
+        z = torch.zeros(hidden.shape[:2], device=hidden.device)
+        return loss.detach(), z, z, torch.zeros((), dtype=torch.long, device=hidden.device)
+
+    @staticmethod
+    def backward(ctx, gl, *_):
+        (g,) = ctx.saved_tensors
+        return g * gl, None, None, None, None, None, None
+
+
+def _small_model(seed=0):
+    cfg = qlora.qwen2_1p5b_config(num_layers=2, hidden_size=256, intermediate_size=640,
+                                  num_attention_heads=4, num_key_value_heads=2, vocab_size=2048)
+    model = qlora.build_qwen2_qlora(cfg, device="cuda", seed=seed)
+    for m in model.modules():  # non-zero B so all LoRA factors receive gradients
+        if isinstance(m, qlora.LoRANF4Linear):
+            torch.nn.init.normal_(m.lora_B, std=0.02)
+    return model
+
+
+def _grads(model, ids, labels, loss_fn):
+    model.zero_grad(set_to_none=True)
+    hidden = model.model(input_ids=ids).last_hidden_state
+    den = float((labels != -100).sum())
+    loss, *_ = loss_fn.apply(hidden, model.lm_head, labels, 64, den, -100, True)
+    loss.backward()
+    return float(loss), {n: p.grad.detach().clone() for n, p in model.named_parameters()
+                         if p.requires_grad}
+
+
+def test_patched_qwen2_matches_original_code():
+    from auspex_soup_demo_b200.kernels import make_triton_chunked_loss_function
+
+    apply()
+    model = _small_model()
+    model.train()
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, 2048, (2, 96), generator=g).cuda()
+    labels = qlora.causal_labels(ids)
+    loss_fused, g_fused = _grads(model, ids, labels, make_triton_chunked_loss_function())
+    with original_transformers_code():
+        loss_ref, g_ref = _grads(model, ids, labels, EagerHeadLoss)
+    assert abs(loss_fused - loss_ref) <= 2e-3 * abs(loss_ref), (loss_fused, loss_ref)
+    worst = min(cosine(g_fused[k], g_ref[k]) for k in g_ref)
+    assert worst > 0.99, worst
+    assert sum(cosine(g_fused[k], g_ref[k]) for k in g_ref) / len(g_ref) > 0.999
+
+
+def test_qlora_trainer_reduces_loss():
+    apply()
+    model = _small_model(seed=1)
+    trainer = qlora.QLoRATrainer(model, lr=2e-3)
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, 2048, (4, 64), generator=g).cuda()
+    labels = qlora.causal_labels(ids)
+    den = float((labels != -100).sum())
+    losses = [float(trainer.step(ids, labels, den)[0]) for _ in range(8)]
+    assert losses[-1] < losses[0] - 0.05, losses

@@ -106,7 +106,10 @@ def patch_qwen2_mlp():
         def _swiglu_forward(hidden_states):
             return fast_swiglu(self.gate_proj(hidden_states), self.up_proj(hidden_states))
 
-        swiglu_out = torch.utils.checkpoint.checkpoint(_swiglu_forward, x, use_reentrant=False)
+        # the recomputed region has no random ops: skip the RNG state save/restore,
+        # which also keeps the step capturable in a CUDA graph
+        swiglu_out = torch.utils.checkpoint.checkpoint(_swiglu_forward, x, use_reentrant=False,
+                                                       preserve_rng_state=False)
         return self.down_proj(swiglu_out)
 
     forward._soup_b200 = True

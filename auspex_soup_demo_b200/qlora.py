@@ -219,39 +219,100 @@ def causal_labels(input_ids: torch.Tensor, ignore_index: int = -100) -> torch.Te
 
 
 class QLoRATrainer:
-    """Forward (fused ops) -> fused head CE -> backward -> AdamW on the LoRA factors."""
+    """Forward (fused ops) -> fused head CE -> backward -> gradient all-reduce -> AdamW.
+
+    The LoRA gradients live in one flat fp32 buffer (each parameter's ``.grad``
+    is a view of it). With ``ddp=True`` (an initialised process group, one
+    process per GPU) the whole buffer is averaged over ranks by a single
+    all-reduce after backward: 73.9 MB for the 1.5B model's 18.5 M LoRA
+    parameters, a fraction of a millisecond over NVLink, so it is not worth
+    overlapping with the backward pass. Everything in :meth:`step` is GPU work
+    with no host synchronisation, so :meth:`capture` can record one whole step
+    (forward, backward, all-reduce, AdamW) as a CUDA graph and :meth:`replay`
+    re-launches it with a single call.
+    """
 
     def __init__(self, model, lr: float = 2e-4, chunk: int = 64, ddp: bool = False,
-                 bucket_cap_mb: float = 25.0, loss_fn=None, fused_adamw: Optional[bool] = None):
+                 loss_fn=None, fused_adamw: Optional[bool] = None):
         from .kernels import make_triton_chunked_loss_function
 
         self.model = model
         self.params = lora_parameters(model)
-        body = model.model
+        self.body = model.model
+        self.ddp = ddp
         if ddp:
             import torch.distributed as dist
 
             assert dist.is_initialized(), "ddp=True needs an initialised process group"
-            dev = next(model.parameters()).device
-            body = torch.nn.parallel.DistributedDataParallel(
-                body, device_ids=[dev.index] if dev.type == "cuda" else None,
-                bucket_cap_mb=bucket_cap_mb, gradient_as_bucket_view=True,
-                broadcast_buffers=False)
-        self.body = body
+            self.world = dist.get_world_size()
+            self.nccl = dist.get_backend() == "nccl"
+            for p in self.params:  # every rank starts from rank 0's adapters
+                dist.broadcast(p.data, src=0)
+        else:
+            self.world = 1
+        total = sum(p.numel() for p in self.params)
+        dev = self.params[0].device
+        self.flat_grad = torch.zeros(total, dtype=torch.float32, device=dev)
+        off = 0
+        for p in self.params:
+            p.grad = self.flat_grad[off:off + p.numel()].view_as(p)
+            off += p.numel()
         on_cuda = self.params[0].is_cuda
         fused = on_cuda if fused_adamw is None else fused_adamw
-        self.opt = torch.optim.AdamW(self.params, lr=lr, fused=fused)
+        self.opt = torch.optim.AdamW(self.params, lr=lr, fused=fused, capturable=on_cuda)
         # loss_fn: an autograd Function with the reference's chunked-loss signature
         self.loss_fn = loss_fn or make_triton_chunked_loss_function()
         self.chunk = chunk
+        self.graph = None
         model.train()
 
+    def _allreduce_grads(self):
+        import torch.distributed as dist
+
+        if self.nccl:
+            dist.all_reduce(self.flat_grad, op=dist.ReduceOp.AVG)
+        else:  # gloo has no AVG
+            dist.all_reduce(self.flat_grad, op=dist.ReduceOp.SUM)
+            self.flat_grad.mul_(1.0 / self.world)
+
     def step(self, input_ids: torch.Tensor, labels: torch.Tensor, denominator: float):
+        self.flat_grad.zero_()
         out = self.body(input_ids=input_ids)
         hidden = out.last_hidden_state if hasattr(out, "last_hidden_state") else out[0]
         loss, entropy, token_loss, correct = self.loss_fn.apply(
             hidden, self.model.lm_head, labels, self.chunk, denominator, -100, True)
         loss.backward()
+        if self.ddp:
+            self._allreduce_grads()
         self.opt.step()
-        self.opt.zero_grad(set_to_none=True)
         return loss.detach(), correct
+
+    def capture(self, input_ids: torch.Tensor, labels: torch.Tensor, denominator: float,
+                warmup: int = 3):
+        """Record one step on static `input_ids`/`labels` buffers as a CUDA graph.
+
+        Later batches are copied into the same buffers before :meth:`replay`.
+        `denominator` is baked into the graph (the count of non-ignored labels
+        is the same for every batch of fixed shape without padding).
+        """
+        self.static_ids = input_ids
+        self.static_labels = labels
+        side = torch.cuda.Stream(input_ids.device)
+        side.wait_stream(torch.cuda.current_stream(input_ids.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.step(input_ids, labels, denominator)
+        torch.cuda.current_stream(input_ids.device).wait_stream(side)
+        torch.cuda.synchronize(input_ids.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.static_loss, self.static_correct = self.step(input_ids, labels, denominator)
+        return self.static_loss
+
+    def replay(self):
+        self.graph.replay()
+        return self.static_loss, self.static_correct
+
+    def release_graph(self):
+        """Drop the captured graph (do this before destroying the process group)."""
+        self.graph = None

@@ -498,8 +498,17 @@ def run_qlora(args):
     labels_cpu = qlora.causal_labels(ids_cpu)
     ids, labels = ids_cpu.to(dev), labels_cpu.to(dev)
     den = float((labels_cpu != -100).sum())
+    # every rank's batch has the same number of labelled tokens (no padding), so
+    # averaging the per-rank gradients gives the gradient of the global mean loss
+    use_graph = not args.no_graph
+    if use_graph:
+        trainer.capture(ids, labels, den, warmup=max(args.warmup, 3))
+
+    def one_step():
+        return trainer.replay() if use_graph else trainer.step(ids, labels, den)
+
     for _ in range(max(args.warmup, 3)):
-        trainer.step(ids, labels, den)
+        one_step()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -510,7 +519,7 @@ def run_qlora(args):
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
-            loss, _ = trainer.step(ids, labels, den)
+            loss, _ = one_step()
         e1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
@@ -532,9 +541,9 @@ def run_qlora(args):
     torch.cuda.synchronize()
     e2.record(stream)
     for _ in range(args.steps):
-        i_d = ids_pin.to(dev, non_blocking=True)
-        l_d = lab_pin.to(dev, non_blocking=True)
-        loss, _ = trainer.step(i_d, l_d, den)
+        ids.copy_(ids_pin, non_blocking=True)
+        labels.copy_(lab_pin, non_blocking=True)
+        loss, _ = one_step()
         out_pin.copy_(loss.view(1), non_blocking=True)
     e3.record(stream)
     torch.cuda.synchronize()
@@ -553,15 +562,16 @@ def run_qlora(args):
                        "layers": args.layers, "batch_per_gpu": B, "seq_len": S,
                        "lora": "r16 a32 q/k/v/o/gate/up/down", "lora_params": n_lora,
                        "base": "NF4 blocksize 64, dequantised per use", "optimizer": "AdamW 2e-4",
-                       "parallelism": f"dp{world}" + (" (DDP, NCCL allreduce of LoRA grads)"
+                       "parallelism": f"dp{world}" + (" (one NCCL allreduce of the flat LoRA grads)"
                                                       if world > 1 else ""),
                        "l2": "weights and activations far larger than L2"},
             "e2e": {"value": round(world * B * S / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 2 * B * S * 8, "d2h_bytes_per_step": 4,
                     "ms_per_step": round(e2e_ms, 3)},
-            "final_loss": float(loss), "clocks": clocks.summary()}
+            "final_loss": float(loss), "cuda_graph": use_graph, "clocks": clocks.summary()}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    trainer.release_graph()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -596,6 +606,7 @@ def main():
     ap.add_argument("--batch", type=int, default=4, help="qlora: sequences per GPU")
     ap.add_argument("--seq", type=int, default=512, help="qlora: tokens per sequence")
     ap.add_argument("--layers", type=int, default=28, help="qlora: decoder layers")
+    ap.add_argument("--no-graph", action="store_true", help="qlora: launch eagerly, no CUDA graph")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

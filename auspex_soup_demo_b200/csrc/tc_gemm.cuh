@@ -20,7 +20,7 @@
 // waiting role records an error code in the device error word (`err`),
 // raises a CTA-wide abort flag, the producer waits (bounded) for its copies
 // still in flight, the MMA warp drains its MMAs, and the CTA frees its TMEM
-// and exits. No TMA multicast is used anywhere.
+// and exits. Every TMA load writes only this CTA's own shared memory.
 #pragma once
 
 #include <cuda.h>
@@ -72,7 +72,7 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
 }
-// 2-D TMA tile load into this CTA's shared memory (no multicast).
+// 2-D TMA tile load into this CTA's own shared memory.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int32_t x, int32_t y) {
   asm volatile(

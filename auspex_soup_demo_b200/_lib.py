@@ -71,6 +71,13 @@ _SIGNATURES = {
                                c_vp]),
     "soup_ce_linear_dweight": (c_int, [c_vp, c_sz, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,
                                        c_int, c_int, c_vp]),
+    "soup_ce_vp_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64]),
+    "soup_ce_vp_forward": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp,
+                                   c_vp, c_sz, c_vp]),
+    "soup_ce_vp_combine": (c_int, [c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp,
+                                   c_vp, c_vp]),
+    "soup_ce_vp_backward": (c_int, [c_vp, c_sz, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64,
+                                    c_i64, c_vp, c_f, c_i64, c_vp, c_int, c_vp, c_int, c_int, c_vp]),
     "soup_set_stage_events": (c_int, [ctypes.POINTER(c_vp), c_int]),
     "soup_nf4_quantize": (c_int, [c_vp, c_i64, c_int, c_int, ctypes.POINTER(c_f), c_vp, c_vp, c_vp]),
     "soup_nf4_dequant": (c_int, [c_vp, c_vp, c_i64, c_int, ctypes.POINTER(c_f), c_vp, c_int, c_vp]),

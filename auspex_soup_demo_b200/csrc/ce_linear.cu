@@ -153,6 +153,7 @@ struct EpiCE {
     float* zt;         // [M] target logit (written by the tile holding it)
     bf16* logits;      // [M][ld_logits] or nullptr
     int64_t ld_logits;
+    int64_t vocab_offset;  // first vocabulary row of this weight shard (0 unsharded)
     int M, N;
   };
   static __device__ __forceinline__ void tile(const Params& p, int mt, int nt, int ks, int quarter,
@@ -160,7 +161,7 @@ struct EpiCE {
     const int row0 = mt * BM + quarter * 32;
     const int row = row0 + lane;
     const bool row_ok = row < p.M;
-    const int64_t t = row_ok ? p.targets[row] : -1;
+    const int64_t t = row_ok ? p.targets[row] - p.vocab_offset : -1;
     float m = -INFINITY, s = 0.f, w = 0.f;
     int bidx = 0x7fffffff;
     float ztv = 0.f;
@@ -412,9 +413,10 @@ __global__ void __launch_bounds__(1024) ce_sums_kernel(const float* __restrict__
   }
 }
 
-// out[m, n] = bf16(sum_s ws[s][m][n]), fixed order over s.
+// out[m, n] = sum_s ws[s][m][n] (fixed order over s), stored as OutT.
+template <typename OutT>
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t slice,
-                                     int rows, int cols, bf16* __restrict__ out, int64_t ldo) {
+                                     int rows, int cols, OutT* __restrict__ out, int64_t ldo) {
   const int64_t n4 = (int64_t)rows * cols / 4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -428,11 +430,107 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
       acc.w += v.w;
     }
     const int64_t r = e / cols, c = e % cols;
-    bf16* o = out + r * ldo + c;
-    o[0] = __float2bfloat16_rn(acc.x);
-    o[1] = __float2bfloat16_rn(acc.y);
-    o[2] = __float2bfloat16_rn(acc.z);
-    o[3] = __float2bfloat16_rn(acc.w);
+    OutT* o = out + r * ldo + c;
+    o[0] = Cvt<OutT>::from_f(acc.x);
+    o[1] = Cvt<OutT>::from_f(acc.y);
+    o[2] = Cvt<OutT>::from_f(acc.z);
+    o[3] = Cvt<OutT>::from_f(acc.w);
+  }
+}
+
+// ------------------------------------------------- vocab-parallel kernels ---
+// Per row (one warp each): merge this shard's tile states into one record
+// {max, sum exp, sum z*exp, global argmax (int bits), target logit or 0}.
+__global__ void __launch_bounds__(256) ce_shard_state_kernel(
+    const float4* __restrict__ partials, int n_tiles, const float* __restrict__ zt,
+    const int64_t* __restrict__ targets, int rows, int vocab_shard, int64_t vocab_offset,
+    float* __restrict__ states) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  SoftmaxState st = sm_init();
+  for (int j = lane; j < n_tiles; j += 32) {
+    float4 p = partials[(int64_t)j * rows + row];
+    st = sm_merge(st, SoftmaxState{p.x, p.y, p.z, __float_as_int(p.w)});
+  }
+  st = sm_warp_reduce(st);
+  if (lane == 0) {
+    const int64_t t = targets[row] - vocab_offset;
+    float* o = states + (int64_t)row * 5;
+    o[0] = st.m;
+    o[1] = st.s;
+    o[2] = st.w;
+    o[3] = __int_as_float(static_cast<int>(st.idx + vocab_offset));
+    o[4] = (t >= 0 && t < vocab_shard) ? zt[row] : 0.f;
+  }
+}
+
+// Per row (one thread each): merge the ranks' records in rank order (ties keep
+// the smaller global index), then the row metrics and the global lse.
+__global__ void __launch_bounds__(256) ce_combine_kernel(
+    const float* __restrict__ states, int nranks, int64_t rank_stride,
+    const int64_t* __restrict__ targets, int rows, int64_t vocab_total, int64_t ignore_index,
+    float* __restrict__ losses, float* __restrict__ entropies, int32_t* __restrict__ correct,
+    float* __restrict__ lse_out) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  SoftmaxState st = sm_init();
+  float z_t = 0.f;
+  for (int r = 0; r < nranks; ++r) {
+    const float* o = states + r * rank_stride + (int64_t)row * 5;
+    st = sm_merge(st, SoftmaxState{o[0], o[1], o[2], __float_as_int(o[3])});
+    z_t += o[4];
+  }
+  const int64_t t = targets[row];
+  const bool ignored = t == ignore_index;
+  const bool in_range = t >= 0 && t < vocab_total;
+  const float safe_s = fmaxf(st.s, 1e-12f);
+  const float lse = st.m + logf(safe_s);
+  float loss = ignored ? 0.f : lse - (in_range ? z_t : 0.f);
+  float ent = fmaxf(0.f, lse - st.w / safe_s);
+  if (!isfinite(loss)) loss = 0.f;
+  if (!isfinite(ent)) ent = 0.f;
+  losses[row] = loss;
+  entropies[row] = ent;
+  correct[row] = (!ignored && in_range && st.idx == static_cast<int>(t)) ? 1 : 0;
+  lse_out[row] = lse;
+}
+
+// dlogits of one shard in place: (exp(z - lse) - onehot) / denominator.
+__global__ void __launch_bounds__(512) ce_dlogits_kernel(bf16* __restrict__ logits, int64_t ld,
+                                                         const float* __restrict__ lse,
+                                                         const int64_t* __restrict__ targets,
+                                                         int vocab_shard, int64_t vocab_offset,
+                                                         float inv_den, int64_t ignore_index) {
+  const int row = blockIdx.x;
+  bf16* lrow = logits + (int64_t)row * ld;
+  const int64_t tg = targets[row];
+  const int64_t t = tg - vocab_offset;
+  const int nvec = vocab_shard / 8;
+  if (tg == ignore_index) {
+    Vec16<bf16> zero;
+    zero.u = make_uint4(0, 0, 0, 0);
+    for (int i = threadIdx.x; i < nvec; i += blockDim.x) st16(lrow + i * 8, zero);
+    for (int c = nvec * 8 + threadIdx.x; c < vocab_shard; c += blockDim.x)
+      lrow[c] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  const float lb = lse[row] * kLog2e;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    Vec16<bf16> z = ld16(lrow + i * 8);
+    Vec16<bf16> o;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float p = fast_exp2(fmaf(__bfloat162float(z.v[j]), kLog2e, -lb));
+      if (i * 8 + j == t) p -= 1.f;
+      o.v[j] = __float2bfloat16_rn(p * inv_den);
+    }
+    st16(lrow + i * 8, o);
+  }
+  for (int c = nvec * 8 + threadIdx.x; c < vocab_shard; c += blockDim.x) {
+    float p = fast_exp2(fmaf(__bfloat162float(lrow[c]), kLog2e, -lb));
+    if (c == t) p -= 1.f;
+    lrow[c] = __float2bfloat16_rn(p * inv_den);
   }
 }
 
@@ -480,6 +578,40 @@ static CEWorkspace ce_layout(int64_t rows, int64_t vocab, int64_t dim) {
   off = align_up(off + (size_t)w.splits * rows * dim * 4, 256);
   w.total = off;
   return w;
+}
+
+// dH[M, D] = dL W: A = dlogits K-major, B = W MN-major. With `splits` > 1 the
+// vocabulary is split into fp32 slices reduced in a fixed order; otherwise the
+// GEMM epilogue writes dH directly. dh_dtype: SOUP_BF16 or SOUP_F32.
+static int dx_gemm(const bf16* L, int64_t ld_logits, const void* weight, int64_t w_ld, int M, int V,
+                   int D, int splits, float* splitk, void* dh, int dh_dtype, cudaStream_t stream,
+                   int gemm_stage = -1) {
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_operand_map(&ma, L, false, M, V, ld_logits, BM))) return rc;
+  if ((rc = make_operand_map(&mb, weight, true, D, V, w_ld, 64))) return rc;
+  Sched sc{(M + BM - 1) / BM, (D + kBN - 1) / kBN, splits, (V + BK - 1) / BK, 1};
+  const bool bf = dh_dtype == SOUP_BF16;
+  if (splits == 1) {
+    EpiStore<kBN>::Params ep{dh, D, 0, nullptr, 1.f, bf ? 1 : 0, 0,
+                             (aligned16(dh) && (D * (bf ? 2 : 4)) % 16 == 0) ? 1 : 0, M, D};
+    rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, sc, ep, stream);
+    if (!rc && gemm_stage >= 0) mark_stage(gemm_stage, stream);
+    return rc;
+  }
+  EpiStore<kBN>::Params ep{splitk, D, (int64_t)M * D, nullptr, 1.f, 0, 0, 1, M, D};
+  if ((rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, sc, ep, stream))) return rc;
+  if (gemm_stage >= 0) mark_stage(gemm_stage, stream);
+  const int64_t n4 = (int64_t)M * D / 4;
+  int blocks = static_cast<int>((n4 + 255) / 256);
+  if (blocks > 4 * num_sms()) blocks = 4 * num_sms();
+  if (bf)
+    splitk_reduce_kernel<bf16><<<blocks, 256, 0, stream>>>(splitk, splits, (int64_t)M * D, M, D,
+                                                          static_cast<bf16*>(dh), D);
+  else
+    splitk_reduce_kernel<float><<<blocks, 256, 0, stream>>>(splitk, splits, (int64_t)M * D, M, D,
+                                                           static_cast<float*>(dh), D);
+  return launch_status();
 }
 
 // dW[V, D] (+)= scale * dL^T H: A = dlogits read MN-major, B = hidden MN-major.
@@ -554,7 +686,7 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
     if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
     if ((rc = make_operand_map(&mb, weight, false, vocab, dim, w_ld, kBN))) return rc;
     Sched sc{(M + BM - 1) / BM, w.n_vtiles, 1, (D + BK - 1) / BK, 0};
-    EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, M, V};
+    EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, 0, M, V};
     if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, sc, ep, stream))) return rc;
     mark_stage(0, stream);
   }
@@ -574,19 +706,9 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   }
   // 4. dH = dL W  (split along the vocab)
   if (dhidden) {
-    CUtensorMap ma, mb;
-    if ((rc = make_operand_map(&ma, L, false, rows, vocab, w.ld_logits, BM))) return rc;
-    if ((rc = make_operand_map(&mb, weight, true, dim, vocab, w_ld, 64))) return rc;
-    Sched sc{(M + BM - 1) / BM, (D + kBN - 1) / kBN, w.splits, (V + BK - 1) / BK, 1};
-    EpiStore<kBN>::Params ep{splitk, dim, (int64_t)rows * dim, nullptr, 1.f, 0, 0, 1, M, D};
-    if ((rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, sc, ep, stream))) return rc;
-    mark_stage(3, stream);
-    const int64_t n4 = (int64_t)rows * dim / 4;
-    int blocks = static_cast<int>((n4 + 255) / 256);
-    if (blocks > 4 * num_sms()) blocks = 4 * num_sms();
-    splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(splitk, w.splits, (int64_t)rows * dim, M, D,
-                                                    static_cast<bf16*>(dhidden), dim);
-    if ((rc = launch_status())) return rc;
+    if ((rc = dx_gemm(L, w.ld_logits, weight, w_ld, M, V, D, w.splits, splitk, dhidden, SOUP_BF16,
+                      stream, 3)))
+      return rc;
     mark_stage(4, stream);
   }
   // 5. dW = dL^T H
@@ -625,6 +747,114 @@ int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const 
   return dweight_gemm(L, w.ld_logits, hidden, h_ld, static_cast<int>(rows), static_cast<int>(vocab),
                       static_cast<int>(dim), grad_scale, dweight, dw_dtype, accumulate_dw,
                       as_stream(stream));
+}
+
+// ------------------------------------------------------ vocab-parallel CE --
+size_t soup_ce_vp_workspace_bytes(int64_t rows, int64_t vocab_shard, int64_t dim) {
+  if (rows <= 0 || vocab_shard <= 0 || dim <= 0) return 0;
+  return ce_layout(rows, vocab_shard, dim).total;
+}
+
+int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shard, int64_t w_ld,
+                       const int64_t* targets, int64_t rows, int64_t vocab_shard,
+                       int64_t vocab_offset, int64_t dim, float* states, void* workspace,
+                       size_t workspace_bytes, void* stream_) {
+  if (!hidden || !weight_shard || !targets || !states || !workspace || rows <= 0 ||
+      vocab_shard <= 0 || dim <= 0 || rows > (1 << 30) || vocab_shard > (1 << 30) ||
+      vocab_offset < 0 || h_ld < dim || w_ld < dim) {
+    set_last_error("soup_ce_vp_forward: bad arguments");
+    return SOUP_ERR_INVALID;
+  }
+  if (!tma_ok(hidden, h_ld) || !tma_ok(weight_shard, w_ld) || (dim % 8) != 0) {
+    set_last_error("soup_ce_vp_forward: hidden/weight need 16-byte aligned rows and dim % 8 == 0");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  CEWorkspace w = ce_layout(rows, vocab_shard, dim);
+  if (workspace_bytes < w.total || !aligned16(workspace)) {
+    set_last_error("soup_ce_vp_forward: workspace too small or misaligned");
+    return SOUP_ERR_WORKSPACE;
+  }
+  cudaStream_t stream = as_stream(stream_);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  bf16* L = reinterpret_cast<bf16*>(ws + w.off_logits);
+  float4* partials = reinterpret_cast<float4*>(ws + w.off_partials);
+  float* zt = reinterpret_cast<float*>(ws + w.off_zt);
+  const int M = static_cast<int>(rows), V = static_cast<int>(vocab_shard), D = static_cast<int>(dim);
+  int rc;
+  CUtensorMap ma, mb;
+  if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
+  if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, kBN))) return rc;
+  Sched sc{(M + BM - 1) / BM, w.n_vtiles, 1, (D + BK - 1) / BK, 0};
+  EpiCE<kBN>::Params ep{targets, partials, zt, L, w.ld_logits, vocab_offset, M, V};
+  if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, sc, ep, stream))) return rc;
+  ce_shard_state_kernel<<<(M + 7) / 8, 256, 0, stream>>>(partials, w.n_vtiles, zt, targets, M, V,
+                                                         vocab_offset, states);
+  return launch_status();
+}
+
+int soup_ce_vp_combine(const float* states_all, int nranks, const int64_t* targets, int64_t rows,
+                       int64_t vocab_total, int64_t ignore_index, float* losses, float* entropies,
+                       int32_t* correct, float* lse, float* sums, void* stream_) {
+  if (!states_all || nranks <= 0 || !targets || !losses || !entropies || !correct || !lse ||
+      rows <= 0 || rows > (1 << 30) || vocab_total <= 0) {
+    set_last_error("soup_ce_vp_combine: bad arguments");
+    return SOUP_ERR_INVALID;
+  }
+  cudaStream_t stream = as_stream(stream_);
+  const int M = static_cast<int>(rows);
+  ce_combine_kernel<<<(M + 255) / 256, 256, 0, stream>>>(states_all, nranks, (int64_t)M * 5, targets,
+                                                         M, vocab_total, ignore_index, losses,
+                                                         entropies, correct, lse);
+  int rc = launch_status();
+  if (rc || !sums) return rc;
+  ce_sums_kernel<<<1, 1024, 0, stream>>>(losses, correct, M, sums);
+  return launch_status();
+}
+
+int soup_ce_vp_backward(void* workspace, size_t workspace_bytes, const void* hidden, int64_t h_ld,
+                        const void* weight_shard, int64_t w_ld, const int64_t* targets,
+                        int64_t rows, int64_t vocab_shard, int64_t vocab_offset, int64_t dim,
+                        const float* lse, float denominator, int64_t ignore_index,
+                        void* dhidden_partial, int dh_dtype, void* dweight_shard, int dw_dtype,
+                        int accumulate_dw, void* stream_) {
+  if (!workspace || !hidden || !weight_shard || !targets || !lse || rows <= 0 ||
+      vocab_shard <= 0 || dim <= 0 || rows > (1 << 30) || vocab_shard > (1 << 30) ||
+      h_ld < dim || w_ld < dim) {
+    set_last_error("soup_ce_vp_backward: bad arguments");
+    return SOUP_ERR_INVALID;
+  }
+  if ((dhidden_partial && dh_dtype != SOUP_F32 && dh_dtype != SOUP_BF16) ||
+      (dweight_shard && dw_dtype != SOUP_F32 && dw_dtype != SOUP_BF16)) {
+    set_last_error("soup_ce_vp_backward: gradient dtypes must be F32 or BF16");
+    return SOUP_ERR_INVALID;
+  }
+  if (!tma_ok(hidden, h_ld) || !tma_ok(weight_shard, w_ld) || (dim % 8) != 0) {
+    set_last_error("soup_ce_vp_backward: hidden/weight need 16-byte aligned rows and dim % 8 == 0");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  CEWorkspace w = ce_layout(rows, vocab_shard, dim);
+  if (workspace_bytes < w.total || !aligned16(workspace)) {
+    set_last_error("soup_ce_vp_backward: workspace too small or misaligned");
+    return SOUP_ERR_WORKSPACE;
+  }
+  cudaStream_t stream = as_stream(stream_);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  bf16* L = reinterpret_cast<bf16*>(ws + w.off_logits);
+  float* splitk = reinterpret_cast<float*>(ws + w.off_splitk);
+  const int M = static_cast<int>(rows), V = static_cast<int>(vocab_shard), D = static_cast<int>(dim);
+  const float den = denominator > 0.f ? denominator : 1.f;
+  ce_dlogits_kernel<<<M, 512, 0, stream>>>(L, w.ld_logits, lse, targets, V, vocab_offset, 1.f / den,
+                                           ignore_index);
+  int rc = launch_status();
+  if (rc) return rc;
+  if (dhidden_partial &&
+      (rc = dx_gemm(L, w.ld_logits, weight_shard, w_ld, M, V, D, w.splits, splitk, dhidden_partial,
+                    dh_dtype, stream)))
+    return rc;
+  if (dweight_shard)
+    return dweight_gemm(L, w.ld_logits, hidden, h_ld, M, V, D, nullptr, dweight_shard, dw_dtype,
+                        accumulate_dw, stream);
+  return SOUP_OK;
 }
 
 int soup_set_stage_events(void** events, int n) {

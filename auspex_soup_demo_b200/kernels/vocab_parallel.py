@@ -1,0 +1,136 @@
+"""Vocab-parallel fused head cross-entropy (lm_head rows sharded over GPUs).
+
+No counterpart in the reference, which runs on one GPU. Rank r holds rows
+``[offset_r, offset_r + V_r)`` of the [V, D] head weight and every token's
+hidden state. Per step:
+
+1. ``soup_ce_vp_forward``: tcgen05 logits GEMM over the shard with the
+   online-softmax epilogue -> one record per token (max, sum exp, sum z*exp,
+   global argmax, target logit or 0);
+2. one NCCL all-gather of the records (rows x 20 bytes per rank);
+3. ``soup_ce_vp_combine``: merge the ranks' records in rank order -> loss,
+   entropy, hit, global lse (identical on every rank);
+4. ``soup_ce_vp_backward``: the shard's dlogits from the global lse, the
+   rank's partial dhidden and its dW shard (local);
+5. one NCCL all-reduce (sum) of the partial dhidden.
+
+Row semantics match the single-GPU path (reference ``chunked_ce.py:46-128``).
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import _lib
+from .chunked_ce import IGNORE_INDEX, _tma_rows_ok
+
+
+def shard_range(vocab: int, rank: int, world: int):
+    """(offset, size) of rank's contiguous vocabulary shard; sizes differ by at most 1."""
+    base, rem = divmod(vocab, world)
+    size = base + (1 if rank < rem else 0)
+    offset = rank * base + min(rank, rem)
+    return offset, size
+
+
+class ShardState:
+    """Workspace and inputs one rank keeps between its forward and backward stages."""
+
+    def __init__(self, hidden, weight_shard, targets, offset, ws):
+        self.hidden = hidden
+        self.weight_shard = weight_shard
+        self.targets = targets
+        self.offset = offset
+        self.ws = ws
+
+
+def _prep(hidden, weight_shard, targets):
+    h = hidden.detach()
+    if h.dtype != torch.bfloat16 or not _tma_rows_ok(h):
+        h = h.to(torch.bfloat16).contiguous()
+    w = weight_shard.detach()
+    if w.dtype != torch.bfloat16 or not _tma_rows_ok(w):
+        w = w.to(torch.bfloat16).contiguous()
+    t = targets.reshape(-1)
+    if t.dtype != torch.int64 or not t.is_contiguous():
+        t = t.to(torch.int64).contiguous()
+    return h, w, t
+
+
+def vp_forward_shard(hidden, weight_shard, targets, offset: int, workspace: Optional[torch.Tensor] = None):
+    """Stage 1 on one rank: returns (records [rows, 5] fp32, ShardState)."""
+    h, w, t = _prep(hidden, weight_shard, targets)
+    n, d = h.shape
+    v = w.shape[0]
+    nbytes = _lib.lib().soup_ce_vp_workspace_bytes(n, v, d)
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=h.device)
+    states = torch.empty(n, 5, dtype=torch.float32, device=h.device)
+    _lib.call("soup_ce_vp_forward", h.device, h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
+              t.data_ptr(), n, v, int(offset), d, states.data_ptr(), workspace.data_ptr(),
+              workspace.numel(), _lib.stream_of(h))
+    return states, ShardState(h, w, t, int(offset), workspace)
+
+
+def vp_combine(states_all: torch.Tensor, targets: torch.Tensor, vocab_total: int,
+               ignore_index: int = IGNORE_INDEX):
+    """Stage 3: states_all [nranks, rows, 5] -> (losses, entropies, correct, lse, sums)."""
+    nranks, n, _ = states_all.shape
+    sa = states_all.contiguous()
+    t = targets.reshape(-1).to(torch.int64).contiguous()
+    dev = sa.device
+    losses = torch.empty(n, dtype=torch.float32, device=dev)
+    ents = torch.empty(n, dtype=torch.float32, device=dev)
+    corr = torch.empty(n, dtype=torch.int32, device=dev)
+    lse = torch.empty(n, dtype=torch.float32, device=dev)
+    sums = torch.empty(2, dtype=torch.float32, device=dev)
+    _lib.call("soup_ce_vp_combine", dev, sa.data_ptr(), nranks, t.data_ptr(), n, int(vocab_total),
+              int(ignore_index), losses.data_ptr(), ents.data_ptr(), corr.data_ptr(), lse.data_ptr(),
+              sums.data_ptr(), _lib.stream_of(sa))
+    return losses, ents, corr, lse, sums
+
+
+def vp_backward_shard(state: ShardState, lse: torch.Tensor, denominator: float,
+                      ignore_index: int = IGNORE_INDEX, dh_dtype=torch.float32,
+                      compute_dw: bool = True, dw_dtype=torch.bfloat16):
+    """Stage 4 on one rank: returns (partial dhidden [rows, D], dW shard [V_r, D] | None)."""
+    h, w = state.hidden, state.weight_shard
+    n, d = h.shape
+    v = w.shape[0]
+    dh = torch.empty(n, d, dtype=dh_dtype, device=h.device)
+    dw = torch.empty(v, d, dtype=dw_dtype, device=h.device) if compute_dw else None
+    _lib.call("soup_ce_vp_backward", h.device, state.ws.data_ptr(), state.ws.numel(), h.data_ptr(),
+              h.stride(0), w.data_ptr(), w.stride(0), state.targets.data_ptr(), n, v, state.offset, d,
+              lse.data_ptr(), float(denominator), int(ignore_index), dh.data_ptr(),
+              _lib.dtype_code(dh_dtype), _lib.ptr(dw), _lib.dtype_code(dw_dtype), 0,
+              _lib.stream_of(h))
+    return dh, dw
+
+
+def vocab_parallel_cross_entropy(hidden: torch.Tensor, weight_shard: torch.Tensor, vocab_offset: int,
+                                 vocab_total: int, targets: torch.Tensor, denominator: float = 1.0,
+                                 ignore_index: int = IGNORE_INDEX, group=None, with_grad: bool = True,
+                                 compute_dw: bool = True, workspace: Optional[torch.Tensor] = None):
+    """All stages on this rank with NCCL collectives over `group`.
+
+    Returns ``(losses, entropies, correct, sums, dhidden fp32 | None, dW shard | None)``;
+    dhidden is summed over ranks (identical everywhere), dW covers this rank's rows.
+    """
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    states, st = vp_forward_shard(hidden, weight_shard, targets, vocab_offset, workspace)
+    if world > 1:
+        states_all = torch.empty(world, *states.shape, dtype=states.dtype, device=states.device)
+        dist.all_gather_into_tensor(states_all, states, group=group)
+    else:
+        states_all = states.unsqueeze(0)
+    losses, ents, corr, lse, sums = vp_combine(states_all, st.targets, vocab_total, ignore_index)
+    dh = dw = None
+    if with_grad:
+        dh, dw = vp_backward_shard(st, lse, denominator, ignore_index, compute_dw=compute_dw)
+        if world > 1:
+            dist.all_reduce(dh, op=dist.ReduceOp.SUM, group=group)
+    return losses, ents, corr, sums, dh, dw

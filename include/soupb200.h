@@ -151,6 +151,36 @@ int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const 
                            const float* grad_scale, void* dweight, int dw_dtype, int accumulate_dw,
                            void* stream);
 
+/* ---- Vocab-parallel fused CE (the lm_head rows sharded over ranks) -----------
+ * No counterpart in the reference (single GPU only). A rank holding rows
+ * [vocab_offset, vocab_offset + vocab_shard) of W runs:
+ *   1. soup_ce_vp_forward: logits GEMM over its shard with the online-softmax
+ *      epilogue; states[rows][5] = {max, sum exp, sum z*exp, global argmax
+ *      (int32 bits), target logit or 0}; the shard's logits stay in workspace;
+ *   2. (caller) all-gather the states of all ranks into states_all[nranks][rows][5];
+ *   3. soup_ce_vp_combine: merges the ranks' states per row in rank order
+ *      (argmax ties keep the smaller index): losses, entropies, correct, the
+ *      global lse [rows] and optional sums[2];
+ *   4. soup_ce_vp_backward: dlogits of the shard in place from the global
+ *      lse, this rank's partial dhidden = dL_shard W_shard (F32 or BF16) and
+ *      its dW_shard = dL_shard^T H (local, no exchange);
+ *   5. (caller) sum the partial dhidden over ranks (all-reduce).
+ * Same row semantics as chunked_ce.py:46-128. */
+size_t soup_ce_vp_workspace_bytes(int64_t rows, int64_t vocab_shard, int64_t dim);
+int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shard, int64_t w_ld,
+                       const int64_t* targets, int64_t rows, int64_t vocab_shard,
+                       int64_t vocab_offset, int64_t dim, float* states, void* workspace,
+                       size_t workspace_bytes, void* stream);
+int soup_ce_vp_combine(const float* states_all, int nranks, const int64_t* targets, int64_t rows,
+                       int64_t vocab_total, int64_t ignore_index, float* losses, float* entropies,
+                       int32_t* correct, float* lse, float* sums, void* stream);
+int soup_ce_vp_backward(void* workspace, size_t workspace_bytes, const void* hidden, int64_t h_ld,
+                        const void* weight_shard, int64_t w_ld, const int64_t* targets,
+                        int64_t rows, int64_t vocab_shard, int64_t vocab_offset, int64_t dim,
+                        const float* lse, float denominator, int64_t ignore_index,
+                        void* dhidden_partial, int dh_dtype, void* dweight_shard, int dw_dtype,
+                        int accumulate_dw, void* stream);
+
 /* Stage timing for measurement: while set (n > 0), each soup_ce_linear call on
  * this host thread records events[i] on its stream after stage i:
  * 0 logits GEMM, 1 finalize, 2 sums, 3 dX GEMM, 4 dX reduce, 5 dW GEMM

@@ -221,3 +221,41 @@ def test_autograd_function_callable_head_path():
     assert abs(float(loss) - float(ref[0])) <= 1e-4 * abs(float(ref[0]))
     assert int(corr) == int(ref[3])
     assert cosine(h.grad, ref[4]) >= 0.9999
+
+
+@pytest.mark.parametrize("world", [1, 3, 8])
+def test_vocab_parallel_ce_emulated_ranks(world):
+    """Shards processed one after another on one GPU, records combined as the
+    all-gather would, partial dhidden summed as the all-reduce would."""
+    from auspex_soup_demo_b200.kernels.vocab_parallel import (shard_range, vp_backward_shard,
+                                                              vp_combine, vp_forward_shard)
+
+    n, v, d = 384, 20011, 256  # vocab not divisible by the rank count or the tile width
+    hidden, weight, targets = _inputs(n, v, d, seed=11)
+    targets[5] = v - 1          # last vocabulary row (last shard)
+    targets[6] = 0              # first row (first shard)
+    den = float((targets != -100).sum())
+    logits = hidden.float() @ weight.float().t()
+    loss, ent, corr, grad, lse_ref = oracle.ce_rows(logits, targets, den)
+    hc, wc, tc = hidden.cuda(), weight.cuda(), targets.cuda()
+    states, shard_states = [], []
+    for r in range(world):
+        off, size = shard_range(v, r, world)
+        s, st = vp_forward_shard(hc, wc[off:off + size], tc, off)
+        states.append(s)
+        shard_states.append(st)
+    losses, ents, hits, lse, sums = vp_combine(torch.stack(states), tc, v)
+    dh = torch.zeros(n, d, device="cuda")
+    dws = []
+    for st in shard_states:
+        p, dw = vp_backward_shard(st, lse, den)
+        dh += p
+        dws.append(dw)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(losses.cpu(), loss, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(ents.cpu(), ent, rtol=2e-3, atol=2e-3)
+    torch.testing.assert_close(lse.cpu(), lse_ref, rtol=1e-5, atol=1e-5)
+    assert torch.equal(hits.cpu(), corr)
+    assert abs(float(sums[0]) - float(loss.sum())) <= 1e-4 * float(loss.sum())
+    assert cosine(dh, grad @ weight.float()) >= 0.9999
+    assert cosine(torch.cat(dws), grad.t() @ hidden.float()) >= 0.9999

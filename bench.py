@@ -577,6 +577,82 @@ def run_qlora(args):
         dist.destroy_process_group()
 
 
+def run_ce_vp(args):
+    """Vocab-parallel fused CE: 65536 tokens, W [151936, 1536] bf16 sharded over N GPUs.
+
+    Strong scaling: the whole problem (6*T*D*V = 91.77 TFLOP per step) is fixed;
+    each rank computes its vocabulary shard for all tokens. Collectives per
+    step: all-gather of per-token softmax records, all-reduce of dhidden (fp32).
+    """
+    import torch.distributed as dist
+
+    from auspex_soup_demo_b200 import _lib
+    from auspex_soup_demo_b200.kernels.vocab_parallel import shard_range, vocab_parallel_cross_entropy
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    T = args.tokens
+    g = torch.Generator(device=dev).manual_seed(7)  # same hidden/targets on every rank
+    hidden = torch.randn(T, DIM, device=dev, generator=g).to(torch.bfloat16)
+    targets = torch.randint(0, VOCAB, (T,), device=dev, generator=g)
+    targets[torch.rand(T, device=dev, generator=g) < 0.1] = -100
+    den = float((targets != -100).sum())
+    off, size = shard_range(VOCAB, rank, world)
+    gw = torch.Generator(device=dev).manual_seed(1000 + rank)
+    w_shard = (0.02 * torch.randn(size, DIM, device=dev, generator=gw)).to(torch.bfloat16)
+    ws = torch.empty(_lib.lib().soup_ce_vp_workspace_bytes(T, size, DIM), dtype=torch.uint8,
+                     device=dev)
+
+    def step():
+        return vocab_parallel_cross_entropy(hidden, w_shard, off, VOCAB, targets, den,
+                                            workspace=ws)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(local) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            out = step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t)
+    flop = 6.0 * T * DIM * VOCAB
+    assert _lib.device_error(dev) == 0
+    line = {"metric": "vocab-parallel fused-CE TFLOP/s (fwd+bwd)", "value": round(flop / (ms * 1e-3) / 1e12, 2),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"vocab-parallel CE, {T} tokens, W [151936,1536] bf16 "
+                                   f"sharded {world} ways ({size} rows on rank 0)",
+                       "collectives": "all_gather of per-token records + all_reduce(sum) of fp32 dhidden",
+                       "l2": "inputs larger than L2"},
+            "loss": float(out[3][0]) / den, "clocks": clocks.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def _committed_traffic():
     """DRAM bytes per launch of the logits GEMM from the committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
@@ -600,9 +676,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", default="ce", choices=["ce", "rmsnorm", "swiglu", "rope", "qlora"],
+    ap.add_argument("--workload", default="ce",
+                    choices=["ce", "rmsnorm", "swiglu", "rope", "qlora", "ce_vp"],
                     help="ce (default): the fused head CE; rmsnorm/swiglu/rope: one memory-bound "
-                         "op's HBM GB/s; qlora: the Qwen2.5-1.5B QLoRA train step's tokens/s")
+                         "op's HBM GB/s; qlora: the Qwen2.5-1.5B QLoRA train step's tokens/s; "
+                         "ce_vp: the vocab-parallel CE over all ranks")
+    ap.add_argument("--tokens", type=int, default=65536, help="ce_vp: tokens per step")
     ap.add_argument("--batch", type=int, default=4, help="qlora: sequences per GPU")
     ap.add_argument("--seq", type=int, default=512, help="qlora: tokens per sequence")
     ap.add_argument("--layers", type=int, default=28, help="qlora: decoder layers")
@@ -612,6 +691,8 @@ def main():
         run_reference(args)
     elif args.workload == "qlora":
         run_qlora(args)
+    elif args.workload == "ce_vp":
+        run_ce_vp(args)
     elif args.workload != "ce":
         run_memory_op(args)
     else:

@@ -1,11 +1,15 @@
 // RMSNorm forward and backward (dx and dw in one pass over dy and x).
 //
-// One warp owns one row: 16-byte vector loads, the row kept in registers,
-// a warp-shuffle sum of squares. The backward accumulates dw partials per
-// lane across the rows its warp visits, reduces the CTA's 8 warps through
-// shared memory in a fixed order into one partial row per CTA, and a second
-// small kernel sums those partial rows column by column, again in a fixed
-// order: no data atomics, bitwise reproducible.
+// Vector path (16-byte aligned rows, cols a multiple of the vector width): a
+// CTA owns one row at a time (grid-stride over rows; as many CTAs as fit on
+// the GPU at once), each thread one to four 16-byte vectors of the row, the
+// next row's vectors loaded before the current row is reduced, a fixed-order
+// block reduction. The backward keeps a dw partial per thread in registers
+// across its CTA's rows and writes one partial row per CTA; a second small
+// kernel adds those rows column by column in a fixed order: no data
+// atomics, bitwise reproducible. Kernels launch with programmatic dependent
+// launch so a kernel's start overlaps the previous kernel's tail.
+// Generic path (any alignment): one warp per row, scalar accesses.
 //
 // Semantics: solution/kernels/rmsnorm.py:22-57 (forward), :60-96 (dx) and
 // :161-167 (dw, fp32, cast to the weight dtype).
@@ -14,6 +18,7 @@
 #include <utility>
 
 #include "soup_common.cuh"
+
 
 namespace soup {
 namespace {
@@ -42,124 +47,234 @@ __device__ __forceinline__ void load_w(const W* w, float (&o)[NE]) {
   }
 }
 
-// VPL = 16-byte vectors of x per lane (row length <= 32 * VPL * NE).
-template <typename T, typename W, int VPL>
-__global__ void __launch_bounds__(kWarps * 32) rms_fwd_kernel(const T* __restrict__ x, int64_t xs,
-                                                              const W* __restrict__ w,
-                                                              T* __restrict__ y, int64_t ys,
-                                                              float* __restrict__ rstd,
-                                                              int64_t rows, int cols, float eps) {
+// ---------------------------------------------------------------------------
+// Vector path: one CTA owns one row at a time (grid-stride over rows, the
+// next row's loads issued before the current row is reduced), every thread
+// one or more 16-byte vectors of the row, a fixed-order block reduction.
+// The weight row stays in registers for all the CTA's rows.
+// ---------------------------------------------------------------------------
+
+// Sum of one float per thread over the CTA, same value returned to every
+// thread; warp sums, then the warp totals added in warp order.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red[] is reused row after row
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int nw = blockDim.x >> 5;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+// Row kernels: a CTA owns one row at a time (grid-stride over rows, one CTA
+// per SM slot), each thread VPT 16-byte vectors of it, the next row's vectors
+// loaded before the current row is reduced. Few registers per thread keep
+// several CTAs (rows) in flight per SM; the weight row stays in registers.
+template <typename T, typename W, int VPT>
+__global__ void __launch_bounds__(512) rms_fwd_rows(const T* __restrict__ x, int64_t xs,
+                                                    const W* __restrict__ w, T* __restrict__ y,
+                                                    int64_t ys, float* __restrict__ rstd,
+                                                    int64_t rows, int cols, float eps) {
   constexpr int NE = Vec16<T>::N;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const T* xr = x + row * xs;
-  Vec16<T> xv[VPL];
-  float ss = 0.f;
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
+  const int nvec = cols / NE;
+  float wf[VPT][NE];
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int c = (i * 32 + lane) * NE;
-    if (c < cols) {
-      xv[i] = ld16_stream(xr + c);
+  for (int v = 0; v < VPT; ++v) {
+    const int j = threadIdx.x + v * blockDim.x;
+    if (j < nvec) load_w<W, NE>(w + j * NE, wf[v]);
+  }
+  Vec16<T> cur[VPT], nxt[VPT];
+  int64_t row = blockIdx.x;
+  if (row < rows) {
 #pragma unroll
-      for (int j = 0; j < NE; ++j) {
-        const float f = Cvt<T>::to_f(xv[i].v[j]);
-        ss = fmaf(f, f, ss);
-      }
+    for (int v = 0; v < VPT; ++v) {
+      const int j = threadIdx.x + v * blockDim.x;
+      if (j < nvec) cur[v] = ld16_stream(x + row * xs + j * NE);
     }
   }
-  ss = warp_sum(ss);
-  const float r = 1.0f / sqrtf(ss / static_cast<float>(cols) + eps);
-  if (lane == 0) rstd[row] = r;
-  T* yr = y + row * ys;
+  for (; row < rows; row += gridDim.x) {
+    const int64_t nrow = row + gridDim.x;
+    if (nrow < rows) {
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int c = (i * 32 + lane) * NE;
-    if (c < cols) {
-      float wf[NE];
-      load_w<W, NE>(w + c, wf);
-      Vec16<T> o;
-#pragma unroll
-      for (int j = 0; j < NE; ++j) o.v[j] = Cvt<T>::from_f((Cvt<T>::to_f(xv[i].v[j]) * r) * wf[j]);
-      st16_stream(yr + c, o);
+      for (int v = 0; v < VPT; ++v) {
+        const int j = threadIdx.x + v * blockDim.x;
+        if (j < nvec) nxt[v] = ld16_stream(x + nrow * xs + j * NE);
+      }
     }
+    float ss = 0.f;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int j = threadIdx.x + v * blockDim.x;
+      if (j < nvec) {
+#pragma unroll
+        for (int e = 0; e < NE; ++e) {
+          const float f = Cvt<T>::to_f(cur[v].v[e]);
+          ss = fmaf(f, f, ss);
+        }
+      }
+    }
+    ss = block_sum(ss, red);
+    const float r = 1.0f / sqrtf(ss / static_cast<float>(cols) + eps);
+    if (threadIdx.x == 0) rstd[row] = r;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int j = threadIdx.x + v * blockDim.x;
+      if (j < nvec) {
+        Vec16<T> o;
+#pragma unroll
+        for (int e = 0; e < NE; ++e) o.v[e] = Cvt<T>::from_f((Cvt<T>::to_f(cur[v].v[e]) * r) * wf[v][e]);
+        st16_stream(y + row * ys + j * NE, o);
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) cur[v] = nxt[v];
   }
 }
 
-// dx for every row; per-CTA dw partial row into `partial` (if non-null).
-template <typename T, typename W, int VPL>
-__global__ void __launch_bounds__(kWarps * 32) rms_bwd_kernel(
+// dx for the CTA's rows; with partial != nullptr the CTA's dw partial
+// (registers, fixed row order) is written as partial[blockIdx.x][cols].
+template <typename T, typename W, int VPT, bool DW>
+__global__ void __launch_bounds__(512) rms_bwd_rows(
     const T* __restrict__ dy, int64_t dys, const T* __restrict__ x, int64_t xs,
     const W* __restrict__ w, const float* __restrict__ rstd, T* __restrict__ dx, int64_t dxs,
     float* __restrict__ partial, int64_t rows, int cols) {
   constexpr int NE = Vec16<T>::N;
-  extern __shared__ float red[];  // [kWarps][cols] when partial != nullptr
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  float acc[VPL][NE];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i)
-#pragma unroll
-    for (int j = 0; j < NE; ++j) acc[i][j] = 0.f;
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
+  const int nvec = cols / NE;
   const float inv_cols = 1.0f / static_cast<float>(cols);
-
-  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows;
-       row += (int64_t)gridDim.x * kWarps) {
-    const T* dyr = dy + row * dys;
-    const T* xr = x + row * xs;
-    Vec16<T> dv[VPL], xv[VPL];
+  float wf[VPT][NE], acc[VPT][NE];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int j = threadIdx.x + v * blockDim.x;
+#pragma unroll
+    for (int e = 0; e < NE; ++e) acc[v][e] = 0.f;
+    if (j < nvec) load_w<W, NE>(w + j * NE, wf[v]);
+  }
+  Vec16<T> cd[VPT], cx[VPT], nd[VPT], nx[VPT];
+  int64_t row = blockIdx.x;
+  if (row < rows) {
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int j = threadIdx.x + v * blockDim.x;
+      if (j < nvec) {
+        cd[v] = ld16_stream(dy + row * dys + j * NE);
+        cx[v] = ld16_stream(x + row * xs + j * NE);
+      }
+    }
+  }
+  for (; row < rows; row += gridDim.x) {
+    const int64_t nrow = row + gridDim.x;
+    if (nrow < rows) {
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int j = threadIdx.x + v * blockDim.x;
+        if (j < nvec) {
+          nd[v] = ld16_stream(dy + nrow * dys + j * NE);
+          nx[v] = ld16_stream(x + nrow * xs + j * NE);
+        }
+      }
+    }
+    const float r = rstd[row];
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int c = (i * 32 + lane) * NE;
-      if (c < cols) {
-        dv[i] = ld16_stream(dyr + c);
-        xv[i] = ld16_stream(xr + c);
-        float wf[NE];
-        load_w<W, NE>(w + c, wf);
+    for (int v = 0; v < VPT; ++v) {
+      const int j = threadIdx.x + v * blockDim.x;
+      if (j < nvec) {
 #pragma unroll
-        for (int j = 0; j < NE; ++j)
-          s = fmaf(Cvt<T>::to_f(dv[i].v[j]) * wf[j], Cvt<T>::to_f(xv[i].v[j]), s);
+        for (int e = 0; e < NE; ++e)
+          s = fmaf(Cvt<T>::to_f(cd[v].v[e]) * wf[v][e], Cvt<T>::to_f(cx[v].v[e]), s);
       }
     }
-    s = warp_sum(s);
-    const float r = rstd[row];
+    s = block_sum(s, red);
     const float k = r * r * s * inv_cols;
-    T* dxr = dx + row * dxs;
 #pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int c = (i * 32 + lane) * NE;
-      if (c < cols) {
-        float wf[NE];
-        load_w<W, NE>(w + c, wf);
+    for (int v = 0; v < VPT; ++v) {
+      const int j = threadIdx.x + v * blockDim.x;
+      if (j < nvec) {
         Vec16<T> o;
 #pragma unroll
-        for (int j = 0; j < NE; ++j) {
-          const float d = Cvt<T>::to_f(dv[i].v[j]);
-          const float xx = Cvt<T>::to_f(xv[i].v[j]);
-          o.v[j] = Cvt<T>::from_f(r * (d * wf[j] - xx * k));
-          acc[i][j] = fmaf(d, xx * r, acc[i][j]);
+        for (int e = 0; e < NE; ++e) {
+          const float d = Cvt<T>::to_f(cd[v].v[e]);
+          const float xx = Cvt<T>::to_f(cx[v].v[e]);
+          o.v[e] = Cvt<T>::from_f(r * (d * wf[v][e] - xx * k));
+          if (DW) acc[v][e] = fmaf(d, xx * r, acc[v][e]);
         }
-        st16_stream(dxr + c, o);
+        st16_stream(dx + row * dxs + j * NE, o);
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      cd[v] = nd[v];
+      cx[v] = nx[v];
+    }
+  }
+  if constexpr (DW) {
+    float* dst = partial + (int64_t)blockIdx.x * cols;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int j = threadIdx.x + v * blockDim.x;
+      if (j < nvec) {
+#pragma unroll
+        for (int q = 0; q < NE; q += 4)
+          *reinterpret_cast<float4*>(dst + j * NE + q) =
+              make_float4(acc[v][q], acc[v][q + 1], acc[v][q + 2], acc[v][q + 3]);
       }
     }
   }
-  if (partial == nullptr) return;
-  // CTA reduction of the 8 warps' dw partials, fixed order.
+}
+
+// dw[c] = sum of the partial rows, fixed order: lanes own 4 columns (float4),
+// the 32 warps of the CTA split the rows (warp w takes rows w, w+32, ...,
+// eight of them in flight per lane), then the warp totals are added in warp
+// order.
+template <typename W>
+__global__ void __launch_bounds__(1024) rms_dw_reduce_vec(const float* __restrict__ partial, int g,
+                                                          int cols, W* __restrict__ dw) {
+  __shared__ float4 red[32][32];
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = (blockIdx.x * 32 + lane) * 4;
+  float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (c < cols) {
+    for (int q0 = warp; q0 < g; q0 += 32 * 8) {
+      float4 a[8];
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int c = (i * 32 + lane) * NE;
-    if (c < cols) {
+      for (int u = 0; u < 8; ++u) {
+        const int q = q0 + 32 * u;
+        a[u] = q < g ? *reinterpret_cast<const float4*>(partial + (int64_t)q * cols + c)
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
 #pragma unroll
-      for (int j = 0; j < NE; ++j) red[warp * cols + c + j] = acc[i][j];
+      for (int u = 0; u < 8; ++u) {
+        t.x += a[u].x;
+        t.y += a[u].y;
+        t.z += a[u].z;
+        t.w += a[u].w;
+      }
     }
   }
+  red[warp][lane] = t;
   __syncthreads();
-  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
-    float t = 0.f;
-#pragma unroll
-    for (int q = 0; q < kWarps; ++q) t += red[q * cols + c];
-    partial[(int64_t)blockIdx.x * cols + c] = t;
+  if (warp == 0 && c < cols) {
+    float4 s = red[0][lane];
+    for (int i = 1; i < 32; ++i) {
+      s.x += red[i][lane].x;
+      s.y += red[i][lane].y;
+      s.z += red[i][lane].z;
+      s.w += red[i][lane].w;
+    }
+    dw[c] = Cvt<W>::from_f(s.x);
+    dw[c + 1] = Cvt<W>::from_f(s.y);
+    dw[c + 2] = Cvt<W>::from_f(s.z);
+    dw[c + 3] = Cvt<W>::from_f(s.w);
   }
 }
 
@@ -169,6 +284,8 @@ template <typename W>
 __global__ void __launch_bounds__(256) rms_dw_reduce_kernel(const float* __restrict__ partial, int g,
                                                             int cols, W* __restrict__ dw) {
   __shared__ float red[8][33];
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
   float t = 0.f;
@@ -240,14 +357,22 @@ __global__ void __launch_bounds__(kWarps * 32) rms_bwd_generic(
 }
 
 // ----------------------------------------------------------- dispatch ------
+// Vectors per thread for the row kernels: the smallest VPT in {1, 2, 4}
+// that keeps the CTA at <= 512 threads; 0 (generic path) when the row is
+// longer than 2048 vectors.
 template <typename T>
-int vpl_for(int64_t cols) {
-  const int64_t per = 32 * Vec16<T>::N;
-  const int64_t need = (cols + per - 1) / per;
-  const int opts[] = {1, 2, 4, 6, 8, 12, 16};
-  for (int o : opts)
-    if (need <= o) return o;
+int vpt_for(int64_t cols) {
+  const int64_t nvec = cols / Vec16<T>::N;
+  for (int v : {1, 2, 4})
+    if ((nvec + v - 1) / v <= 512) return v;
   return 0;
+}
+
+template <typename T>
+int row_threads(int64_t cols, int vpt) {
+  const int64_t nvec = cols / Vec16<T>::N;
+  const int64_t t = (nvec + vpt - 1) / vpt;
+  return static_cast<int>((t + 31) / 32 * 32);
 }
 
 template <typename T, typename W>
@@ -256,7 +381,43 @@ bool vec_ok(int64_t cols, std::initializer_list<std::pair<const void*, int64_t>>
   if (!aligned16(w)) return false;
   for (auto& m : mats)
     if (!aligned16(m.first) || ((m.second * (int64_t)sizeof(T)) % 16) != 0) return false;
-  return vpl_for<T>(cols) > 0;
+  return vpt_for<T>(cols) > 0;
+}
+
+// Resident CTAs per SM of a kernel at this block size / shared memory (cached).
+template <typename K>
+int ctas_per_sm(K kernel, int threads, size_t smem) {
+  struct Entry {
+    const void* k;
+    int threads;
+    size_t smem;
+    int dev;
+    int n;
+  };
+  static Entry cache[64];
+  static int used = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].k == (const void*)kernel && cache[i].threads == threads && cache[i].smem == smem &&
+        cache[i].dev == dev)
+      return cache[i].n;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess || n < 1)
+    n = 1;
+  if (used < 64) cache[used++] = Entry{(const void*)kernel, threads, smem, dev, n};
+  return n;
+}
+
+template <typename T, typename W, int VPT>
+int fwd_rows_launch(const T* X, int64_t xs, const W* Wt, T* Y, int64_t ys, float* rstd, int64_t rows,
+                    int cols, float eps, cudaStream_t st) {
+  const int threads = row_threads<T>(cols, VPT);
+  auto k = rms_fwd_rows<T, W, VPT>;
+  const int64_t cap = (int64_t)num_sms() * ctas_per_sm(k, threads, 0);
+  const int grid = static_cast<int>(rows < cap ? rows : cap);
+  return cuda_status(launch_pdl(k, dim3(grid), dim3(threads), 0, st, X, xs, Wt, Y, ys, rstd, rows,
+                                cols, eps));
 }
 
 template <typename T, typename W>
@@ -265,38 +426,82 @@ int fwd_impl(const void* x, int64_t xs, const void* w, void* y, int64_t ys, floa
   const T* X = static_cast<const T*>(x);
   const W* Wt = static_cast<const W*>(w);
   T* Y = static_cast<T*>(y);
-  const unsigned grid = static_cast<unsigned>((rows + kWarps - 1) / kWarps);
   if (vec_ok<T, W>(cols, {{x, xs}, {y, ys}}, w)) {
-    switch (vpl_for<T>(cols)) {
-#define SOUP_RMS_F(V)                                                                     \
-  case V:                                                                                 \
-    rms_fwd_kernel<T, W, V><<<grid, kWarps * 32, 0, st>>>(X, xs, Wt, Y, ys, rstd, rows,   \
-                                                          (int)cols, eps);                \
-    break;
-      SOUP_RMS_F(1) SOUP_RMS_F(2) SOUP_RMS_F(4) SOUP_RMS_F(6) SOUP_RMS_F(8) SOUP_RMS_F(12)
-      SOUP_RMS_F(16)
-#undef SOUP_RMS_F
+    switch (vpt_for<T>(cols)) {
+      case 1: return fwd_rows_launch<T, W, 1>(X, xs, Wt, Y, ys, rstd, rows, (int)cols, eps, st);
+      case 2: return fwd_rows_launch<T, W, 2>(X, xs, Wt, Y, ys, rstd, rows, (int)cols, eps, st);
+      default: return fwd_rows_launch<T, W, 4>(X, xs, Wt, Y, ys, rstd, rows, (int)cols, eps, st);
     }
-  } else {
-    rms_fwd_generic<T, W><<<grid, kWarps * 32, 0, st>>>(X, xs, Wt, Y, ys, rstd, rows, (int)cols, eps);
   }
+  const unsigned grid = static_cast<unsigned>((rows + kWarps - 1) / kWarps);
+  rms_fwd_generic<T, W><<<grid, kWarps * 32, 0, st>>>(X, xs, Wt, Y, ys, rstd, rows, (int)cols, eps);
   return launch_status();
 }
 
-// Number of CTAs of the backward (and of dw partial rows).
+// Grid of the generic backward (one dw partial row per warp).
 int bwd_grid(int64_t rows) {
   int64_t g = (rows + kWarps - 1) / kWarps;
   const int64_t cap = num_sms();
   return static_cast<int>(g < cap ? g : cap);
 }
 
+// Grid of the vector backward with dw: at most 3 CTAs per SM (bounds the
+// partial rows: at most 3 x #SMs rows of cols floats).
+template <typename T, typename W, int VPT>
+int bwd_rows_grid(int64_t rows, int cols) {
+  const int threads = row_threads<T>(cols, VPT);
+  auto k = rms_bwd_rows<T, W, VPT, true>;
+  int per_sm = ctas_per_sm(k, threads, 0);
+  if (per_sm > 3) per_sm = 3;
+  const int64_t cap = (int64_t)num_sms() * per_sm;
+  return static_cast<int>(rows < cap ? rows : cap);
+}
+
+template <typename T, typename W, int VPT>
+int bwd_rows_launch(const T* DY, int64_t dys, const T* X, int64_t xs, const W* Wt, const float* rstd,
+                    T* DX, int64_t dxs, W* dw, void* ws, size_t ws_bytes, int64_t rows, int cols,
+                    cudaStream_t st) {
+  const int threads = row_threads<T>(cols, VPT);
+  if (!dw) {
+    auto k = rms_bwd_rows<T, W, VPT, false>;
+    const int64_t cap = (int64_t)num_sms() * ctas_per_sm(k, threads, 0);
+    const int grid = static_cast<int>(rows < cap ? rows : cap);
+    return cuda_status(launch_pdl(k, dim3(grid), dim3(threads), 0, st, DY, dys, X, xs, Wt, rstd, DX,
+                                  dxs, static_cast<float*>(nullptr), rows, cols));
+  }
+  const int grid = bwd_rows_grid<T, W, VPT>(rows, cols);
+  if (!ws || ws_bytes < (size_t)grid * cols * sizeof(float) || !aligned16(ws)) {
+    set_last_error("soup_rmsnorm_bwd: workspace too small");
+    return SOUP_ERR_WORKSPACE;
+  }
+  float* partial = static_cast<float*>(ws);
+  int rc = cuda_status(launch_pdl(rms_bwd_rows<T, W, VPT, true>, dim3(grid), dim3(threads), 0, st, DY,
+                                  dys, X, xs, Wt, rstd, DX, dxs, partial, rows, cols));
+  if (rc) return rc;
+  return cuda_status(launch_pdl(rms_dw_reduce_vec<W>, dim3((unsigned)((cols + 127) / 128)), dim3(1024),
+                                0, st, static_cast<const float*>(partial), grid, cols, dw));
+}
+
 template <typename T, typename W>
 int bwd_impl(const void* dy, int64_t dys, const void* x, int64_t xs, const void* w,
              const float* rstd, void* dx, int64_t dxs, void* dw, void* ws, size_t ws_bytes,
              int64_t rows, int64_t cols, cudaStream_t st) {
+  const T* DY = static_cast<const T*>(dy);
+  const T* X = static_cast<const T*>(x);
+  const W* Wt = static_cast<const W*>(w);
+  T* DX = static_cast<T*>(dx);
+  W* DW = static_cast<W*>(dw);
+  if (vec_ok<T, W>(cols, {{dy, dys}, {x, xs}, {dx, dxs}}, w)) {
+    const int c = static_cast<int>(cols);
+    switch (vpt_for<T>(cols)) {
+      case 1: return bwd_rows_launch<T, W, 1>(DY, dys, X, xs, Wt, rstd, DX, dxs, DW, ws, ws_bytes, rows, c, st);
+      case 2: return bwd_rows_launch<T, W, 2>(DY, dys, X, xs, Wt, rstd, DX, dxs, DW, ws, ws_bytes, rows, c, st);
+      default: return bwd_rows_launch<T, W, 4>(DY, dys, X, xs, Wt, rstd, DX, dxs, DW, ws, ws_bytes, rows, c, st);
+    }
+  }
+  // generic path: one partial row per warp
   const int grid = bwd_grid(rows);
-  const bool vec = vec_ok<T, W>(cols, {{dy, dys}, {x, xs}, {dx, dxs}}, w);
-  const int prows = vec ? grid : grid * kWarps;
+  const int prows = grid * kWarps;
   float* partial = nullptr;
   if (dw) {
     if (!ws || ws_bytes < (size_t)prows * cols * sizeof(float) || !aligned16(ws)) {
@@ -305,38 +510,26 @@ int bwd_impl(const void* dy, int64_t dys, const void* x, int64_t xs, const void*
     }
     partial = static_cast<float*>(ws);
   }
-  const T* DY = static_cast<const T*>(dy);
-  const T* X = static_cast<const T*>(x);
-  const W* Wt = static_cast<const W*>(w);
-  T* DX = static_cast<T*>(dx);
-  if (vec) {
-    const size_t smem = dw ? (size_t)kWarps * cols * sizeof(float) : 0;
-    switch (vpl_for<T>(cols)) {
-#define SOUP_RMS_B(V)                                                                         \
-  case V: {                                                                                   \
-    auto k = rms_bwd_kernel<T, W, V>;                                                         \
-    if (smem > 48 * 1024) {                                                                   \
-      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
-                                           (int)smem);                                        \
-      if (e != cudaSuccess) return cuda_status(e);                                            \
-    }                                                                                         \
-    k<<<grid, kWarps * 32, smem, st>>>(DY, dys, X, xs, Wt, rstd, DX, dxs, partial, rows,      \
-                                       (int)cols);                                            \
-    break;                                                                                    \
-  }
-      SOUP_RMS_B(1) SOUP_RMS_B(2) SOUP_RMS_B(4) SOUP_RMS_B(6) SOUP_RMS_B(8) SOUP_RMS_B(12)
-      SOUP_RMS_B(16)
-#undef SOUP_RMS_B
-    }
-  } else {
-    rms_bwd_generic<T, W><<<grid, kWarps * 32, 0, st>>>(DY, dys, X, xs, Wt, rstd, DX, dxs, partial,
-                                                        rows, (int)cols);
-  }
+  rms_bwd_generic<T, W><<<grid, kWarps * 32, 0, st>>>(DY, dys, X, xs, Wt, rstd, DX, dxs, partial,
+                                                      rows, (int)cols);
   int rc = launch_status();
   if (rc || !dw) return rc;
-  rms_dw_reduce_kernel<W><<<(unsigned)((cols + 31) / 32), 256, 0, st>>>(partial, prows, (int)cols,
-                                                                       static_cast<W*>(dw));
+  rms_dw_reduce_kernel<W><<<(unsigned)((cols + 31) / 32), 256, 0, st>>>(partial, prows, (int)cols, DW);
   return launch_status();
+}
+
+// Bytes of dw partial rows the backward writes for these operands.
+template <typename T, typename W>
+size_t bwd_partial_rows(const void* dy, int64_t dys, const void* x, int64_t xs, const void* w,
+                        const void* dx, int64_t dxs, int64_t rows, int64_t cols) {
+  if (vec_ok<T, W>(cols, {{dy, dys}, {x, xs}, {dx, dxs}}, w)) {
+    switch (vpt_for<T>(cols)) {
+      case 1: return bwd_rows_grid<T, W, 1>(rows, (int)cols);
+      case 2: return bwd_rows_grid<T, W, 2>(rows, (int)cols);
+      default: return bwd_rows_grid<T, W, 4>(rows, (int)cols);
+    }
+  }
+  return static_cast<size_t>(bwd_grid(rows)) * kWarps;
 }
 
 }  // namespace
@@ -378,7 +571,8 @@ int soup_rmsnorm_fwd(const void* x, int64_t x_row_stride, const void* weight, vo
 
 size_t soup_rmsnorm_bwd_workspace_bytes(int64_t rows, int64_t cols) {
   if (rows <= 0 || cols <= 0) return 0;
-  // generic path keeps one partial row per warp; the vector path one per CTA
+  // upper bound: the generic path keeps one partial row per warp; the vector
+  // path one per CTA (at most 3 per SM)
   return (size_t)bwd_grid(rows) * kWarps * (size_t)cols * sizeof(float);
 }
 
@@ -449,13 +643,11 @@ float* noalloc_scratch(int* status) {
   return addr[dev];
 }
 
-// Bytes of dw partial rows the backward writes for these operands.
 template <typename T, typename W>
 size_t bwd_partial_bytes(const void* dy, int64_t dys, const void* x, int64_t xs, const void* w,
                          const void* dx, int64_t dxs, int64_t rows, int64_t cols) {
-  const bool vec = vec_ok<T, W>(cols, {{dy, dys}, {x, xs}, {dx, dxs}}, w);
-  const size_t prows = static_cast<size_t>(vec ? bwd_grid(rows) : bwd_grid(rows) * kWarps);
-  return prows * static_cast<size_t>(cols) * sizeof(float);
+  return bwd_partial_rows<T, W>(dy, dys, x, xs, w, dx, dxs, rows, cols) *
+         static_cast<size_t>(cols) * sizeof(float);
 }
 
 size_t bwd_partial_bytes_any(int xd, int wd, const void* dy, int64_t dys, const void* x,

@@ -23,63 +23,102 @@ struct RopeTensor {
   int64_t heads;
 };
 
-template <typename T, typename CT, bool VEC>
-__global__ void __launch_bounds__(256) rope_kernel(RopeTensor q, RopeTensor k, const CT* __restrict__ cos,
-                                                   const CT* __restrict__ sin, int64_t cb, int64_t cs,
-                                                   int64_t S, int64_t half, float sign) {
-  constexpr int NE = VEC ? Vec16<T>::N : 1;
-  // per-batch item counts fit in 32 bits (checked on the host)
-  const uint32_t chunks = static_cast<uint32_t>(half / NE);
-  const uint32_t S32 = static_cast<uint32_t>(S);
-  const uint32_t nq = static_cast<uint32_t>(q.heads) * S32 * chunks;
-  const uint32_t nk = static_cast<uint32_t>(k.heads) * S32 * chunks;
-  const uint32_t per_b = nq + nk;
-  const int64_t b = blockIdx.y;  // batch on grid.y
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < per_b; i += gridDim.x * blockDim.x) {
+// Vector path: CTA (blockIdx.x, blockIdx.y) covers positions
+// [blockIdx.x * P, +P) of batch blockIdx.y for every head of Q and K; thread
+// slot i = (head, 16-byte chunk) is fixed, so addresses are computed once and
+// the loads of all P positions are in flight together.
+template <typename T, typename CT, int P>
+__global__ void __launch_bounds__(256) rope_rows_kernel(RopeTensor q, RopeTensor k,
+                                                        const CT* __restrict__ cos,
+                                                        const CT* __restrict__ sin, int64_t cb,
+                                                        int64_t cs, int S, int half, float sign) {
+  constexpr int NE = Vec16<T>::N;
+  pdl_wait();
+  pdl_trigger();
+  const int chunks = half / NE;
+  const int slots = static_cast<int>(q.heads + k.heads) * chunks;
+  const int64_t b = blockIdx.y;
+  const int s0 = blockIdx.x * P;
+  for (int i = threadIdx.x; i < slots; i += blockDim.x) {
+    const int h = i / chunks;
+    const int d = (i - h * chunks) * NE;
+    const bool isq = h < q.heads;
+    const RopeTensor& t = isq ? q : k;
+    const int64_t hh = isq ? h : h - q.heads;
+    const T* xb = static_cast<const T*>(t.x) + b * t.sb + hh * t.sh + d;
+    T* ob = static_cast<T*>(t.out) + b * t.ob + hh * t.oh + d;
+    const CT* cbp = cos + b * cb + d;
+    const CT* sbp = sin + b * cb + d;
+    Vec16<T> x1[P], x2[P];
+    float c[P][NE], sn[P][NE];
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const int s = s0 + p;
+      if (s < S) {
+        x1[p] = ld16_stream(xb + s * t.ss);
+        x2[p] = ld16_stream(xb + s * t.ss + half);
+        if constexpr (sizeof(CT) == sizeof(T)) {
+          Vec16<CT> cv = ld16(cbp + s * cs), sv = ld16(sbp + s * cs);
+#pragma unroll
+          for (int e = 0; e < NE; ++e) {
+            c[p][e] = Cvt<CT>::to_f(cv.v[e]);
+            sn[p][e] = sign * Cvt<CT>::to_f(sv.v[e]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < NE; ++e) {
+            c[p][e] = Cvt<CT>::to_f(cbp[s * cs + e]);
+            sn[p][e] = sign * Cvt<CT>::to_f(sbp[s * cs + e]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < P; ++p) {
+      const int s = s0 + p;
+      if (s < S) {
+        Vec16<T> y1, y2;
+#pragma unroll
+        for (int e = 0; e < NE; ++e) {
+          const float a = Cvt<T>::to_f(x1[p].v[e]), bb = Cvt<T>::to_f(x2[p].v[e]);
+          y1.v[e] = Cvt<T>::from_f(a * c[p][e] - bb * sn[p][e]);
+          y2.v[e] = Cvt<T>::from_f(a * sn[p][e] + bb * c[p][e]);
+        }
+        st16_stream(ob + s * t.os, y1);
+        st16_stream(ob + s * t.os + half, y2);
+      }
+    }
+  }
+}
+
+// Scalar path (any alignment): one pair per thread-iteration.
+template <typename T, typename CT>
+__global__ void __launch_bounds__(256) rope_scalar_kernel(RopeTensor q, RopeTensor k,
+                                                          const CT* __restrict__ cos,
+                                                          const CT* __restrict__ sin, int64_t cb,
+                                                          int64_t cs, int64_t S, int64_t half,
+                                                          float sign) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t nq = q.heads * S * half;
+  const int64_t per_b = nq + k.heads * S * half;
+  const int64_t b = blockIdx.y;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < per_b;
+       i += (int64_t)gridDim.x * blockDim.x) {
     const bool isq = i < nq;
     const RopeTensor& t = isq ? q : k;
-    uint32_t j = isq ? i : i - nq;
-    const uint32_t ch = j % chunks;
-    j /= chunks;
-    const int64_t s = j % S32;
-    const int64_t h = j / S32;
-    const int64_t d = static_cast<int64_t>(ch) * NE;
+    int64_t j = isq ? i : i - nq;
+    const int64_t d = j % half;
+    j /= half;
+    const int64_t s = j % S;
+    const int64_t h = j / S;
     const T* xp = static_cast<const T*>(t.x) + b * t.sb + h * t.sh + s * t.ss + d;
     T* op = static_cast<T*>(t.out) + b * t.ob + h * t.oh + s * t.os + d;
-    const CT* cp = cos + b * cb + s * cs + d;
-    const CT* sp = sin + b * cb + s * cs + d;
-    if constexpr (VEC) {
-      Vec16<T> x1 = ld16(xp), x2 = ld16(xp + half);
-      float c[NE], sn[NE];
-      if constexpr (sizeof(CT) == sizeof(T)) {
-        Vec16<CT> cv = ld16(cp), sv = ld16(sp);
-#pragma unroll
-        for (int e = 0; e < NE; ++e) {
-          c[e] = Cvt<CT>::to_f(cv.v[e]);
-          sn[e] = sign * Cvt<CT>::to_f(sv.v[e]);
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < NE; ++e) {
-          c[e] = Cvt<CT>::to_f(cp[e]);
-          sn[e] = sign * Cvt<CT>::to_f(sp[e]);
-        }
-      }
-      Vec16<T> y1, y2;
-#pragma unroll
-      for (int e = 0; e < NE; ++e) {
-        const float a = Cvt<T>::to_f(x1.v[e]), bb = Cvt<T>::to_f(x2.v[e]);
-        y1.v[e] = Cvt<T>::from_f(a * c[e] - bb * sn[e]);
-        y2.v[e] = Cvt<T>::from_f(a * sn[e] + bb * c[e]);
-      }
-      st16(op, y1);
-      st16(op + half, y2);
-    } else {
-      const float c = Cvt<CT>::to_f(cp[0]), sn = sign * Cvt<CT>::to_f(sp[0]);
-      const float a = Cvt<T>::to_f(xp[0]), bb = Cvt<T>::to_f(xp[half]);
-      op[0] = Cvt<T>::from_f(a * c - bb * sn);
-      op[half] = Cvt<T>::from_f(a * sn + bb * c);
-    }
+    const float c = Cvt<CT>::to_f(cos[b * cb + s * cs + d]);
+    const float sn = sign * Cvt<CT>::to_f(sin[b * cb + s * cs + d]);
+    const float a = Cvt<T>::to_f(xp[0]), bb = Cvt<T>::to_f(xp[half]);
+    op[0] = Cvt<T>::from_f(a * c - bb * sn);
+    op[half] = Cvt<T>::from_f(a * sn + bb * c);
   }
 }
 
@@ -96,26 +135,30 @@ int rope_run(const RopeTensor& q, const RopeTensor& k, const void* cos, const vo
            (t.os * es) % 16 == 0;
   };
   const int64_t ces = sizeof(CT);
-  bool vec = (half % NE) == 0 && ok_t(q) && ok_t(k);
+  bool vec = (half % NE) == 0 && ok_t(q) && ok_t(k) && S < (int64_t(1) << 31);
   if (vec && sizeof(CT) == sizeof(T))
     vec = aligned16(cos) && aligned16(sin) && (cb * ces) % 16 == 0 && (cs * ces) % 16 == 0;
-  const int64_t per_b = (q.heads + k.heads) * S * (vec ? half / NE : half);
-  if (per_b >= (int64_t(1) << 31)) {
-    set_last_error("soup_rope: heads * seq * head_dim too large for one batch");
-    return SOUP_ERR_UNSUPPORTED;
+  const CT* C = static_cast<const CT*>(cos);
+  const CT* Sn = static_cast<const CT*>(sin);
+  cudaError_t e;
+  if (vec) {
+    constexpr int P = 4;
+    const int64_t slots = (q.heads + k.heads) * (half / NE);
+    int threads = static_cast<int>((slots + 31) / 32 * 32);
+    if (threads > 256) threads = 256;
+    dim3 grid(static_cast<unsigned>((S + P - 1) / P), static_cast<unsigned>(B));
+    e = launch_pdl(rope_rows_kernel<T, CT, P>, grid, dim3(threads), 0, st, q, k, C, Sn, cb, cs,
+                   static_cast<int>(S), static_cast<int>(half), sign);
+  } else {
+    const int64_t per_b = (q.heads + k.heads) * S * half;
+    int64_t bx = (per_b + 255) / 256;
+    const int64_t cap = (int64_t)num_sms() * 8 / (B > 0 ? B : 1) + 1;
+    if (bx > cap) bx = cap;
+    if (bx < 1) bx = 1;
+    e = launch_pdl(rope_scalar_kernel<T, CT>, dim3((unsigned)bx, (unsigned)B), dim3(256), 0, st, q, k,
+                   C, Sn, cb, cs, S, half, sign);
   }
-  int64_t bx = (per_b + 255) / 256;
-  const int64_t cap = (int64_t)num_sms() * 8 / (B > 0 ? B : 1) + 1;
-  if (bx > cap) bx = cap;
-  if (bx < 1) bx = 1;
-  dim3 grid((unsigned)bx, (unsigned)B);
-  if (vec)
-    rope_kernel<T, CT, true><<<grid, 256, 0, st>>>(q, k, static_cast<const CT*>(cos),
-                                                   static_cast<const CT*>(sin), cb, cs, S, half, sign);
-  else
-    rope_kernel<T, CT, false><<<grid, 256, 0, st>>>(q, k, static_cast<const CT*>(cos),
-                                                    static_cast<const CT*>(sin), cb, cs, S, half, sign);
-  return launch_status();
+  return cuda_status(e);
 }
 
 }  // namespace

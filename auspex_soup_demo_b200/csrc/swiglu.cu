@@ -46,6 +46,8 @@ template <typename T, class Op>
 __global__ void __launch_bounds__(256) ew_vec_kernel(Ptrs<T, Op::kIn, Op::kOut> p, int64_t rows,
                                                      int64_t cols, int flat) {
   constexpr int NE = Vec16<T>::N;
+  pdl_wait();
+  pdl_trigger();
   const int64_t vpr = cols / NE;
   const int64_t total = rows * vpr;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -113,12 +115,9 @@ int run(const Ptrs<T, Op::kIn, Op::kOut>& p, int64_t rows, int64_t cols, cudaStr
   if (blocks < 1) blocks = 1;
   if (vec) {
     Ptrs<T, Op::kIn, Op::kOut> q = p;
-    if (flat) {
-      // one row of rows*cols elements
-      ew_vec_kernel<T, Op><<<(unsigned)blocks, 256, 0, st>>>(q, 1, rows * cols, 1);
-    } else {
-      ew_vec_kernel<T, Op><<<(unsigned)blocks, 256, 0, st>>>(q, rows, cols, 0);
-    }
+    // flat: one row of rows*cols elements
+    return cuda_status(launch_pdl(ew_vec_kernel<T, Op>, dim3((unsigned)blocks), dim3(256), 0, st, q,
+                                  flat ? int64_t(1) : rows, flat ? rows * cols : cols, flat ? 1 : 0));
   } else {
     ew_scalar_kernel<T, Op><<<(unsigned)blocks, 256, 0, st>>>(p, rows, cols);
   }

@@ -69,10 +69,10 @@ int soup_rmsnorm_bwd(const void* dy, int64_t dy_row_stride, const void* x, int64
  * code that must avoid cudaMalloc because it can synchronise the device.
  * Same arguments and results as soup_rmsnorm_bwd without the workspace: the dw
  * partial rows go to a 4 MiB array built into the library (every GPU that
- * loads the library holds it until exit). Calls needing more than 4 MiB of
- * partials (about rows-independent: one fp32 row of `cols` per CTA, at most
- * one CTA per SM, so cols up to ~7000 on 148 SMs on the vector path) return
- * SOUP_ERR_WORKSPACE. The first call on a device looks up the array's device
+ * loads the library holds it until exit). The partials are one fp32 row of
+ * `cols` per CTA, at most 3 CTAs per SM on the vector path (cols up to about
+ * 2360 on a 148-SM B200, e.g. hidden sizes 1536 and 2048); calls needing more
+ * than 4 MiB return SOUP_ERR_WORKSPACE. The first call on a device looks up the array's device
  * address; make that first call before any stream capture. All calls share
  * the array, so calls whose kernels overlap on the GPU (other streams, other
  * host threads) race: serialise them. */

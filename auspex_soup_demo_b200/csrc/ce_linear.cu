@@ -34,10 +34,10 @@ using bf16 = __nv_bfloat16;
 // row segment instead of scattered 16 B pieces.
 
 __device__ __forceinline__ void stage_row(uint8_t* stage, int lane, const float (&v)[32], float a) {
-  float4* dst = reinterpret_cast<float4*>(stage + lane * kStageRowBytes);
 #pragma unroll
   for (int q = 0; q < 8; ++q)
-    dst[q] = make_float4(a * v[4 * q], a * v[4 * q + 1], a * v[4 * q + 2], a * v[4 * q + 3]);
+    *reinterpret_cast<float4*>(stage + stage_off(lane, q)) =
+        make_float4(a * v[4 * q], a * v[4 * q + 1], a * v[4 * q + 2], a * v[4 * q + 3]);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -59,7 +59,7 @@ __device__ __forceinline__ void write_block(const uint8_t* stage, int lane, void
     const int r = i * 4 + rsub;
     const int grow = row0 + r;
     if (grow >= M) continue;
-    float4 x = *reinterpret_cast<const float4*>(stage + r * kStageRowBytes + cv * 16);
+    float4 x = *reinterpret_cast<const float4*>(stage + stage_off(r, cv));
     if (vec && gcol + 4 <= N) {
       if constexpr (BF16) {
         bf16* dst = reinterpret_cast<bf16*>(C) + (int64_t)grow * ldc + gcol;
@@ -121,13 +121,15 @@ struct EpiStore {
     int M, N;
   };
   static __device__ __forceinline__ void tile(const Params& p, int mt, int nt, int ks, int quarter,
-                                              int lane, uint32_t taddr, uint8_t* stage) {
+                                              int lane, uint32_t taddr, uint8_t* stage, int group,
+                                              int ngroups) {
     const int row0 = mt * BM + quarter * 32;
     const float a = p.alpha * (p.scale ? *p.scale : 1.f);
     const size_t es = p.c_bf16 ? 2 : 4;
     void* C = static_cast<uint8_t*>(p.c) + (size_t)ks * p.split_stride * es;
+    const int nch = BN / 32 / ngroups;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = group * nch; c < (group + 1) * nch; ++c) {
       float v[32];
       tmem_ld32(taddr + c * 32, v);
       const int col0 = nt * BN + c * 32;
@@ -149,7 +151,7 @@ template <int BN>
 struct EpiCE {
   struct Params {
     const int64_t* targets;
-    float4* partials;  // [n_tiles][M]: (max, sum exp, sum z*exp, argmax bits)
+    float4* partials;  // [n_tiles * ngroups][M]: (max, sum exp, sum z*exp, argmax bits)
     float* zt;         // [M] target logit (written by the tile holding it)
     bf16* logits;      // [M][ld_logits] or nullptr
     int64_t ld_logits;
@@ -157,9 +159,11 @@ struct EpiCE {
     int M, N;
   };
   static __device__ __forceinline__ void tile(const Params& p, int mt, int nt, int ks, int quarter,
-                                              int lane, uint32_t taddr, uint8_t* stage) {
+                                              int lane, uint32_t taddr, uint8_t* stage, int group,
+                                              int ngroups) {
     const int row0 = mt * BM + quarter * 32;
     const int row = row0 + lane;
+    const int nch = BN / 32 / ngroups;
     const bool row_ok = row < p.M;
     const int64_t t = row_ok ? p.targets[row] - p.vocab_offset : -1;
     float m = -INFINITY, s = 0.f, w = 0.f;
@@ -167,7 +171,7 @@ struct EpiCE {
     float ztv = 0.f;
     bool found = false;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = group * nch; c < (group + 1) * nch; ++c) {
       float v[32];
       tmem_ld32(taddr + c * 32, v);
       const int col0 = nt * BN + c * 32;
@@ -227,7 +231,7 @@ struct EpiCE {
       }
     }
     if (row_ok) {
-      p.partials[(int64_t)nt * p.M + row] = make_float4(m, s, w, __int_as_float(bidx));
+      p.partials[(int64_t)(nt * ngroups + group) * p.M + row] = make_float4(m, s, w, __int_as_float(bidx));
       if (found) p.zt[row] = ztv;
     }
   }
@@ -289,11 +293,14 @@ static bool tma_ok(const void* p, int64_t ld) {
 constexpr int kBN = 256;
 constexpr int kStages = 4;
 
+// Epilogue warps of every GEMM launch (two per TMEM lane quarter).
+constexpr int kEpiWarps = 8;
+
 template <bool A_MN, bool B_MN, class Epi>
 static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
                        const typename Epi::Params& ep, cudaStream_t stream) {
-  using L = SmemLayout<kBN, kStages>;
-  auto kern = gemm_kernel<kBN, kStages, A_MN, B_MN, Epi>;
+  using L = SmemLayout<kBN, kStages, kEpiWarps>;
+  auto kern = gemm_kernel<kBN, kStages, A_MN, B_MN, Epi, kEpiWarps>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -311,7 +318,7 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched
     return SOUP_ERR_CUDA;
   }
   const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, kThreads, L::kBytes, stream>>>(ma, mb, sched, ep, err);
+  kern<<<grid, gemm_threads(kEpiWarps), L::kBytes, stream>>>(ma, mb, sched, ep, err);
   return launch_status();
 }
 
@@ -546,6 +553,7 @@ static void mark_stage(int i, cudaStream_t s) {
 struct CEWorkspace {
   int64_t ld_logits;
   int n_vtiles;
+  int n_parts;  // online-softmax records per row (vocab tiles x epilogue column groups)
   int splits;
   size_t off_logits, off_partials, off_zt, off_splitk, total;
 };
@@ -566,12 +574,13 @@ static CEWorkspace ce_layout(int64_t rows, int64_t vocab, int64_t dim) {
   CEWorkspace w;
   w.ld_logits = (vocab + 7) / 8 * 8;
   w.n_vtiles = static_cast<int>((vocab + kBN - 1) / kBN);
+  w.n_parts = w.n_vtiles * (kEpiWarps / 4);
   w.splits = choose_splits(rows, dim, vocab, num_sms());
   size_t off = 0;
   w.off_logits = off;
   off = align_up(off + (size_t)rows * w.ld_logits * 2, 256);
   w.off_partials = off;
-  off = align_up(off + (size_t)w.n_vtiles * rows * 16, 256);
+  off = align_up(off + (size_t)w.n_parts * rows * 16, 256);
   w.off_zt = off;
   off = align_up(off + (size_t)rows * 4, 256);
   w.off_splitk = off;
@@ -693,7 +702,7 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   // 2. metrics + dlogits
   {
     const float den = denominator > 0.f ? denominator : 1.f;
-    ce_finalize_kernel<<<M, 512, 0, stream>>>(partials, w.n_vtiles, zt, targets, L, w.ld_logits, M,
+    ce_finalize_kernel<<<M, 512, 0, stream>>>(partials, w.n_parts, zt, targets, L, w.ld_logits, M,
                                                V, 1.f / den, ignore_index, losses, entropies,
                                                correct, need_grad ? 1 : 0);
     if ((rc = launch_status())) return rc;
@@ -787,7 +796,7 @@ int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shar
   Sched sc{(M + BM - 1) / BM, w.n_vtiles, 1, (D + BK - 1) / BK, 0};
   EpiCE<kBN>::Params ep{targets, partials, zt, L, w.ld_logits, vocab_offset, M, V};
   if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, sc, ep, stream))) return rc;
-  ce_shard_state_kernel<<<(M + 7) / 8, 256, 0, stream>>>(partials, w.n_vtiles, zt, targets, M, V,
+  ce_shard_state_kernel<<<(M + 7) / 8, 256, 0, stream>>>(partials, w.n_parts, zt, targets, M, V,
                                                          vocab_offset, states);
   return launch_status();
 }

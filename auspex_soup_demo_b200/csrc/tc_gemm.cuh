@@ -10,7 +10,9 @@
 //
 //   warp 0      TMA producer (one elected lane)      smem ring of STAGES
 //   warp 1      TMEM allocator + MMA issuer (lane 0)  2 accumulators in TMEM
-//   warps 2..5  epilogue: tcgen05.ld -> registers -> Epi::tile(...)
+//   warps 2..   epilogue (EPI_WARPS = 4 or 8): tcgen05.ld -> registers -> Epi::tile(...);
+//               warp w reads TMEM lane quarter w % 4; with 8 warps the two
+//               warps of a quarter take the left / right half of the columns
 //
 // Each tile is BM=128 rows x BN columns with BK=64 per stage; the MMA shape
 // is 128 x BN x 16. The TMEM accumulators are double buffered (2 x BN fp32
@@ -34,7 +36,8 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+// threads of a CTA with `epi_warps` epilogue warps (+ producer and MMA warps)
+__host__ __device__ constexpr int gemm_threads(int epi_warps) { return 64 + 32 * epi_warps; }
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
 
 // error codes written to the device error word
@@ -176,17 +179,23 @@ struct Sched {
   }
 };
 
-// Per-epilogue-warp staging buffer: 32 rows x 32 fp32 (128 B) + 16 B pad.
-constexpr int kStageRowBytes = 144;
+// Per-epilogue-warp staging buffer: 32 rows x 32 fp32 (128 B per row); the
+// 16-byte granule q of row r is stored at granule q ^ (r & 7) (bank-conflict
+// free for both the row-per-thread writes and the row-segment reads).
+constexpr int kStageRowBytes = 128;
 constexpr int kEpiWarpBytes = 32 * kStageRowBytes;
 
-template <int BN, int STAGES>
+__device__ __forceinline__ int stage_off(int row, int granule) {
+  return row * kStageRowBytes + ((granule ^ (row & 7)) << 4);
+}
+
+template <int BN, int STAGES, int EPI_WARPS>
 struct SmemLayout {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kEpiOff = STAGES * kStageBytes;
-  static constexpr int kBarOff = kEpiOff + 4 * kEpiWarpBytes;
+  static constexpr int kBarOff = kEpiOff + EPI_WARPS * kEpiWarpBytes;
   // full[S], empty[S], tfull[2], tempty[2], drain, then tmem base + abort flag
   static constexpr int kNumBars = 2 * STAGES + 5;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
@@ -214,12 +223,14 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity,
 //   struct Params;
 //   static __device__ void tile(const Params&, int mt, int nt, int ks, int quarter,
 //                               int lane, uint32_t tmem_acc /* lane base applied */,
-//                               uint8_t* stage /* this warp's kEpiWarpBytes of smem */);
-template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi>
-__global__ void __launch_bounds__(kThreads, 1)
+//                               uint8_t* stage /* this warp's kEpiWarpBytes of smem */,
+//                               int group, int ngroups /* column part of the tile */);
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS>
+__global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 Sched sched, typename Epi::Params ep, int* err) {
-  using L = SmemLayout<BN, STAGES>;
+  static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
+  using L = SmemLayout<BN, STAGES, EPI_WARPS>;
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, multiple of 64");
   static_assert(2 * BN <= 512, "two accumulators must fit in 512 TMEM columns");
   constexpr int kTmemCols = (2 * BN <= 128) ? 128 : ((2 * BN <= 256) ? 256 : 512);
@@ -248,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 4);
+      mbar_init(tempty_bar(a), EPI_WARPS);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -370,7 +381,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------ epilogue ----
     const int quarter = warp & 3;  // TMEM lanes this warp may access
-    uint8_t* stage = smem + L::kEpiOff + (warp - 2) * kEpiWarpBytes;
+    const int e = warp - 2;
+    constexpr int kGroups = EPI_WARPS / 4;
+    const int group = e >> 2;
+    uint8_t* stage = smem + L::kEpiOff + e * kEpiWarpBytes;
     uint32_t lt = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++lt) {
       int mt, nt, ks;
@@ -383,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      Epi::tile(ep, mt, nt, ks, quarter, lane, taddr, stage);
+      Epi::tile(ep, mt, nt, ks, quarter, lane, taddr, stage, group, kGroups);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));

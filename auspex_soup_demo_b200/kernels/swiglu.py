@@ -78,6 +78,12 @@ def fast_swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return FastSwiGLUFunction.apply(gate, up)
 
 
+#: Recompute gate/up + SwiGLU in backward (the reference's selective recompute,
+#: ``swiglu.py:197-214``). False keeps the activations instead: more memory
+#: (2 x tokens x intermediate bf16 per layer), no second gate/up GEMM pass.
+RECOMPUTE = True
+
+
 def patch_qwen2_mlp():
     """Route ``Qwen2MLP.forward`` on CUDA tensors through the fused SwiGLU.
 
@@ -100,7 +106,8 @@ def patch_qwen2_mlp():
         act = getattr(getattr(self, "config", None), "hidden_act", "silu")
         if act != "silu" or not x.is_cuda:
             return original_forward(self, x)
-        if not (self.training and torch.is_grad_enabled() and getattr(x, "requires_grad", False)):
+        if not (RECOMPUTE and self.training and torch.is_grad_enabled()
+                and getattr(x, "requires_grad", False)):
             return self.down_proj(fast_swiglu(self.gate_proj(x), self.up_proj(x)))
 
         def _swiglu_forward(hidden_states):

@@ -104,6 +104,20 @@ class _NF4LinearFn(torch.autograd.Function):
         return dx, None, None, None, None, None
 
 
+def _add_lora(y: torch.Tensor, x: torch.Tensor, lora_a: torch.Tensor, lora_b: torch.Tensor,
+              scaling: float) -> torch.Tensor:
+    """y + scaling * (x A^T) B^T with the addition done by the GEMM (beta = 1).
+
+    The scale is folded into the [out, r] factor and the rank-r product is
+    accumulated onto y by one addmm, so no pass over the [tokens, out]
+    activations is spent on scaling or adding.
+    """
+    xa = F.linear(x, lora_a.to(x.dtype))
+    b = (lora_b * scaling).to(x.dtype)
+    out = torch.addmm(y.reshape(-1, y.shape[-1]), xa.reshape(-1, xa.shape[-1]), b.t())
+    return out.view(y.shape)
+
+
 class LoRANF4Linear(torch.nn.Module):
     """Frozen NF4 base linear + trainable LoRA: y = base(x) + (alpha/r) * B(A(x))."""
 
@@ -131,9 +145,7 @@ class LoRANF4Linear(torch.nn.Module):
     def forward(self, x):
         y = _NF4LinearFn.apply(x, self.packed, self.absmax, self.bias, self.out_features,
                                self.in_features)
-        a = self.lora_A.to(x.dtype)
-        b = self.lora_B.to(x.dtype)
-        return y + F.linear(F.linear(x, a), b) * self.scaling
+        return _add_lora(y, x, self.lora_A, self.lora_B, self.scaling)
 
 
 class LoRADenseLinear(torch.nn.Module):
@@ -157,7 +169,7 @@ class LoRADenseLinear(torch.nn.Module):
 
     def forward(self, x):
         y = F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
-        return y + F.linear(F.linear(x, self.lora_A.to(x.dtype)), self.lora_B.to(x.dtype)) * self.scaling
+        return _add_lora(y, x, self.lora_A, self.lora_B, self.scaling)
 
 
 def qwen2_1p5b_config(num_layers: int = 28, **overrides):

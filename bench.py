@@ -489,6 +489,9 @@ def run_qlora(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     apply()
+    if args.no_recompute:
+        from auspex_soup_demo_b200.kernels import swiglu as _swiglu
+        _swiglu.RECOMPUTE = False
     B, S = args.batch, args.seq
     model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=args.layers), device=dev,
                                     seed=0)
@@ -562,6 +565,7 @@ def run_qlora(args):
                        "layers": args.layers, "batch_per_gpu": B, "seq_len": S,
                        "lora": "r16 a32 q/k/v/o/gate/up/down", "lora_params": n_lora,
                        "base": "NF4 blocksize 64, dequantised per use", "optimizer": "AdamW 2e-4",
+                       "mlp_recompute": not args.no_recompute,
                        "parallelism": f"dp{world}" + (" (one NCCL allreduce of the flat LoRA grads)"
                                                       if world > 1 else ""),
                        "l2": "weights and activations far larger than L2"},
@@ -686,6 +690,8 @@ def main():
     ap.add_argument("--seq", type=int, default=512, help="qlora: tokens per sequence")
     ap.add_argument("--layers", type=int, default=28, help="qlora: decoder layers")
     ap.add_argument("--no-graph", action="store_true", help="qlora: launch eagerly, no CUDA graph")
+    ap.add_argument("--no-recompute", action="store_true",
+                    help="qlora: keep MLP activations instead of recomputing gate/up in backward")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -17,6 +17,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "soup_common.cuh"
 #include "tc_gemm.cuh"
@@ -120,10 +121,10 @@ struct EpiStore {
     int vec_ok;  // 16-byte aligned rows
     int M, N;
   };
-  static __device__ __forceinline__ void tile(const Params& p, int mt, int nt, int ks, int quarter,
-                                              int lane, uint32_t taddr, uint8_t* stage, int group,
-                                              int ngroups) {
-    const int row0 = mt * BM + quarter * 32;
+  static __device__ __forceinline__ void tile(const Params& p, int row_base, int nt, int ks,
+                                              int quarter, int lane, uint32_t taddr, uint8_t* stage,
+                                              int group, int ngroups) {
+    const int row0 = row_base + quarter * 32;
     const float a = p.alpha * (p.scale ? *p.scale : 1.f);
     const size_t es = p.c_bf16 ? 2 : 4;
     void* C = static_cast<uint8_t*>(p.c) + (size_t)ks * p.split_stride * es;
@@ -158,10 +159,10 @@ struct EpiCE {
     int64_t vocab_offset;  // first vocabulary row of this weight shard (0 unsharded)
     int M, N;
   };
-  static __device__ __forceinline__ void tile(const Params& p, int mt, int nt, int ks, int quarter,
-                                              int lane, uint32_t taddr, uint8_t* stage, int group,
-                                              int ngroups) {
-    const int row0 = mt * BM + quarter * 32;
+  static __device__ __forceinline__ void tile(const Params& p, int row_base, int nt, int ks,
+                                              int quarter, int lane, uint32_t taddr, uint8_t* stage,
+                                              int group, int ngroups) {
+    const int row0 = row_base + quarter * 32;
     const int row = row0 + lane;
     const int nch = BN / 32 / ngroups;
     const bool row_ok = row < p.M;
@@ -296,9 +297,26 @@ constexpr int kStages = 4;
 // Epilogue warps of every GEMM launch (two per TMEM lane quarter).
 constexpr int kEpiWarps = 8;
 
+// CTA-pair tiles (256 rows over two SMs, cta_group::2) are the default;
+// SOUP_GEMM_PAIRS=0 in the environment selects single-CTA 128-row tiles.
+static bool use_pairs() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("SOUP_GEMM_PAIRS");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+// rows of one output tile, and the row box of a K-major B operand map
+static int tile_m() { return use_pairs() ? 2 * BM : BM; }
+static int b_box_rows() { return use_pairs() ? kBN / 2 : kBN; }
+static int m_tiles(int64_t m) { return static_cast<int>((m + tile_m() - 1) / tile_m()); }
+
+constexpr int kPairStages = 6;
+
 template <bool A_MN, bool B_MN, class Epi>
-static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
-                       const typename Epi::Params& ep, cudaStream_t stream) {
+static int launch_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
+                              const typename Epi::Params& ep, cudaStream_t stream, int* err) {
   using L = SmemLayout<kBN, kStages, kEpiWarps>;
   auto kern = gemm_kernel<kBN, kStages, A_MN, B_MN, Epi, kEpiWarps>;
   static bool attr_set[64] = {false};
@@ -311,15 +329,65 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched
     attr_set[dev] = true;
   }
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
+  const int grid = units < num_sms() ? units : num_sms();
+  kern<<<grid, gemm_threads(kEpiWarps), L::kBytes, stream>>>(ma, mb, sched, ep, err);
+  return launch_status();
+}
+
+template <bool A_MN, bool B_MN, class Epi>
+static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
+                            const typename Epi::Params& ep, cudaStream_t stream, int* err) {
+  using L = SmemLayout<kBN / 2, kPairStages, kEpiWarps>;
+  static_assert(L::kBytes <= 232448, "pair GEMM shared memory exceeds 227 KB");
+  auto kern = gemm_pair_kernel<kBN, kPairStages, A_MN, B_MN, Epi, kEpiWarps>;
+  static int max_clusters[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cuda_status(cudaErrorInvalidDevice);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(gemm_threads(kEpiWarps));
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_clusters[dev] == 0) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    if (e != cudaSuccess) return cuda_status(e);
+    int n = 0;
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess) return cuda_status(e);
+    if (n <= 0) {
+      set_last_error("pair GEMM: no cluster of two CTAs fits on this device");
+      return SOUP_ERR_UNSUPPORTED;
+    }
+    max_clusters[dev] = n;
+  }
+  const int units = sched.m_tiles * sched.n_tiles * sched.splits;
+  const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
+  cfg.gridDim = dim3(2 * clusters);
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mb, sched, ep, err));
+}
+
+// sched.m_tiles counts tile_m() rows.
+template <bool A_MN, bool B_MN, class Epi>
+static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
+                       const typename Epi::Params& ep, cudaStream_t stream) {
+  const int units = sched.m_tiles * sched.n_tiles * sched.splits;
   if (units <= 0) return SOUP_OK;
   int* err = device_err_ptr();
   if (!err) {
     set_last_error("device error word unavailable");
     return SOUP_ERR_CUDA;
   }
-  const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, gemm_threads(kEpiWarps), L::kBytes, stream>>>(ma, mb, sched, ep, err);
-  return launch_status();
+  if (use_pairs()) return launch_gemm_pair<A_MN, B_MN, Epi>(ma, mb, sched, ep, stream, err);
+  return launch_gemm_single<A_MN, B_MN, Epi>(ma, mb, sched, ep, stream, err);
 }
 
 // ------------------------------------------------------ CE row kernels -----
@@ -560,14 +628,33 @@ struct CEWorkspace {
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Vocabulary splits of the dX GEMM (1..16, >= 16 k-blocks per unit). Units
+// are (m tile, n tile, split); the estimated time of a split count is
+//   waves x k-blocks per unit           (one k-block of a tile ~ 512 tensor
+//                                        cycles ~ 0.28 us on every worker)
+//   + fp32 partial bytes re-read by the reduce, at HBM speed
+// (0.28 us of HBM ~ 1.8 MB), and the cheapest count wins.
 static int choose_splits(int64_t rows, int64_t dim, int64_t vocab, int sms) {
-  const int64_t tiles = ((rows + BM - 1) / BM) * ((dim + kBN - 1) / kBN);
-  int64_t s = (2 * sms + tiles - 1) / tiles;  // about two waves of work units
+  const int64_t tiles = m_tiles(rows) * ((dim + kBN - 1) / kBN);
+  const int64_t workers = use_pairs() ? sms / 2 : sms;
   const int64_t kb = (vocab + BK - 1) / BK;
-  if (s > kb / 16) s = kb / 16;              // keep >= 16 k-blocks per unit
-  if (s < 1) s = 1;
-  if (s > 16) s = 16;
-  return static_cast<int>(s);
+  int64_t s_max = kb / 16;
+  if (s_max > 16) s_max = 16;
+  if (s_max < 1) s_max = 1;
+  constexpr double kBytesPerKBlock = 1.8e6;
+  int best = 1;
+  double best_cost = 0.0;
+  for (int64_t s = 1; s <= s_max; ++s) {
+    const int64_t units = tiles * s;
+    const int64_t waves = (units + workers - 1) / workers;
+    double cost = static_cast<double>(waves * ((kb + s - 1) / s));
+    if (s > 1) cost += static_cast<double>(s * rows * dim * 4) / kBytesPerKBlock;
+    if (s == 1 || cost < best_cost) {
+      best_cost = cost;
+      best = static_cast<int>(s);
+    }
+  }
+  return best;
 }
 
 static CEWorkspace ce_layout(int64_t rows, int64_t vocab, int64_t dim) {
@@ -599,7 +686,7 @@ static int dx_gemm(const bf16* L, int64_t ld_logits, const void* weight, int64_t
   int rc;
   if ((rc = make_operand_map(&ma, L, false, M, V, ld_logits, BM))) return rc;
   if ((rc = make_operand_map(&mb, weight, true, D, V, w_ld, 64))) return rc;
-  Sched sc{(M + BM - 1) / BM, (D + kBN - 1) / kBN, splits, (V + BK - 1) / BK, 1};
+  Sched sc{m_tiles(M), (D + kBN - 1) / kBN, splits, (V + BK - 1) / BK, 1};
   const bool bf = dh_dtype == SOUP_BF16;
   if (splits == 1) {
     EpiStore<kBN>::Params ep{dh, D, 0, nullptr, 1.f, bf ? 1 : 0, 0,
@@ -631,7 +718,7 @@ static int dweight_gemm(const bf16* L, int64_t ld_logits, const void* hidden, in
   int rc;
   if ((rc = make_operand_map(&ma, L, true, V, M, ld_logits, 64))) return rc;
   if ((rc = make_operand_map(&mb, hidden, true, D, M, h_ld, 64))) return rc;
-  Sched sc{(V + BM - 1) / BM, (D + kBN - 1) / kBN, 1, (M + BK - 1) / BK, 1};
+  Sched sc{m_tiles(V), (D + kBN - 1) / kBN, 1, (M + BK - 1) / BK, 1};
   const int es = dw_dtype == SOUP_BF16 ? 2 : 4;
   EpiStore<kBN>::Params ep{dweight, D, 0, scale, 1.f, dw_dtype == SOUP_BF16 ? 1 : 0,
                            accumulate ? 1 : 0,
@@ -693,8 +780,8 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   {
     CUtensorMap ma, mb;
     if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
-    if ((rc = make_operand_map(&mb, weight, false, vocab, dim, w_ld, kBN))) return rc;
-    Sched sc{(M + BM - 1) / BM, w.n_vtiles, 1, (D + BK - 1) / BK, 0};
+    if ((rc = make_operand_map(&mb, weight, false, vocab, dim, w_ld, b_box_rows()))) return rc;
+    Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
     EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, 0, M, V};
     if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, sc, ep, stream))) return rc;
     mark_stage(0, stream);
@@ -792,8 +879,9 @@ int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shar
   int rc;
   CUtensorMap ma, mb;
   if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
-  if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, kBN))) return rc;
-  Sched sc{(M + BM - 1) / BM, w.n_vtiles, 1, (D + BK - 1) / BK, 0};
+  if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, b_box_rows())))
+    return rc;
+  Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
   EpiCE<kBN>::Params ep{targets, partials, zt, L, w.ld_logits, vocab_offset, M, V};
   if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, sc, ep, stream))) return rc;
   ce_shard_state_kernel<<<(M + 7) / 8, 256, 0, stream>>>(partials, w.n_parts, zt, targets, M, V,
@@ -898,11 +986,11 @@ int soup_gemm_bf16(const void* a, int64_t lda, int a_mn_major, const void* b, in
   CUtensorMap ma, mb;
   int rc;
   if ((rc = make_operand_map(&ma, a, a_mn_major != 0, m, k, lda, BM))) return rc;
-  if ((rc = make_operand_map(&mb, b, b_mn_major != 0, n, k, ldb, kBN))) return rc;
+  if ((rc = make_operand_map(&mb, b, b_mn_major != 0, n, k, ldb, b_box_rows()))) return rc;
   const int es = c_dtype == SOUP_BF16 ? 2 : 4;
   EpiStore<kBN>::Params ep{c, ldc, 0, nullptr, alpha, c_dtype == SOUP_BF16 ? 1 : 0, accumulate ? 1 : 0,
                            (aligned16(c) && (ldc * es) % 16 == 0) ? 1 : 0, (int)m, (int)n};
-  const int mt = (int)((m + BM - 1) / BM), nt = (int)((n + kBN - 1) / kBN);
+  const int mt = m_tiles(m), nt = (int)((n + kBN - 1) / kBN);
   Sched sc{mt, nt, 1, (int)((k + BK - 1) / BK), nt > mt ? 0 : 1};
   cudaStream_t stream = as_stream(stream_);
   if (!a_mn_major && !b_mn_major) return launch_gemm<false, false, EpiStore<kBN>>(ma, mb, sc, ep, stream);

@@ -68,6 +68,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Same, acquiring at cluster scope (arrivals that come from the peer CTA).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -144,11 +156,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo,
   return d;
 }
 
-// Instruction descriptor: fp32 accumulate, bf16 A and B, M=128, N=bn.
-__host__ __device__ constexpr uint32_t idesc_bf16(int bn, bool a_mn, bool b_mn) {
+// Instruction descriptor: fp32 accumulate, bf16 A and B, M=bm, N=bn.
+__host__ __device__ constexpr uint32_t idesc_bf16(int bn, bool a_mn, bool b_mn, int bm = BM) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
          ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
-         (static_cast<uint32_t>(BM >> 4) << 24);
+         (static_cast<uint32_t>(bm >> 4) << 24);
 }
 
 // ---------------------------------------------------------- tile schedule --
@@ -204,12 +216,16 @@ struct SmemLayout {
 
 // Bounded wait. Returns false when the CTA is aborting (timeout here or
 // elsewhere); on a local timeout it records `code` and raises the flag.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity,
                                              volatile int* abort_flag, int* err, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+  auto try_wait = [&]() {
+    return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+  };
+  if (try_wait()) return true;
   uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (try_wait()) return true;
     if (*abort_flag) return false;
     if (globaltimer() - t0 > kWaitNs) {
       *abort_flag = 1;
@@ -221,7 +237,8 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity,
 
 // Epi must provide:
 //   struct Params;
-//   static __device__ void tile(const Params&, int mt, int nt, int ks, int quarter,
+//   static __device__ void tile(const Params&, int row_base /* first row of the CTA's
+//                               128-row block */, int nt, int ks, int quarter,
 //                               int lane, uint32_t tmem_acc /* lane base applied */,
 //                               uint8_t* stage /* this warp's kEpiWarpBytes of smem */,
 //                               int group, int ngroups /* column part of the tile */);
@@ -397,7 +414,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      Epi::tile(ep, mt, nt, ks, quarter, lane, taddr, stage, group, kGroups);
+      Epi::tile(ep, mt * BM, nt, ks, quarter, lane, taddr, stage, group, kGroups);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
@@ -409,6 +426,277 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+
+// ============================================================ CTA pairs ====
+// Same GEMM with a cluster of two CTAs on two SMs computing one 256 x BN
+// tile (tcgen05 cta_group::2, MMA shape 256 x BN x 16). CTA rank r of the
+// pair loads rows [r*128, r*128+128) of the A tile and columns
+// [r*BN/2, (r+1)*BN/2) of the B tile into its own shared memory; the MMA,
+// issued by rank 0 alone, reads both CTAs' halves and leaves rows
+// [r*128, r*128+128) x BN columns of the accumulator in rank r's TMEM. Per SM
+// a k-block now moves (128 + BN/2) x 64 operand elements instead of
+// (128 + BN) x 64.
+//
+// Cross-CTA protocol (all waits bounded as in the 1-CTA kernel):
+//   full[s]   rank 0's barrier only: rank 0 arms it with both CTAs' bytes;
+//             both CTAs' TMA copies (cta_group::2) complete on it
+//   empty[s]  one per CTA: rank 0's MMA completion commits to both
+//   tfull[a]  one per CTA: rank 0 commits to both after a tile's last MMA
+//   tempty[a] rank 0's only, count 2 x EPI_WARPS: every epilogue warp of both
+//             CTAs arrives (rank 1 remotely) after draining its TMEM lanes
+// A cluster barrier after set-up and before TMEM release keeps each CTA's
+// shared memory alive while its peer may still signal it.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+// 2-D TMA tile into this CTA's shared memory, completing on an mbarrier that
+// may live in the peer CTA of the pair.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map,
+                                                 uint32_t cluster_bar, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   cluster_bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                                 uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Sched for this kernel counts m tiles of 2 x BM rows; the grid is
+// 2 x (number of clusters) with cluster dimension (2, 1, 1).
+template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS>
+__global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
+                     const __grid_constant__ CUtensorMap tma_b, Sched sched,
+                     typename Epi::Params ep, int* err) {
+  static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
+  static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+  constexpr int BNH = BN / 2;  // B rows held by each CTA
+  using L = SmemLayout<BNH, STAGES, EPI_WARPS>;
+  constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;
+  constexpr uint32_t kIdesc = idesc_bf16(BN, A_MN, B_MN, 2 * BM);
+  constexpr uint32_t kPairBytes = 2u * L::kStageBytes;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::kBarOff;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMiscOff + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int cluster = blockIdx.x >> 1;
+  const int n_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 2 * EPI_WARPS);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    // both CTAs' warp 1 take part; the address lands at the same offset in each
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const int n_units = sched.units();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer ----
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = cluster; u < n_units && ok; u += n_clusters) {
+        int mt, nt, ks, kb0, kb1;
+        sched.decode(u, mt, nt, ks);
+        sched.k_range(ks, kb0, kb1);
+        const int a_row = mt * 2 * BM + static_cast<int>(rank) * BM;
+        const int b_row = nt * BN + static_cast<int>(rank) * BNH;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!bounded_wait(empty_bar(s), ph ^ 1u, abort_flag, err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t a_dst = sbase + s * L::kStageBytes;
+          const uint32_t b_dst = a_dst + L::kABytes;
+          const uint32_t fb = cluster_addr(full_bar(s), 0);
+          if (rank == 0) mbar_arrive_expect_tx(full_bar(s), kPairBytes);
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d_pair(a_dst + j * 8192, &tma_a, fb, a_row + j * 64, k0);
+          } else {
+            tma_load_2d_pair(a_dst, &tma_a, fb, k0, a_row);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BNH / 64; ++j)
+              tma_load_2d_pair(b_dst + j * 8192, &tma_b, fb, b_row + j * 64, k0);
+          } else {
+            tma_load_2d_pair(b_dst, &tma_b, fb, k0, b_row);
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        // both CTAs' copies complete on rank 0's full barriers: wait for the
+        // last min(it, STAGES) stages (bounded) before leaving
+        int n = it < (uint32_t)STAGES ? (int)it : STAGES;
+        for (int i = 1; i <= n; ++i) {
+          uint32_t j = it - i;
+          uint32_t bar = full_bar(j % STAGES), ph = (j / STAGES) & 1u;
+          uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(bar, ph) && globaltimer() - t0 < kWaitNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ----------------------------------------- MMA issuer (rank 0) ----
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int u = cluster; u < n_units && ok; u += n_clusters, ++lt) {
+        int mt, nt, ks, kb0, kb1;
+        sched.decode(u, mt, nt, ks);
+        sched.k_range(ks, kb0, kb1);
+        const uint32_t acc = lt & 1u;
+        const uint32_t acc_ph = (lt >> 1) & 1u;
+        if (!bounded_wait<true>(tempty_bar(acc), acc_ph ^ 1u, abort_flag, err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!bounded_wait<true>(full_bar(s), ph, abort_flag, err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sbase + s * L::kStageBytes;
+          const uint32_t b_addr = a_addr + L::kABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t ad, bd;
+            if (A_MN) ad = smem_desc_sw128(a_addr + k * 2048, 8192, 1024);
+            else ad = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            if (B_MN) bd = smem_desc_sw128(b_addr + k * 2048, 8192, 1024);
+            else bd = smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            tc_mma_bf16_pair(tmem_d, ad, bd, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          issued = true;
+          // stage s of both CTAs is free once these MMAs finish
+          tc_commit_pair(cluster_addr(empty_bar(s), 0));
+          tc_commit_pair(cluster_addr(empty_bar(s), 1));
+        }
+        if (!ok) break;
+        tc_commit_pair(cluster_addr(tfull_bar(acc), 0));
+        tc_commit_pair(cluster_addr(tfull_bar(acc), 1));
+      }
+      if (!ok && issued) {
+        tc_commit_pair(cluster_addr(drain_bar, 0));
+        uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain_bar, 0) && globaltimer() - t0 < kWaitNs) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------ epilogue ----
+    const int quarter = warp & 3;
+    const int e = warp - 2;
+    constexpr int kGroups = EPI_WARPS / 4;
+    const int group = e >> 2;
+    uint8_t* stage = smem + L::kEpiOff + e * kEpiWarpBytes;
+    uint32_t lt = 0;
+    for (int u = cluster; u < n_units; u += n_clusters, ++lt) {
+      int mt, nt, ks;
+      sched.decode(u, mt, nt, ks);
+      const uint32_t acc = lt & 1u;
+      const uint32_t acc_ph = (lt >> 1) & 1u;
+      bool ok = true;
+      if (lane == 0) ok = bounded_wait(tfull_bar(acc), acc_ph, abort_flag, err, kErrWaitEpilogue);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
+      Epi::tile(ep, mt * 2 * BM + static_cast<int>(rank) * BM, nt, ks, quarter, lane, taddr, stage,
+                group, kGroups);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(tempty_bar(acc), 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(kTmemCols)
                  : "memory");
   }

@@ -72,3 +72,58 @@ def test_gemm_leading_dimension_padding():
     run_gemm(A, 0, B, 0, m, n, k, c=c)
     ref = A.float() @ B.float().t()
     assert (c - ref).abs().max().item() / ref.abs().max().item() < 1e-5
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("m,n,k", [(64, 128, 64), (104, 136, 128), (136, 256, 64), (264, 384, 320)])
+def test_gemm_pair_tile_edges(a_mn, b_mn, m, n, k):
+    # a 256-row tile split over two CTAs: the second CTA's rows (m <= 128) or
+    # its half of the B columns (n <= 128) may lie wholly outside the matrix
+    a, b, ref = operands(m, n, k, a_mn, b_mn, seed=11)
+    c = run_gemm(a, a_mn, b, b_mn, m, n, k)
+    err = (c - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-5, err
+
+
+def test_gemm_many_tiles_mn_major():
+    m, n, k = 3000, 2048, 448
+    a, b, ref = operands(m, n, k, 1, 1, seed=13)
+    c = run_gemm(a, 1, b, 1, m, n, k)
+    err = (c - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-5, err
+
+
+_SINGLE_CTA_SCRIPT = r"""
+import torch
+from auspex_soup_demo_b200 import _lib
+torch.manual_seed(0)
+for (m, n, k, a_mn, b_mn) in [(200, 328, 192, 0, 0), (1000, 1536, 704, 0, 1), (384, 512, 256, 1, 1)]:
+    A = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    B = torch.randn(n, k, device="cuda").to(torch.bfloat16)
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    c = torch.zeros(m, n, device="cuda")
+    _lib.call("soup_gemm_bf16", a.device, a.data_ptr(), a.stride(0), a_mn, b.data_ptr(),
+              b.stride(0), b_mn, c.data_ptr(), c.stride(0), _lib.dtype_code(c.dtype), m, n, k,
+              1.0, 0, _lib.stream_of(c))
+    torch.cuda.synchronize()
+    assert _lib.device_error(a.device) == 0
+    ref = A.float() @ B.float().t()
+    err = (c - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 1e-5, (m, n, k, a_mn, b_mn, err)
+print("single-cta ok")
+"""
+
+
+def test_gemm_single_cta_mode():
+    # SOUP_GEMM_PAIRS=0 selects the 128-row single-CTA kernel (read once per process)
+    import os
+    import subprocess
+    import sys
+
+    env = dict(os.environ, SOUP_GEMM_PAIRS="0")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _SINGLE_CTA_SCRIPT], env=env, cwd=root,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "single-cta ok" in r.stdout

@@ -325,6 +325,12 @@ class QLoRATrainer:
         self.graph.replay()
         return self.static_loss, self.static_correct
 
+    def save_adapter(self, directory: str, base_model_name_or_path: str = "Qwen/Qwen2.5-1.5B-Instruct"):
+        """Write the LoRA factors as a PEFT adapter directory (see ``adapter.save_adapter``)."""
+        from .adapter import save_adapter
+
+        return save_adapter(self.model, directory, base_model_name_or_path)
+
     def release_graph(self):
         """Drop the captured graph (do this before destroying the process group)."""
         self.graph = None

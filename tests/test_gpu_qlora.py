@@ -139,3 +139,28 @@ def test_qlora_trainer_reduces_loss():
     den = float((labels != -100).sum())
     losses = [float(trainer.step(ids, labels, den)[0]) for _ in range(8)]
     assert losses[-1] < losses[0] - 0.05, losses
+
+
+def test_trained_adapter_saves_and_reloads_as_peft(tmp_path):
+    from auspex_soup_demo_b200 import adapter
+
+    apply()
+    model = _small_model(seed=2)
+    trainer = qlora.QLoRATrainer(model, lr=2e-3)
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, 2048, (2, 64), generator=g).cuda()
+    labels = qlora.causal_labels(ids)
+    den = float((labels != -100).sum())
+    for _ in range(3):
+        trainer.step(ids, labels, den)
+    out = trainer.save_adapter(str(tmp_path / "adapter"))
+    listing = adapter.header_listing(str(tmp_path / "adapter" / "adapter_model.safetensors"))
+    assert len(listing) == 2 * 7 * 2 and all(v[0] == "F32" for v in listing.values())
+    fresh = _small_model(seed=2)  # same NF4 base, different (perturbed) LoRA B
+    adapter.load_adapter(fresh, out)
+    model.eval()
+    fresh.eval()
+    with torch.no_grad():
+        a = model(input_ids=ids).logits
+        b = fresh(input_ids=ids).logits
+    assert torch.equal(a, b)

@@ -445,8 +445,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
 // Cross-CTA protocol (all waits bounded as in the 1-CTA kernel):
 //   full[s]   rank 0's barrier only: rank 0 arms it with both CTAs' bytes;
 //             both CTAs' TMA copies (cta_group::2) complete on it
-//   empty[s]  one per CTA: rank 0's MMA completion commits to both
-//   tfull[a]  one per CTA: rank 0 commits to both after a tile's last MMA
+//   empty[s]  one per CTA: rank 0's MMA completion arrives on both (one
+//             commit with a two-CTA mask)
+//   tfull[a]  one per CTA: the same, after a tile's last MMA
 //   tempty[a] rank 0's only, count 2 x EPI_WARPS: every epilogue warp of both
 //             CTAs arrives (rank 1 remotely) after draining its TMEM lanes
 // A cluster barrier after set-up and before TMEM release keeps each CTA's
@@ -483,6 +484,13 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
 __device__ __forceinline__ void tc_commit_pair(uint32_t cluster_bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    cluster_bar)
+               : "memory");
+}
+// One commit that arrives on the barrier at offset `bar` in every CTA of
+// `cta_mask` (both CTAs of the pair: 0b11). A second, separate commit per
+// k-block costs about 10% of tensor throughput; this form does not.
+__device__ __forceinline__ void tc_commit_pair_both(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar), "h"((uint16_t)0x3)
                : "memory");
 }
 __device__ __forceinline__ void tc_mma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -650,12 +658,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
           }
           issued = true;
           // stage s of both CTAs is free once these MMAs finish
-          tc_commit_pair(cluster_addr(empty_bar(s), 0));
-          tc_commit_pair(cluster_addr(empty_bar(s), 1));
+          tc_commit_pair_both(empty_bar(s));
         }
         if (!ok) break;
-        tc_commit_pair(cluster_addr(tfull_bar(acc), 0));
-        tc_commit_pair(cluster_addr(tfull_bar(acc), 1));
+        tc_commit_pair_both(tfull_bar(acc));
       }
       if (!ok && issued) {
         tc_commit_pair(cluster_addr(drain_bar, 0));

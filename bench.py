@@ -316,7 +316,8 @@ def run_b200(args):
     peak_tf, peak_hbm, peak_src = _peaks()
     gemm_ms = [st[0], st[3], st[5]]
     achieved = FLOP_PER_GEMM / (statistics.mean(gemm_ms) * 1e-3) / 1e12
-    traffic = _committed_traffic()
+    pairs = os.environ.get("SOUP_GEMM_PAIRS", "1") != "0"
+    traffic = _committed_traffic("gemm_pair_kernel" if pairs else "gemm_kernel")
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
@@ -332,7 +333,8 @@ def run_b200(args):
                 "api": "make_triton_chunked_loss_function().apply + backward (head weight trainable)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak_tf,
                      "unit": "TFLOP/s", "frac": round(achieved / peak_tf, 4), "traffic": traffic,
-                     "kernel": "soup::tc::gemm_kernel (logits / dX / dW launches, 2*N*V*D each)",
+                     "kernel": ("soup::tc::gemm_pair_kernel" if pairs else "soup::tc::gemm_kernel")
+                     + " (logits / dX / dW launches, 2*N*V*D each)",
                      "peak_source": f"{peak_src} bf16_tflops (burst)"},
         "stages_ms": {"logits_gemm": round(st[0], 4), "finalize": round(st[1], 4),
                       "sums": round(st[2], 4), "dx_gemm": round(st[3], 4),
@@ -657,12 +659,12 @@ def run_ce_vp(args):
         dist.destroy_process_group()
 
 
-def _committed_traffic():
-    """DRAM bytes per launch of the logits GEMM from the committed ncu summary, if any."""
+def _committed_traffic(kernel):
+    """Mean DRAM bytes per GEMM launch of `kernel` from the committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get("gemm_kernel_bytes_per_launch")
+            return json.load(f).get(f"{kernel}_bytes_per_launch")
     except Exception:
         return None
 

@@ -391,16 +391,14 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched
 }
 
 // ------------------------------------------------------ CE row kernels -----
-// Per row: merge the tile states, metrics, then dlogits in place.
-__global__ void __launch_bounds__(512) ce_finalize_kernel(
-    const float4* __restrict__ partials, int n_tiles, const float* __restrict__ zt,
+// One row: merge the tile states, metrics, then dlogits in place. Every
+// thread of the block takes part (block-uniform control flow).
+__device__ __forceinline__ void ce_finalize_row(
+    int row, const float4* __restrict__ partials, int n_tiles, const float* __restrict__ zt,
     const int64_t* __restrict__ targets, bf16* __restrict__ logits, int64_t ld_logits, int rows,
     int vocab, float inv_den, int64_t ignore_index, float* __restrict__ losses,
-    float* __restrict__ entropies, int32_t* __restrict__ correct, int write_grad) {
-  const int row = blockIdx.x;
-  if (row >= rows) return;
-  __shared__ SoftmaxState red[16];
-  __shared__ float s_lse;
+    float* __restrict__ entropies, int32_t* __restrict__ correct, int write_grad,
+    SoftmaxState* red, float* s_lse) {
   SoftmaxState st = sm_init();
   for (int j = threadIdx.x; j < n_tiles; j += blockDim.x) {
     float4 p = partials[(int64_t)j * rows + row];
@@ -428,7 +426,7 @@ __global__ void __launch_bounds__(512) ce_finalize_kernel(
     losses[row] = loss;
     entropies[row] = ent;
     correct[row] = (!ignored && in_range && r.idx == static_cast<int>(t)) ? 1 : 0;
-    s_lse = lse;
+    *s_lse = lse;
   }
   if (!write_grad) return;
   __syncthreads();
@@ -441,7 +439,7 @@ __global__ void __launch_bounds__(512) ce_finalize_kernel(
     for (int c = nvec * 8 + threadIdx.x; c < vocab; c += blockDim.x) lrow[c] = __float2bfloat16_rn(0.f);
     return;
   }
-  const float lb = s_lse * kLog2e;
+  const float lb = *s_lse * kLog2e;
   for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
     Vec16<bf16> z = ld16(lrow + i * 8);
     Vec16<bf16> o;
@@ -457,6 +455,23 @@ __global__ void __launch_bounds__(512) ce_finalize_kernel(
     float p = fast_exp2(fmaf(__bfloat162float(lrow[c]), kLog2e, -lb));
     if (c == t) p -= 1.f;
     lrow[c] = __float2bfloat16_rn(p * inv_den);
+  }
+}
+
+// Rows [row0, row_end): block b takes rows row0 + b, row0 + b + gridDim.x, ...
+// `rows` is the partial records' row stride (all rows of the call).
+__global__ void __launch_bounds__(512) ce_finalize_kernel(
+    const float4* __restrict__ partials, int n_tiles, const float* __restrict__ zt,
+    const int64_t* __restrict__ targets, bf16* __restrict__ logits, int64_t ld_logits, int rows,
+    int vocab, float inv_den, int64_t ignore_index, float* __restrict__ losses,
+    float* __restrict__ entropies, int32_t* __restrict__ correct, int write_grad, int row0,
+    int row_end) {
+  __shared__ SoftmaxState red[16];
+  __shared__ float s_lse;
+  for (int row = row0 + blockIdx.x; row < row_end; row += gridDim.x) {
+    ce_finalize_row(row, partials, n_tiles, zt, targets, logits, ld_logits, rows, vocab, inv_den,
+                    ignore_index, losses, entropies, correct, write_grad, red, &s_lse);
+    __syncthreads();  // red / s_lse are rewritten by the next row
   }
 }
 
@@ -622,7 +637,7 @@ struct CEWorkspace {
   int64_t ld_logits;
   int n_vtiles;
   int n_parts;  // online-softmax records per row (vocab tiles x epilogue column groups)
-  int splits;
+  int splits;  // dX vocabulary splits
   size_t off_logits, off_partials, off_zt, off_splitk, total;
 };
 
@@ -786,12 +801,12 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
     if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, sc, ep, stream))) return rc;
     mark_stage(0, stream);
   }
+  const float inv_den = 1.f / (denominator > 0.f ? denominator : 1.f);
   // 2. metrics + dlogits
   {
-    const float den = denominator > 0.f ? denominator : 1.f;
     ce_finalize_kernel<<<M, 512, 0, stream>>>(partials, w.n_parts, zt, targets, L, w.ld_logits, M,
-                                               V, 1.f / den, ignore_index, losses, entropies,
-                                               correct, need_grad ? 1 : 0);
+                                               V, inv_den, ignore_index, losses, entropies,
+                                               correct, need_grad ? 1 : 0, 0, M);
     if ((rc = launch_status())) return rc;
     mark_stage(1, stream);
   }

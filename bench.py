@@ -314,9 +314,10 @@ def run_b200(args):
     assert _lib.device_error(dev) == 0
 
     peak_tf, peak_hbm, peak_src = _peaks()
+    pairs = os.environ.get("SOUP_GEMM_PAIRS", "1") != "0"
     gemm_ms = [st[0], st[3], st[5]]
     achieved = FLOP_PER_GEMM / (statistics.mean(gemm_ms) * 1e-3) / 1e12
-    pairs = os.environ.get("SOUP_GEMM_PAIRS", "1") != "0"
+    stage_names = ["logits_gemm", "finalize", "sums", "dx_gemm", "dx_reduce", "dw_gemm"]
     traffic = _committed_traffic("gemm_pair_kernel" if pairs else "gemm_kernel")
 
     line = {
@@ -336,9 +337,7 @@ def run_b200(args):
                      "kernel": ("soup::tc::gemm_pair_kernel" if pairs else "soup::tc::gemm_kernel")
                      + " (logits / dX / dW launches, 2*N*V*D each)",
                      "peak_source": f"{peak_src} bf16_tflops (burst)"},
-        "stages_ms": {"logits_gemm": round(st[0], 4), "finalize": round(st[1], 4),
-                      "sums": round(st[2], 4), "dx_gemm": round(st[3], 4),
-                      "dx_reduce": round(st[4], 4), "dw_gemm": round(st[5], 4)},
+        "stages_ms": {k: round(v, 4) for k, v in zip(stage_names, st)},
         "gpu_launches": 6 * args.steps,
         "clocks": clocks.summary(),
     }

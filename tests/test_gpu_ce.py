@@ -259,3 +259,8 @@ def test_vocab_parallel_ce_emulated_ranks(world):
     assert abs(float(sums[0]) - float(loss.sum())) <= 1e-4 * float(loss.sum())
     assert cosine(dh, grad @ weight.float()) >= 0.9999
     assert cosine(torch.cat(dws), grad.t() @ hidden.float()) >= 0.9999
+
+
+def test_fused_ce_ragged_rows_over_several_pair_tiles():
+    # 700 rows: two full 256-row pair tiles and a ragged third
+    _check_fused(700, 8192, 256, seed=8)

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 import oracle.nf4 as onf4
-from auspex_soup_demo_b200 import apply, qlora
+from auspex_soup_demo_b200 import _lib, apply, qlora
 from helpers import cosine
 
 pytestmark = pytest.mark.gpu
@@ -164,3 +164,47 @@ def test_trained_adapter_saves_and_reloads_as_peft(tmp_path):
         a = model(input_ids=ids).logits
         b = fresh(input_ids=ids).logits
     assert torch.equal(a, b)
+
+
+def test_captured_step_matches_eager_steps():
+    # the whole train step (fused ops, head CE, backward, AdamW) recorded as one CUDA
+    # graph and replayed on new batches
+    apply()
+    g = torch.Generator().manual_seed(6)
+    batches = [torch.randint(0, 2048, (2, 256), generator=g).cuda() for _ in range(3)]
+    labels = [qlora.causal_labels(b) for b in batches]
+    den = float((labels[0] != -100).sum())
+
+    eager = qlora.QLoRATrainer(_small_model(seed=3), lr=1e-3)
+    ref = []
+    for _ in range(4):  # the capture's 3 warm-up steps + the captured step, on batch 0
+        ref.append(float(eager.step(batches[0], labels[0], den)[0]))
+    for b, lab in zip(batches[1:], labels[1:]):
+        ref.append(float(eager.step(b, lab, den)[0]))
+
+    graphed = qlora.QLoRATrainer(_small_model(seed=3), lr=1e-3)
+    init = {n: p.detach().clone() for n, p in graphed.model.named_parameters() if p.requires_grad}
+    ids = batches[0].clone()
+    lab = labels[0].clone()
+    graphed.capture(ids, lab, den, warmup=3)
+    got = []
+    loss, _ = graphed.replay()
+    got.append(float(loss))
+    for b, l2 in zip(batches[1:], labels[1:]):
+        ids.copy_(b)
+        lab.copy_(l2)
+        loss, _ = graphed.replay()
+        got.append(float(loss))
+    torch.cuda.synchronize()
+    graphed.release_graph()
+    assert _lib.device_error(torch.device("cuda")) == 0
+    # Replays follow the eager steps to 1e-4 of the loss (the attention backward's
+    # accumulation order varies between runs and AdamW magnifies it); the batches'
+    # losses differ from one another by ~5e-3, so stale graph inputs would show.
+    for a, b in zip(ref[3:], got):
+        assert abs(a - b) <= 1e-4 * abs(a), (ref[3:], got)
+    assert abs(got[1] - got[2]) > 1e-3, got
+    pa = dict(eager.model.named_parameters())
+    for n, p in graphed.model.named_parameters():
+        if p.requires_grad:  # the 6 updates agree in direction
+            assert cosine(p - init[n], pa[n] - init[n]) > 0.99, n

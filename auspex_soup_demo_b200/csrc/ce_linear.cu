@@ -120,6 +120,7 @@ struct EpiStore {
     int accumulate;
     int vec_ok;  // 16-byte aligned rows
     int M, N;
+    const bf16* bias;  // optional [N] added to every row after scaling
   };
   static __device__ __forceinline__ void tile(const Params& p, int row_base, int nt, int ks,
                                               int quarter, int lane, uint32_t taddr, uint8_t* stage,
@@ -135,7 +136,14 @@ struct EpiStore {
       tmem_ld32(taddr + c * 32, v);
       const int col0 = nt * BN + c * 32;
       if (col0 >= p.N) continue;
-      stage_row(stage, lane, v, a);
+      if (p.bias) {  // every lane reads the same 32 values (broadcast)
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          v[j] = fmaf(a, v[j], col0 + j < p.N ? __bfloat162float(p.bias[col0 + j]) : 0.f);
+        stage_row(stage, lane, v, 1.f);
+      } else {
+        stage_row(stage, lane, v, a);
+      }
       __syncwarp();
       if (p.c_bf16)
         write_block<true>(stage, lane, C, p.ldc, row0, p.M, col0, p.N, p.vec_ok, p.accumulate);
@@ -315,7 +323,8 @@ static int m_tiles(int64_t m) { return static_cast<int>((m + tile_m() - 1) / til
 constexpr int kPairStages = 6;
 
 template <bool A_MN, bool B_MN, class Epi>
-static int launch_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
+static int launch_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma2,
+                              const CUtensorMap& mb2, Sched sched,
                               const typename Epi::Params& ep, cudaStream_t stream, int* err) {
   using L = SmemLayout<kBN, kStages, kEpiWarps>;
   auto kern = gemm_kernel<kBN, kStages, A_MN, B_MN, Epi, kEpiWarps>;
@@ -330,12 +339,13 @@ static int launch_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb, Sche
   }
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
   const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, gemm_threads(kEpiWarps), L::kBytes, stream>>>(ma, mb, sched, ep, err);
+  kern<<<grid, gemm_threads(kEpiWarps), L::kBytes, stream>>>(ma, mb, ma2, mb2, sched, ep, err);
   return launch_status();
 }
 
 template <bool A_MN, bool B_MN, class Epi>
-static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
+static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma2,
+                            const CUtensorMap& mb2, Sched sched,
                             const typename Epi::Params& ep, cudaStream_t stream, int* err) {
   using L = SmemLayout<kBN / 2, kPairStages, kEpiWarps>;
   static_assert(L::kBytes <= 232448, "pair GEMM shared memory exceeds 227 KB");
@@ -372,13 +382,15 @@ static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, Sched 
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
   const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
   cfg.gridDim = dim3(2 * clusters);
-  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mb, sched, ep, err));
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mb, ma2, mb2, sched, ep, err));
 }
 
-// sched.m_tiles counts tile_m() rows.
+// sched.m_tiles counts tile_m() rows. ma2 / mb2 are read for the last
+// sched.kb2 k-blocks (the second K segment).
 template <bool A_MN, bool B_MN, class Epi>
-static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
-                       const typename Epi::Params& ep, cudaStream_t stream) {
+static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma2,
+                       const CUtensorMap& mb2, Sched sched, const typename Epi::Params& ep,
+                       cudaStream_t stream) {
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
   if (units <= 0) return SOUP_OK;
   int* err = device_err_ptr();
@@ -386,8 +398,17 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched
     set_last_error("device error word unavailable");
     return SOUP_ERR_CUDA;
   }
-  if (use_pairs()) return launch_gemm_pair<A_MN, B_MN, Epi>(ma, mb, sched, ep, stream, err);
-  return launch_gemm_single<A_MN, B_MN, Epi>(ma, mb, sched, ep, stream, err);
+  if (use_pairs())
+    return launch_gemm_pair<A_MN, B_MN, Epi>(ma, mb, ma2, mb2, sched, ep, stream, err);
+  return launch_gemm_single<A_MN, B_MN, Epi>(ma, mb, ma2, mb2, sched, ep, stream, err);
+}
+
+// One K segment (sched.kb2 must be 0).
+template <bool A_MN, bool B_MN, class Epi>
+static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
+                       const typename Epi::Params& ep, cudaStream_t stream) {
+  sched.kb2 = 0;
+  return launch_gemm<A_MN, B_MN, Epi>(ma, mb, ma, mb, sched, ep, stream);
 }
 
 // ------------------------------------------------------ CE row kernels -----
@@ -982,7 +1003,16 @@ int soup_set_stage_events(void** events, int n) {
 int soup_gemm_bf16(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb,
                    int b_mn_major, void* c, int64_t ldc, int c_dtype, int64_t m, int64_t n,
                    int64_t k, float alpha, int accumulate, void* stream_) {
-  if (!a || !b || !c || m <= 0 || n <= 0 || k <= 0 || m > (1 << 30) || n > (1 << 30)) {
+  return soup_gemm_bf16_lora(a, lda, a_mn_major, b, ldb, b_mn_major, nullptr, 0, nullptr, 0, 0,
+                             nullptr, c, ldc, c_dtype, m, n, k, alpha, accumulate, stream_);
+}
+
+int soup_gemm_bf16_lora(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb,
+                        int b_mn_major, const void* a2, int64_t lda2, const void* b2, int64_t ldb2,
+                        int64_t r, const void* bias, void* c, int64_t ldc, int c_dtype, int64_t m,
+                        int64_t n, int64_t k, float alpha, int accumulate, void* stream_) {
+  if (!a || !b || !c || m <= 0 || n <= 0 || k <= 0 || m > (1 << 30) || n > (1 << 30) ||
+      k > (1 << 30) || r < 0 || r > 4096 || (r > 0 && (!a2 || !b2))) {
     set_last_error("soup_gemm_bf16: bad arguments");
     return SOUP_ERR_INVALID;
   }
@@ -990,28 +1020,41 @@ int soup_gemm_bf16(const void* a, int64_t lda, int a_mn_major, const void* b, in
     set_last_error("soup_gemm_bf16: C dtype must be F32 or BF16");
     return SOUP_ERR_INVALID;
   }
-  if ((a_mn_major ? lda < m : lda < k) || (b_mn_major ? ldb < n : ldb < k) || ldc < n) {
+  if ((a_mn_major ? lda < m : lda < k) || (b_mn_major ? ldb < n : ldb < k) || ldc < n ||
+      (r > 0 && ((a_mn_major ? lda2 < m : lda2 < r) || (b_mn_major ? ldb2 < n : ldb2 < r)))) {
     set_last_error("soup_gemm_bf16: leading dimension too small");
     return SOUP_ERR_INVALID;
   }
-  if (!tma_ok(a, lda) || !tma_ok(b, ldb)) {
+  if (!tma_ok(a, lda) || !tma_ok(b, ldb) || (r > 0 && (!tma_ok(a2, lda2) || !tma_ok(b2, ldb2)))) {
     set_last_error("soup_gemm_bf16: operands need 16-byte aligned rows");
     return SOUP_ERR_UNSUPPORTED;
   }
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, ma2, mb2;
   int rc;
   if ((rc = make_operand_map(&ma, a, a_mn_major != 0, m, k, lda, BM))) return rc;
   if ((rc = make_operand_map(&mb, b, b_mn_major != 0, n, k, ldb, b_box_rows()))) return rc;
+  if (r > 0) {
+    // the rank-r segment: boxes are 64 deep along K; TMA fills the columns
+    // (K-major) or rows (MN-major) beyond r with zeros
+    if ((rc = make_operand_map(&ma2, a2, a_mn_major != 0, m, r, lda2, BM))) return rc;
+    if ((rc = make_operand_map(&mb2, b2, b_mn_major != 0, n, r, ldb2, b_box_rows()))) return rc;
+  } else {
+    ma2 = ma;
+    mb2 = mb;
+  }
   const int es = c_dtype == SOUP_BF16 ? 2 : 4;
   EpiStore<kBN>::Params ep{c, ldc, 0, nullptr, alpha, c_dtype == SOUP_BF16 ? 1 : 0, accumulate ? 1 : 0,
-                           (aligned16(c) && (ldc * es) % 16 == 0) ? 1 : 0, (int)m, (int)n};
+                           (aligned16(c) && (ldc * es) % 16 == 0) ? 1 : 0, (int)m, (int)n,
+                           static_cast<const bf16*>(bias)};
   const int mt = m_tiles(m), nt = (int)((n + kBN - 1) / kBN);
-  Sched sc{mt, nt, 1, (int)((k + BK - 1) / BK), nt > mt ? 0 : 1};
+  const int kb1 = (int)((k + BK - 1) / BK), kb2 = (int)((r + BK - 1) / BK);
+  Sched sc{mt, nt, 1, kb1 + kb2, nt > mt ? 0 : 1, kb2};
   cudaStream_t stream = as_stream(stream_);
-  if (!a_mn_major && !b_mn_major) return launch_gemm<false, false, EpiStore<kBN>>(ma, mb, sc, ep, stream);
-  if (!a_mn_major && b_mn_major) return launch_gemm<false, true, EpiStore<kBN>>(ma, mb, sc, ep, stream);
-  if (a_mn_major && !b_mn_major) return launch_gemm<true, false, EpiStore<kBN>>(ma, mb, sc, ep, stream);
-  return launch_gemm<true, true, EpiStore<kBN>>(ma, mb, sc, ep, stream);
+  using E = EpiStore<kBN>;
+  if (!a_mn_major && !b_mn_major) return launch_gemm<false, false, E>(ma, mb, ma2, mb2, sc, ep, stream);
+  if (!a_mn_major && b_mn_major) return launch_gemm<false, true, E>(ma, mb, ma2, mb2, sc, ep, stream);
+  if (a_mn_major && !b_mn_major) return launch_gemm<true, false, E>(ma, mb, ma2, mb2, sc, ep, stream);
+  return launch_gemm<true, true, E>(ma, mb, ma2, mb2, sc, ep, stream);
 }
 
 }  // extern "C"

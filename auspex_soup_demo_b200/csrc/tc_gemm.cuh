@@ -1,7 +1,13 @@
 // Persistent, warp-specialised bf16 GEMM for sm_100a on the 5th-generation
 // tensor cores (tcgen05.mma, accumulators in TMEM, operands staged by TMA).
 //
-//   C[m, n] = sum_k A(m, k) * B(n, k)
+//   C[m, n] = sum_k A(m, k) * B(n, k)  [+ sum_k2 A2(m, k2) * B2(n, k2)]
+//
+// The optional second K segment (Sched::kb2 > 0 blocks, read through the
+// tensor maps tma_a2 / tma_b2 with the same majorness as A / B) follows the
+// first in the same accumulator: a low-rank update such as a LoRA term
+// x A^T B^T rides on the base GEMM as one or two extra k-blocks, its columns
+// beyond the rank zero-filled by TMA (out-of-bounds box elements).
 //
 // A and B are each either K-major (stored [rows, K], K contiguous) or
 // MN-major (stored [K, rows], rows contiguous); both are loaded by 2-D TMA
@@ -169,8 +175,14 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int bn, bool a_mn, bool b_mn, 
 // The k split is the slowest index so concurrently running units share k.
 struct Sched {
   int m_tiles, n_tiles, splits;
-  int kb_total;  // number of BK blocks along K
+  int kb_total;  // number of BK blocks along K (both segments)
   int order;
+  int kb2;       // trailing blocks of kb_total read from the second segment (0: none)
+  // maps and k offset of block kb
+  __device__ __forceinline__ bool second(int kb) const { return kb >= kb_total - kb2; }
+  __device__ __forceinline__ int k_elem(int kb) const {
+    return (second(kb) ? kb - (kb_total - kb2) : kb) * BK;
+  }
   __device__ __forceinline__ int units() const { return m_tiles * n_tiles * splits; }
   __device__ __forceinline__ void decode(int u, int& mt, int& nt, int& ks) const {
     int mn = m_tiles * n_tiles;
@@ -245,7 +257,9 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity,
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS>
 __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                Sched sched, typename Epi::Params ep, int* err) {
+                const __grid_constant__ CUtensorMap tma_a2,
+                const __grid_constant__ CUtensorMap tma_b2, Sched sched,
+                typename Epi::Params ep, int* err) {
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
   using L = SmemLayout<BN, STAGES, EPI_WARPS>;
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, multiple of 64");
@@ -284,6 +298,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
+    if (sched.kb2 > 0) {
+      tma_prefetch_desc(&tma_a2);
+      tma_prefetch_desc(&tma_b2);
+    }
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -317,20 +335,23 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
           const uint32_t a_dst = sbase + s * L::kStageBytes;
           const uint32_t b_dst = a_dst + L::kABytes;
           mbar_arrive_expect_tx(full_bar(s), L::kStageBytes);
-          const int k0 = kb * BK;
+          const int k0 = sched.k_elem(kb);
+          const bool seg2 = sched.second(kb);
+          const CUtensorMap* ma = seg2 ? &tma_a2 : &tma_a;
+          const CUtensorMap* mb = seg2 ? &tma_b2 : &tma_b;
           if (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j)
-              tma_load_2d(a_dst + j * 8192, &tma_a, full_bar(s), mt * BM + j * 64, k0);
+              tma_load_2d(a_dst + j * 8192, ma, full_bar(s), mt * BM + j * 64, k0);
           } else {
-            tma_load_2d(a_dst, &tma_a, full_bar(s), k0, mt * BM);
+            tma_load_2d(a_dst, ma, full_bar(s), k0, mt * BM);
           }
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(b_dst + j * 8192, &tma_b, full_bar(s), nt * BN + j * 64, k0);
+              tma_load_2d(b_dst + j * 8192, mb, full_bar(s), nt * BN + j * 64, k0);
           } else {
-            tma_load_2d(b_dst, &tma_b, full_bar(s), k0, nt * BN);
+            tma_load_2d(b_dst, mb, full_bar(s), k0, nt * BN);
           }
         }
       }
@@ -508,7 +529,9 @@ __device__ __forceinline__ void tc_mma_bf16_pair(uint32_t tmem_d, uint64_t adesc
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS>
 __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
-                     const __grid_constant__ CUtensorMap tma_b, Sched sched,
+                     const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ CUtensorMap tma_a2,
+                     const __grid_constant__ CUtensorMap tma_b2, Sched sched,
                      typename Epi::Params ep, int* err) {
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
   static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
@@ -552,6 +575,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
+    if (sched.kb2 > 0) {
+      tma_prefetch_desc(&tma_a2);
+      tma_prefetch_desc(&tma_b2);
+    }
   }
   if (warp == 1) {
     // both CTAs' warp 1 take part; the address lands at the same offset in each
@@ -589,20 +616,23 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
           const uint32_t b_dst = a_dst + L::kABytes;
           const uint32_t fb = cluster_addr(full_bar(s), 0);
           if (rank == 0) mbar_arrive_expect_tx(full_bar(s), kPairBytes);
-          const int k0 = kb * BK;
+          const int k0 = sched.k_elem(kb);
+          const bool seg2 = sched.second(kb);
+          const CUtensorMap* ma = seg2 ? &tma_a2 : &tma_a;
+          const CUtensorMap* mb = seg2 ? &tma_b2 : &tma_b;
           if (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j)
-              tma_load_2d_pair(a_dst + j * 8192, &tma_a, fb, a_row + j * 64, k0);
+              tma_load_2d_pair(a_dst + j * 8192, ma, fb, a_row + j * 64, k0);
           } else {
-            tma_load_2d_pair(a_dst, &tma_a, fb, k0, a_row);
+            tma_load_2d_pair(a_dst, ma, fb, k0, a_row);
           }
           if (B_MN) {
 #pragma unroll
             for (int j = 0; j < BNH / 64; ++j)
-              tma_load_2d_pair(b_dst + j * 8192, &tma_b, fb, b_row + j * 64, k0);
+              tma_load_2d_pair(b_dst + j * 8192, mb, fb, b_row + j * 64, k0);
           } else {
-            tma_load_2d_pair(b_dst, &tma_b, fb, k0, b_row);
+            tma_load_2d_pair(b_dst, mb, fb, k0, b_row);
           }
         }
       }

@@ -9,15 +9,18 @@ step that surround the fused ops:
 * :class:`LoRANF4Linear` - a frozen NF4 base weight (blocksize 64, our CUDA
   quantiser/dequantiser) plus trainable LoRA factors; the base weight is
   dequantised to bf16 for each use (forward and backward) and never stored;
+  base product and LoRA term are one tcgen05 GEMM whose last k-block is the
+  rank-16 term (soup_gemm_bf16_lora), and the LoRA gradients accumulate
+  straight into fp32 buffers;
 * :func:`build_qwen2_qlora` - the Qwen2.5-1.5B architecture (28 layers, hidden
   1536, MLP 8960, 12 query / 2 KV heads of 128, vocab 151936, tied embeddings,
   rope theta 1e6) randomly initialised (N(0, 0.02)) with LoRA on
   q/k/v/o/gate/up/down;
 * :class:`QLoRATrainer` - one optimiser step: transformer body (with the fused
   RMSNorm / RoPE / SwiGLU patches), fused head cross-entropy, backward, AdamW.
-  With ``torch.distributed`` initialised (one process per GPU, NCCL), the body
-  is wrapped in DistributedDataParallel: only the LoRA gradients exist, so only
-  they are all-reduced, in buckets overlapped with the backward pass.
+  With ``torch.distributed`` initialised (one process per GPU, NCCL), only the
+  LoRA gradients exist, and they are averaged over ranks by one all-reduce of
+  their flat buffer after the backward pass.
 """
 
 from __future__ import annotations
@@ -83,93 +86,183 @@ def nf4_dequantize(packed: torch.Tensor, absmax: torch.Tensor, shape, dtype=torc
     return out
 
 
-class _NF4LinearFn(torch.autograd.Function):
-    """y = x W^T + b with W dequantised from NF4 on each use; W is frozen."""
+def _accumulate_grad(param: torch.Tensor, m1: torch.Tensor, m2: torch.Tensor, alpha: float):
+    """param.grad += alpha * m1 @ m2, in place when the gradient is an fp32 CUDA
+    buffer and the factors are 16-bit (cuBLAS accumulates the bf16 product into
+    the fp32 gradient; no cast or add kernels). Returns None in that case, else
+    the gradient for autograd to accumulate."""
+    g = param.grad
+    if (g is not None and g.is_cuda and g.dtype == torch.float32 and m1.dtype in (torch.bfloat16, torch.float16)
+            and g.is_contiguous()):
+        torch.addmm(g, m1, m2, alpha=alpha, out_dtype=torch.float32, out=g)
+        return None
+    return (alpha * (m1.float() @ m2.float())).to(param.dtype)
+
+
+# Contractions longer than this stay on cuBLAS plus an accumulating rank-r
+# GEMM: measured on B200 at 2048 and 8192 tokens, the one-GEMM tcgen05 path
+# wins for every Qwen2.5-1.5B projection with K = 1536 (q/k/v/o, gate/up
+# forward, down backward) and loses for K = 8960 (down forward, gate/up
+# backward), where the output is narrow, the extra pass over it cheap, and
+# the persistent kernel's last wave of 256 x 256 tiles mostly idle.
+FUSED_MAX_K = 4096
+
+
+def _fused_ok(k: int, *ts: torch.Tensor) -> bool:
+    if k > FUSED_MAX_K:
+        return False
+    for t in ts:
+        if t is None:
+            continue
+        if (not t.is_cuda or t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1
+                or t.stride(0) % 8 or t.data_ptr() % 16):
+            return False
+    return True
+
+
+def lora_gemm(a: torch.Tensor, b: torch.Tensor, b_mn_major: bool, a2: torch.Tensor, b2: torch.Tensor,
+              out: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[M, N] = a @ op(b) + a2 @ op(b2) (+ bias) in one tcgen05 GEMM (soup_gemm_bf16_lora).
+
+    a [M, K] and a2 [M, r] are row-major; op(b) is b^T for b [N, K]
+    (b_mn_major False) or b for b [K, N] (True), and op(b2) likewise for b2
+    [N, r] / [r, N]. The rank-r term is the GEMM's last k-block(s).
+    """
+    m, k = a.shape
+    n = out.shape[1]
+    r = a2.shape[1]
+    _lib.call("soup_gemm_bf16_lora", a.device, a.data_ptr(), a.stride(0), 0, b.data_ptr(), b.stride(0),
+              int(b_mn_major), a2.data_ptr(), a2.stride(0), b2.data_ptr(), b2.stride(0), r,
+              None if bias is None else bias.data_ptr(), out.data_ptr(), out.stride(0),
+              _lib.dtype_code(out.dtype), m, n, k, 1.0, 0, _lib.stream_of(a))
+    return out
+
+
+class _LoRALinearFn(torch.autograd.Function):
+    """y = x W^T (+ b) + (x As^T) B^T for a frozen base weight W and LoRA factors
+    A [r, in], B [out, r], with As = s A (s = alpha / r).
+
+    ``weight_fn(dtype)`` returns W [out, in] (dequantised from NF4 for each use,
+    never stored); ``As16`` and ``B16`` are As and B in the activation dtype.
+    Forward: xa = x As^T (a rank-r GEMM), then y = x W^T + xa B^T (+ b) as ONE
+    tcgen05 GEMM whose last k-block is the rank-r term (lora_gemm) when the
+    output is large enough, else cuBLAS plus an accumulating rank-r GEMM.
+    Backward: dxa = dy B, dx = dy W + dxa As (again one GEMM with a rank-r
+    k-block), dA += s dxa^T x and dB += dy^T xa straight into fp32 gradient
+    buffers when the parameters have them (see _accumulate_grad).
+    """
 
     @staticmethod
-    def forward(ctx, x, packed, absmax, bias, out_features, in_features):
-        w = nf4_dequantize(packed, absmax, (out_features, in_features), dtype=x.dtype)
-        y = F.linear(x, w, bias)
-        ctx.save_for_backward(packed, absmax)
-        ctx.shape = (out_features, in_features)
+    def forward(ctx, x, A, B, As16, B16, scaling, weight_fn, bias):
+        w = weight_fn(x.dtype)
+        x2 = x.reshape(-1, x.shape[-1])
+        xa = x2 @ As16.t()
+        m, n = x2.shape[0], w.shape[0]
+        if _fused_ok(x2.shape[1], x2, w, xa, B16, bias.view(1, -1) if bias is not None else None):
+            y2 = lora_gemm(x2, w, False, xa, B16, torch.empty(m, n, device=x.device, dtype=x.dtype), bias)
+            y = y2.view(*x.shape[:-1], n)
+        else:
+            y = F.linear(x, w, bias)
+            y.view(-1, n).addmm_(xa, B16.t())
+        ctx.save_for_backward(x, xa, As16, B16)
+        ctx.params = (A, B)
+        ctx.scaling = scaling
+        ctx.weight_fn = weight_fn
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        packed, absmax = ctx.saved_tensors
-        dx = None
+        x, xa, As16, B16 = ctx.saved_tensors
+        A, B = ctx.params
+        s = ctx.scaling
+        dy2 = dy.reshape(-1, dy.shape[-1])
+        if dy2.stride(1) != 1:
+            dy2 = dy2.contiguous()
+        x2 = x.reshape(-1, x.shape[-1])
+        dxa = dy2 @ B16
+        dx = gA = gB = None
         if ctx.needs_input_grad[0]:
-            w = nf4_dequantize(packed, absmax, ctx.shape, dtype=dy.dtype)
-            dx = dy @ w
-        return dx, None, None, None, None, None
+            w = ctx.weight_fn(dy.dtype)
+            m, n = dy2.shape[0], w.shape[1]
+            if _fused_ok(dy2.shape[1], dy2, w, dxa, As16):
+                dx2 = lora_gemm(dy2, w, True, dxa, As16, torch.empty(m, n, device=dy.device, dtype=dy.dtype))
+            else:
+                dx2 = dy2 @ w
+                dx2.addmm_(dxa, As16)
+            dx = dx2.view(x.shape)
+        if ctx.needs_input_grad[1]:
+            gA = _accumulate_grad(A, dxa.t(), x2, s)
+        if ctx.needs_input_grad[2]:
+            gB = _accumulate_grad(B, dy2.t(), xa, 1.0)
+        return dx, gA, gB, None, None, None, None, None
 
 
-def _add_lora(y: torch.Tensor, x: torch.Tensor, lora_a: torch.Tensor, lora_b: torch.Tensor,
-              scaling: float) -> torch.Tensor:
-    """y + scaling * (x A^T) B^T with the addition done by the GEMM (beta = 1).
+class _LoRABase(torch.nn.Module):
+    """Trainable LoRA factors (fp32) beside a frozen base weight.
 
-    The scale is folded into the [out, r] factor and the rank-r product is
-    accumulated onto y by one addmm, so no pass over the [tokens, out]
-    activations is spent on scaling or adding.
+    ``lora_As16`` / ``lora_B16`` may be set to 16-bit copies of (alpha/r) * A
+    and of B that the owner refreshes after every optimiser step
+    (QLoRATrainer keeps them in one buffer and refreshes them with two
+    kernels per step); without them the factors are cast on each use.
     """
-    xa = F.linear(x, lora_a.to(x.dtype))
-    b = (lora_b * scaling).to(x.dtype)
-    out = torch.addmm(y.reshape(-1, y.shape[-1]), xa.reshape(-1, xa.shape[-1]), b.t())
-    return out.view(y.shape)
+
+    def _init_lora(self, linear: torch.nn.Linear, r: int, alpha: int, lora_dtype: torch.dtype):
+        self.in_features = linear.in_features
+        self.out_features = linear.out_features
+        if linear.bias is not None:
+            self.register_buffer("bias", linear.bias.detach().clone())
+        else:
+            self.bias = None
+        dev = linear.weight.device
+        self.lora_A = torch.nn.Parameter(torch.empty(r, self.in_features, device=dev, dtype=lora_dtype))
+        self.lora_B = torch.nn.Parameter(torch.zeros(self.out_features, r, device=dev, dtype=lora_dtype))
+        torch.nn.init.kaiming_uniform_(self.lora_A, a=math.sqrt(5))
+        self.scaling = alpha / r
+        self.lora_As16 = None
+        self.lora_B16 = None
+
+    def base_weight(self, dtype) -> torch.Tensor:
+        raise NotImplementedError
+
+    def forward(self, x):
+        as16, b16 = self.lora_As16, self.lora_B16
+        if as16 is None or as16.dtype != x.dtype:
+            as16 = (self.lora_A.detach() * self.scaling).to(x.dtype)
+            b16 = self.lora_B.detach().to(x.dtype)
+        bias = None if self.bias is None else self.bias.to(x.dtype)
+        return _LoRALinearFn.apply(x, self.lora_A, self.lora_B, as16, b16, self.scaling,
+                                   self.base_weight, bias)
 
 
-class LoRANF4Linear(torch.nn.Module):
+class LoRANF4Linear(_LoRABase):
     """Frozen NF4 base linear + trainable LoRA: y = base(x) + (alpha/r) * B(A(x))."""
 
     def __init__(self, linear: torch.nn.Linear, r: int = 16, alpha: int = 32,
                  lora_dtype: torch.dtype = torch.float32):
         super().__init__()
-        self.in_features = linear.in_features
-        self.out_features = linear.out_features
         packed, absmax = nf4_quantize(linear.weight)
         self.register_buffer("packed", packed)
         self.register_buffer("absmax", absmax)
-        if linear.bias is not None:
-            self.register_buffer("bias", linear.bias.detach().clone())
-        else:
-            self.bias = None
-        dev = linear.weight.device
-        self.lora_A = torch.nn.Parameter(torch.empty(r, self.in_features, device=dev, dtype=lora_dtype))
-        self.lora_B = torch.nn.Parameter(torch.zeros(self.out_features, r, device=dev, dtype=lora_dtype))
-        torch.nn.init.kaiming_uniform_(self.lora_A, a=math.sqrt(5))
-        self.scaling = alpha / r
+        self._init_lora(linear, r, alpha, lora_dtype)
 
     def dequantized_weight(self, dtype=torch.bfloat16) -> torch.Tensor:
         return nf4_dequantize(self.packed, self.absmax, (self.out_features, self.in_features), dtype)
 
-    def forward(self, x):
-        y = _NF4LinearFn.apply(x, self.packed, self.absmax, self.bias, self.out_features,
-                               self.in_features)
-        return _add_lora(y, x, self.lora_A, self.lora_B, self.scaling)
+    def base_weight(self, dtype) -> torch.Tensor:
+        return self.dequantized_weight(dtype)
 
 
-class LoRADenseLinear(torch.nn.Module):
+class LoRADenseLinear(_LoRABase):
     """Frozen dense base linear + trainable LoRA (for non-quantised runs and CPU tests)."""
 
     def __init__(self, linear: torch.nn.Linear, r: int = 16, alpha: int = 32,
                  lora_dtype: torch.dtype = torch.float32):
         super().__init__()
-        self.in_features = linear.in_features
-        self.out_features = linear.out_features
         self.register_buffer("weight", linear.weight.detach().clone())
-        if linear.bias is not None:
-            self.register_buffer("bias", linear.bias.detach().clone())
-        else:
-            self.bias = None
-        dev = linear.weight.device
-        self.lora_A = torch.nn.Parameter(torch.empty(r, self.in_features, device=dev, dtype=lora_dtype))
-        self.lora_B = torch.nn.Parameter(torch.zeros(self.out_features, r, device=dev, dtype=lora_dtype))
-        torch.nn.init.kaiming_uniform_(self.lora_A, a=math.sqrt(5))
-        self.scaling = alpha / r
+        self._init_lora(linear, r, alpha, lora_dtype)
 
-    def forward(self, x):
-        y = F.linear(x, self.weight.to(x.dtype), None if self.bias is None else self.bias.to(x.dtype))
-        return _add_lora(y, x, self.lora_A, self.lora_B, self.scaling)
+    def base_weight(self, dtype) -> torch.Tensor:
+        return self.weight.to(dtype)
 
 
 def qwen2_1p5b_config(num_layers: int = 28, **overrides):
@@ -262,13 +355,40 @@ class QLoRATrainer:
                 dist.broadcast(p.data, src=0)
         else:
             self.world = 1
-        total = sum(p.numel() for p in self.params)
         dev = self.params[0].device
+        # Parameters, gradients and the 16-bit copies the forward uses are views
+        # of flat buffers: one all-reduce for the gradients, two kernels per
+        # step to refresh the copies. The A factors come first (their copies
+        # hold (alpha/r) * A), then everything else.
+        lora = [m for m in model.modules() if isinstance(m, _LoRABase) and m.lora_A.requires_grad]
+        a_ids = {id(m.lora_A) for m in lora}
+        order = [p for p in self.params if id(p) in a_ids] + [p for p in self.params if id(p) not in a_ids]
+        self.n_a = sum(p.numel() for p in order if id(p) in a_ids)
+        scalings = {m.scaling for m in lora}
+        self.scaling = scalings.pop() if len(scalings) == 1 else None
+        total = sum(p.numel() for p in order)
+        self.flat_param = torch.empty(total, dtype=torch.float32, device=dev)
         self.flat_grad = torch.zeros(total, dtype=torch.float32, device=dev)
+        act_dtype = model.get_input_embeddings().weight.dtype
+        self.flat_param16 = (torch.empty(total, dtype=act_dtype, device=dev)
+                             if act_dtype in (torch.bfloat16, torch.float16) and self.scaling is not None
+                             else None)
+        views16 = {}
         off = 0
-        for p in self.params:
-            p.grad = self.flat_grad[off:off + p.numel()].view_as(p)
-            off += p.numel()
+        for p in order:
+            n = p.numel()
+            self.flat_param[off:off + n].copy_(p.data.reshape(-1))
+            p.data = self.flat_param[off:off + n].view_as(p)
+            p.grad = self.flat_grad[off:off + n].view_as(p)
+            if self.flat_param16 is not None:
+                views16[id(p)] = self.flat_param16[off:off + n].view_as(p)
+            off += n
+        if self.flat_param16 is not None:
+            for m in lora:
+                if id(m.lora_B) in views16:
+                    m.lora_As16 = views16[id(m.lora_A)]
+                    m.lora_B16 = views16[id(m.lora_B)]
+            self._refresh_param16()
         on_cuda = self.params[0].is_cuda
         fused = on_cuda if fused_adamw is None else fused_adamw
         self.opt = torch.optim.AdamW(self.params, lr=lr, fused=fused, capturable=on_cuda)
@@ -276,6 +396,9 @@ class QLoRATrainer:
         self.loss_fn = loss_fn or make_triton_chunked_loss_function()
         self.chunk = chunk
         self.graph = None
+        # prepared per-layer-type masks: None = plain causal (full attention only)
+        types = set(getattr(model.config, "layer_types", None) or ["full_attention"])
+        self._no_mask = {"full_attention": None} if types == {"full_attention"} else None
         model.train()
 
     def _allreduce_grads(self):
@@ -289,7 +412,15 @@ class QLoRATrainer:
 
     def step(self, input_ids: torch.Tensor, labels: torch.Tensor, denominator: float):
         self.flat_grad.zero_()
-        out = self.body(input_ids=input_ids)
+        self._refresh_param16()  # the factors may have been changed outside the trainer
+        # Batches here are unpadded single sequences, so the attention mask is
+        # exactly the causal pattern. Handing transformers a prepared "no mask"
+        # keeps SDPA on is_causal with grouped K/V heads also while a CUDA graph
+        # is captured: its own mask builder cannot inspect position ids during
+        # stream capture and then materialises a [B, 1, S, S] mask, which makes
+        # SDPA expand K/V to every query head and use a masked kernel (about 3x
+        # slower on B200 at S=2048).
+        out = self.body(input_ids=input_ids, attention_mask=self._no_mask)
         hidden = out.last_hidden_state if hasattr(out, "last_hidden_state") else out[0]
         loss, entropy, token_loss, correct = self.loss_fn.apply(
             hidden, self.model.lm_head, labels, self.chunk, denominator, -100, True)
@@ -297,7 +428,14 @@ class QLoRATrainer:
         if self.ddp:
             self._allreduce_grads()
         self.opt.step()
+        self._refresh_param16()  # forwards outside the trainer see the updated factors
         return loss.detach(), correct
+
+    def _refresh_param16(self):
+        if self.flat_param16 is not None:
+            na = self.n_a
+            torch.mul(self.flat_param[:na], self.scaling, out=self.flat_param16[:na])
+            self.flat_param16[na:].copy_(self.flat_param[na:])
 
     def capture(self, input_ids: torch.Tensor, labels: torch.Tensor, denominator: float,
                 warmup: int = 3):

@@ -210,6 +210,22 @@ int soup_gemm_bf16(const void* a, int64_t lda, int a_mn_major, const void* b, in
                    int b_mn_major, void* c, int64_t ldc, int c_dtype, int64_t m, int64_t n,
                    int64_t k, float alpha, int accumulate, void* stream);
 
+/* ---- Base GEMM plus a rank-r update in the same accumulator (QLoRA linears) --
+ * C[m, n] = alpha * (sum_k A(m,k) B(n,k) + sum_{j<r} A2(m,j) B2(n,j)) + bias[n]
+ *           (+ C if accumulate).
+ * A2 has A's majorness (a_mn_major = 0: stored [M, r], lda2 >= r; 1: stored
+ * [r, M], lda2 >= M) and B2 has B's (b_mn_major = 0: stored [N, r]; 1: stored
+ * [r, N]); the update is one or more extra 64-deep k-blocks of the same
+ * tcgen05 GEMM, zero-filled beyond r, so y = x W^T + (x A^T)(s B)^T or
+ * dx = dy W + (dy B)(s A) costs no pass over C of its own. r = 0: plain GEMM.
+ * bias: optional bf16 [N] (NULL: none). All row strides 16-byte aligned.
+ * No counterpart in the reference: there the LoRA linears are peft modules
+ * over bitsandbytes 4-bit layers, each term its own GEMM. */
+int soup_gemm_bf16_lora(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb,
+                        int b_mn_major, const void* a2, int64_t lda2, const void* b2, int64_t ldb2,
+                        int64_t r, const void* bias, void* c, int64_t ldc, int c_dtype, int64_t m,
+                        int64_t n, int64_t k, float alpha, int accumulate, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

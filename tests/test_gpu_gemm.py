@@ -1,7 +1,9 @@
-"""tcgen05 GEMM engine through the C ABI (soup_gemm_bf16) vs an fp32 matmul.
+"""tcgen05 GEMM engine through the C ABI (soup_gemm_bf16, soup_gemm_bf16_lora) vs
+an fp32 matmul.
 
 Covers the four operand layouts the fused CE uses (K-major / MN-major A and B),
-ragged edges in M, N and K, alpha, accumulate, fp32 and bf16 outputs.
+ragged edges in M, N and K, alpha, accumulate, fp32 and bf16 outputs, and the
+trailing rank-r K segment with bias that the QLoRA linears use.
 """
 
 import pytest
@@ -93,6 +95,46 @@ def test_gemm_many_tiles_mn_major():
     assert err < 1e-5, err
 
 
+def run_lora_gemm(a, b, b_mn, a2, b2, m, n, k, r, bias=None, c_dtype=torch.float32, alpha=1.0):
+    c = torch.full((m, n), float("nan"), dtype=c_dtype, device=a.device)
+    _lib.call("soup_gemm_bf16_lora", a.device, a.data_ptr(), a.stride(0), 0, b.data_ptr(), b.stride(0),
+              int(b_mn), a2.data_ptr(), a2.stride(0), b2.data_ptr(), b2.stride(0), r,
+              None if bias is None else bias.data_ptr(), c.data_ptr(), c.stride(0),
+              _lib.dtype_code(c.dtype), m, n, k, float(alpha), 0, _lib.stream_of(c))
+    torch.cuda.synchronize()
+    assert _lib.device_error(a.device) == 0
+    return c
+
+
+@pytest.mark.parametrize("b_mn", [0, 1])
+@pytest.mark.parametrize("m,n,k,r", [(256, 512, 128, 16), (1000, 1536, 704, 16), (520, 264, 1536, 48),
+                                     (2048, 1536, 1536, 80)])
+@pytest.mark.parametrize("with_bias,c_bf16", [(False, False), (True, True)])
+def test_gemm_lora_segment(b_mn, m, n, k, r, with_bias, c_bf16):
+    # C = alpha (A B^T + A2 B2^T) + bias: the rank-r term is the GEMM's trailing
+    # k-block(s), zero-filled by TMA past r (r = 16, 48: one block; 80: two)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    A = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    B = torch.randn(n, k, device="cuda", generator=g).to(torch.bfloat16)
+    A2 = torch.randn(m, r, device="cuda", generator=g).to(torch.bfloat16)
+    B2 = torch.randn(n, r, device="cuda", generator=g).to(torch.bfloat16)
+    bias = torch.randn(n, device="cuda", generator=g).to(torch.bfloat16) if with_bias else None
+    b = B.t().contiguous() if b_mn else B
+    b2 = B2.t().contiguous() if b_mn else B2
+    c = run_lora_gemm(A, b, b_mn, A2, b2, m, n, k, r, bias, torch.bfloat16 if c_bf16 else torch.float32,
+                      alpha=0.5)
+    ref = 0.5 * (A.float() @ B.float().t() + A2.float() @ B2.float().t())
+    if with_bias:
+        ref = ref + bias.float()
+    err = (c.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < (8e-3 if c_bf16 else 1e-5), err
+    # r = 0 is the plain GEMM
+    if r == 16 and not with_bias:
+        c0 = run_lora_gemm(A, b, b_mn, A2, b2, m, n, k, 0)
+        ref0 = A.float() @ B.float().t()
+        assert (c0 - ref0).abs().max().item() / ref0.abs().max().item() < 1e-5
+
+
 _SINGLE_CTA_SCRIPT = r"""
 import torch
 from auspex_soup_demo_b200 import _lib
@@ -111,6 +153,20 @@ for (m, n, k, a_mn, b_mn) in [(200, 328, 192, 0, 0), (1000, 1536, 704, 0, 1), (3
     ref = A.float() @ B.float().t()
     err = (c - ref).abs().max().item() / ref.abs().max().item()
     assert err < 1e-5, (m, n, k, a_mn, b_mn, err)
+m, n, k, r = 1000, 1536, 704, 16
+A = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+B = torch.randn(k, n, device="cuda").to(torch.bfloat16)
+A2 = torch.randn(m, r, device="cuda").to(torch.bfloat16)
+B2 = torch.randn(r, n, device="cuda").to(torch.bfloat16)
+c = torch.zeros(m, n, device="cuda")
+_lib.call("soup_gemm_bf16_lora", A.device, A.data_ptr(), A.stride(0), 0, B.data_ptr(), B.stride(0), 1,
+          A2.data_ptr(), A2.stride(0), B2.data_ptr(), B2.stride(0), r, None, c.data_ptr(), c.stride(0),
+          _lib.dtype_code(c.dtype), m, n, k, 1.0, 0, _lib.stream_of(c))
+torch.cuda.synchronize()
+assert _lib.device_error(A.device) == 0
+ref = A.float() @ B.float() + A2.float() @ B2.float()
+err = (c - ref).abs().max().item() / ref.abs().max().item()
+assert err < 1e-5, ("lora", err)
 print("single-cta ok")
 """
 

@@ -32,7 +32,9 @@ def test_nf4_quantize_dequantize_bit_exact(shape, dtype):
     assert torch.equal(d32.cpu(), onf4.nf4_dequantize(p_ref, a_ref, code, dtype=torch.float32).view(shape))
 
 
-def test_lora_nf4_linear_forward_backward():
+@pytest.mark.parametrize("fused_max_k", [10 ** 9, 0])  # tcgen05 rank-r GEMM / cuBLAS path
+def test_lora_nf4_linear_forward_backward(fused_max_k, monkeypatch):
+    monkeypatch.setattr(qlora, "FUSED_MAX_K", fused_max_k)
     torch.manual_seed(0)
     lin = torch.nn.Linear(512, 384, bias=True, device="cuda", dtype=torch.bfloat16)
     mod = qlora.LoRANF4Linear(lin, r=16, alpha=32)

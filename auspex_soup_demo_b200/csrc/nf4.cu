@@ -54,43 +54,65 @@ __global__ void __launch_bounds__(256) nf4_quantize_kernel(const T* __restrict__
   }
 }
 
-// Each thread expands 16 packed bytes (32 weights of one block) to 32 outputs.
+// Dequantisation: thread i expands packed 32-bit word i (8 weights, bytes in
+// memory order, the earlier weight of a byte in its high nibble) into one
+// 16-byte output vector (two for fp32), so a warp's loads and stores are each
+// one contiguous segment. U words per thread are in flight together. The
+// stores use the default cache policy: the weight is read again right away
+// by the GEMM that follows, which then finds it in L2.
 template <typename T>
-__global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint8_t* __restrict__ packed,
+__device__ __forceinline__ void store8(T* dst, const float (&v)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    Vec16<T> o;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o.v[e] = Cvt<T>::from_f(v[e]);
+    st16(dst, o);
+  } else {
+    Vec16<T> a, b;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      a.v[e] = Cvt<T>::from_f(v[e]);
+      b.v[e] = Cvt<T>::from_f(v[4 + e]);
+    }
+    st16(dst, a);
+    st16(dst + 4, b);
+  }
+}
+
+template <typename T, int U>
+__global__ void __launch_bounds__(256) nf4_dequant_kernel(const uint32_t* __restrict__ packed,
                                                           const float* __restrict__ absmax,
-                                                          int64_t nvec, Code16 code,
+                                                          int64_t nwords, Code16 code,
                                                           T* __restrict__ out) {
   __shared__ float tbl[16];
   if (threadIdx.x < 16) tbl[threadIdx.x] = code.v[threadIdx.x];
+  pdl_wait();
+  pdl_trigger();
   __syncthreads();
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const uint4 p = __ldcs(reinterpret_cast<const uint4*>(packed) + i);
-    const float s = absmax[i >> 1];  // 32 weights per vector, 64 per block
-    const uint32_t words[4] = {p.x, p.y, p.z, p.w};
-    T* dst = out + i * 32;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < nwords; i0 += stride * U) {
+    uint32_t p[U];
+    float s[U];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      Vec16<T> o0, o1;  // 8 bytes of this word -> 8 outputs (bf16: one vector)
-      float vals[8];
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const uint32_t byte = (words[q] >> (8 * b)) & 0xffu;
-        vals[2 * b] = tbl[byte >> 4] * s;
-        vals[2 * b + 1] = tbl[byte & 0xf] * s;
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < nwords) {
+        p[u] = __ldcs(packed + i);
+        s[u] = __ldg(absmax + (i >> 3));  // 8 words = one block of 64 weights
       }
-      if constexpr (sizeof(T) == 2) {
+    }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o0.v[e] = Cvt<T>::from_f(vals[e]);
-        st16_stream(dst + q * 8, o0);
-      } else {
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = i0 + u * stride;
+      if (i < nwords) {
+        float v[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          o0.v[e] = Cvt<T>::from_f(vals[e]);
-          o1.v[e] = Cvt<T>::from_f(vals[4 + e]);
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t byte = (p[u] >> (8 * b)) & 0xffu;
+          v[2 * b] = tbl[byte >> 4] * s[u];
+          v[2 * b + 1] = tbl[byte & 0xf] * s[u];
         }
-        st16_stream(dst + q * 8, o0);
-        st16_stream(dst + q * 8 + 4, o1);
+        store8(out + i * 8, v);
       }
     }
   }
@@ -149,23 +171,26 @@ int soup_nf4_dequant(const uint8_t* packed, const float* absmax, int64_t n, int 
   }
   Code16 code;
   for (int i = 0; i < 16; ++i) code.v[i] = code16[i];
-  const int64_t nvec = n / 32;
-  const int grid = grid_for(nvec, 256);
+  constexpr int U = 4;
+  const int64_t nwords = n / 8;
+  const int grid = grid_for(nwords, 256 * U);
   cudaStream_t st = as_stream(stream);
+  const uint32_t* pw = reinterpret_cast<const uint32_t*>(packed);
+  cudaError_t e = cudaSuccess;
   if (dtype == SOUP_BF16)
-    nf4_dequant_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(packed, absmax, nvec, code,
-                                                            static_cast<__nv_bfloat16*>(out));
+    e = launch_pdl(nf4_dequant_kernel<__nv_bfloat16, U>, dim3(grid), dim3(256), 0, st, pw, absmax,
+                   nwords, code, static_cast<__nv_bfloat16*>(out));
   else if (dtype == SOUP_F16)
-    nf4_dequant_kernel<__half><<<grid, 256, 0, st>>>(packed, absmax, nvec, code,
-                                                     static_cast<__half*>(out));
+    e = launch_pdl(nf4_dequant_kernel<__half, U>, dim3(grid), dim3(256), 0, st, pw, absmax, nwords,
+                   code, static_cast<__half*>(out));
   else if (dtype == SOUP_F32)
-    nf4_dequant_kernel<float><<<grid, 256, 0, st>>>(packed, absmax, nvec, code,
-                                                    static_cast<float*>(out));
+    e = launch_pdl(nf4_dequant_kernel<float, U>, dim3(grid), dim3(256), 0, st, pw, absmax, nwords,
+                   code, static_cast<float*>(out));
   else {
     set_last_error("soup_nf4_dequant: unsupported dtype");
     return SOUP_ERR_INVALID;
   }
-  return launch_status();
+  return cuda_status(e);
 }
 
 }  // extern "C"

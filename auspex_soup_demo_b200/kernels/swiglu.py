@@ -106,8 +106,14 @@ def patch_qwen2_mlp():
         act = getattr(getattr(self, "config", None), "hidden_act", "silu")
         if act != "silu" or not x.is_cuda:
             return original_forward(self, x)
-        if not (RECOMPUTE and self.training and torch.is_grad_enabled()
-                and getattr(x, "requires_grad", False)):
+        recompute = (RECOMPUTE and self.training and torch.is_grad_enabled()
+                     and getattr(x, "requires_grad", False))
+        group = getattr(self.gate_proj, "lora_group", None)
+        if (group is not None and group.kind == "gate_up" and group.members[0] is self.gate_proj
+                and group.members[1] is self.up_proj and group.usable(x)):
+            # gate/up as one GEMM feeding the fused SwiGLU; same recompute policy
+            return self.down_proj(group.swiglu(x, recompute))
+        if not recompute:
             return self.down_proj(fast_swiglu(self.gate_proj(x), self.up_proj(x)))
 
         def _swiglu_forward(hidden_states):

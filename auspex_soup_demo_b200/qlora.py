@@ -220,11 +220,17 @@ class _LoRABase(torch.nn.Module):
         self.scaling = alpha / r
         self.lora_As16 = None
         self.lora_B16 = None
+        self.lora_group = None
 
     def base_weight(self, dtype) -> torch.Tensor:
         raise NotImplementedError
 
     def forward(self, x):
+        grp = self.lora_group
+        if grp is not None and grp.kind == "qkv" and grp.usable(x):
+            out = grp.member_output(self, x)
+            if out is not None:
+                return out
         as16, b16 = self.lora_As16, self.lora_B16
         if as16 is None or as16.dtype != x.dtype:
             as16 = (self.lora_A.detach() * self.scaling).to(x.dtype)
@@ -265,6 +271,294 @@ class LoRADenseLinear(_LoRABase):
         return self.weight.to(dtype)
 
 
+class LoRAProjectionGroup:
+    """Projections of one input (q/k/v, or gate/up) computed as ONE GEMM.
+
+    The members keep their own LoRA parameters, names and buffers (the adapter
+    layout does not change), but their frozen base weights live in one
+    concatenated buffer - NF4 ``packed``/``absmax`` (the 64-element blocks of
+    row-concatenated weights are the members' blocks in order) or a dense
+    weight - of which each member's buffer is a view, and likewise the biases.
+    One call then does one dequantisation, one rank-R GEMM xa = x As^T
+    (R = sum of the members' ranks, As the members' scaled A factors stacked)
+    and one tcgen05 GEMM y = x W^T + xa Bblk^T (+ bias) whose rank-R k-block
+    uses the block-diagonal Bblk (member j's rows use only member j's xa
+    columns). Backward is one dX GEMM with a rank-R k-block, one dxa GEMM,
+    one gA GEMM into the stacked A gradients, and one gB GEMM per member.
+
+    On B200 with Qwen2.5-1.5B shapes at 2048 tokens this replaces k_proj /
+    v_proj GEMMs with N = 256 (8 of 74 CTA pairs busy) and the separate
+    dequantisations, rank-16 GEMMs and autograd gradient sums of each member.
+    """
+
+    def __init__(self, members, kind: str):
+        self.members = list(members)
+        self.kind = kind
+        ins = {m.in_features for m in self.members}
+        assert len(ins) == 1, "grouped projections must share their input"
+        self.in_features = ins.pop()
+        self.outs = [m.out_features for m in self.members]
+        self.ranks = [m.lora_A.shape[0] for m in self.members]
+        self.out_off = [0]
+        for n in self.outs:
+            self.out_off.append(self.out_off[-1] + n)
+        self.rank_off = [0]
+        for r in self.ranks:
+            self.rank_off.append(self.rank_off[-1] + r)
+        self.n_total = self.out_off[-1]
+        self.r_total = self.rank_off[-1]
+        scal = {m.scaling for m in self.members}
+        self.scaling = scal.pop() if len(scal) == 1 else None
+        self.nf4 = all(isinstance(m, LoRANF4Linear) for m in self.members)
+        if self.nf4:
+            self.packed = torch.cat([m.packed for m in self.members])
+            self.absmax = torch.cat([m.absmax for m in self.members])
+            po = ao = 0
+            for m in self.members:
+                n_p, n_a = m.packed.numel(), m.absmax.numel()
+                m._buffers["packed"] = self.packed[po:po + n_p]
+                m._buffers["absmax"] = self.absmax[ao:ao + n_a]
+                po += n_p
+                ao += n_a
+        else:
+            assert all(isinstance(m, LoRADenseLinear) for m in self.members)
+            self.weight = torch.cat([m.weight for m in self.members])
+            for m, a, b in zip(self.members, self.out_off[:-1], self.out_off[1:]):
+                m._buffers["weight"] = self.weight[a:b]
+        if any(m.bias is not None for m in self.members):
+            self.bias = torch.cat([m.bias if m.bias is not None else
+                                   torch.zeros(m.out_features, dtype=self.members[0].lora_A.dtype
+                                               if self.members[0].bias is None else self.members[0].bias.dtype,
+                                               device=self.members[0].lora_A.device)
+                                   for m in self.members])
+            for m, a, b in zip(self.members, self.out_off[:-1], self.out_off[1:]):
+                if m.bias is not None:
+                    m._buffers["bias"] = self.bias[a:b]
+        else:
+            self.bias = None
+        # set by QLoRATrainer: 16-bit stacked As and block-diagonal B (refreshed
+        # after every optimiser step) and the fp32 gradient view of the stacked A
+        self.As16 = None
+        self.Bblk16 = None
+        self.gradA = None
+        self._stash = None
+        for m in self.members:
+            m.lora_group = self
+
+    # -- operands ---------------------------------------------------------------
+    def base_weight(self, dtype) -> torch.Tensor:
+        if self.nf4:
+            return nf4_dequantize(self.packed, self.absmax, (self.n_total, self.in_features), dtype)
+        return self.weight.to(dtype)
+
+    def factors(self, dtype):
+        """(As [R, in], Bblk [N, R]) in ``dtype``."""
+        if self.As16 is not None and self.As16.dtype == dtype:
+            return self.As16, self.Bblk16
+        As = torch.cat([(m.lora_A.detach() * m.scaling).to(dtype) for m in self.members])
+        Bblk = torch.zeros(self.n_total, self.r_total, dtype=dtype, device=As.device)
+        for j, m in enumerate(self.members):
+            Bblk[self.out_off[j]:self.out_off[j + 1], self.rank_off[j]:self.rank_off[j + 1]] = \
+                m.lora_B.detach().to(dtype)
+        return As, Bblk
+
+    def out_features_of(self, j: int) -> int:
+        return self.outs[j]
+
+    def usable(self, x: torch.Tensor) -> bool:
+        return (x.is_cuda and x.dtype == torch.bfloat16 and x.shape[-1] == self.in_features
+                and all(m.lora_group is self for m in self.members))
+
+    def params(self):
+        out = []
+        for m in self.members:
+            out += [m.lora_A, m.lora_B]
+        return out
+
+    # -- calls ------------------------------------------------------------------
+    def project(self, x: torch.Tensor):
+        """The members' outputs for input x (a tuple, member order)."""
+        return _LoRAGroupFn.apply(x, self, *self.params())
+
+    def member_output(self, member, x: torch.Tensor) -> Optional[torch.Tensor]:
+        """Output of ``member`` for x: the first member's call computes every
+        member's output and keeps the others until they are asked for with
+        the same input tensor (HF's attention calls q_proj, k_proj, v_proj on
+        one hidden-state tensor in turn). None means: compute it alone."""
+        st = self._stash
+        if st is not None and st[0] is x and st[1] == x._version and member in st[2]:
+            out = st[2].pop(member)
+            if not st[2]:
+                self._stash = None
+            return out
+        if member is not self.members[0]:
+            return None
+        outs = self.project(x)
+        self._stash = (x, x._version, dict(zip(self.members[1:], outs[1:])))
+        return outs[0]
+
+    def swiglu(self, x: torch.Tensor, recompute: bool) -> torch.Tensor:
+        """silu(gate(x)) * up(x) for a gate/up group, with the gate/up GEMM
+        recomputed in backward when ``recompute`` (the reference's selective
+        recompute of the MLP, solution/kernels/swiglu.py:197-214)."""
+        return _LoRAGateUpFn.apply(x, self, bool(recompute), *self.params())
+
+
+def _group_gemm(group: LoRAProjectionGroup, x2: torch.Tensor, w: torch.Tensor, As16, Bblk):
+    """(y = x2 W^T + (x2 As^T) Bblk^T + bias [M, N], xa = x2 As^T)."""
+    xa = x2 @ As16.t()
+    m = x2.shape[0]
+    n = group.n_total
+    bias = None if group.bias is None else group.bias.to(x2.dtype)
+    if _fused_ok(x2.shape[1], x2, w, xa, Bblk, bias.view(1, -1) if bias is not None else None):
+        y = lora_gemm(x2, w, False, xa, Bblk, torch.empty(m, n, device=x2.device, dtype=x2.dtype), bias)
+    else:
+        y = F.linear(x2, w, bias)
+        y.addmm_(xa, Bblk.t())
+    return y, xa
+
+
+def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tensor, xa: torch.Tensor,
+                    w: torch.Tensor, As16, Bblk, need_dx: bool, need_params):
+    """dx (or None) and the LoRA gradients for a group GEMM's output gradient
+    dy [M, N]. Gradients go straight into fp32 ``.grad`` buffers where the
+    parameters have them (None is returned for those)."""
+    dxa = dy @ Bblk
+    dx = None
+    if need_dx:
+        m, n = dy.shape[0], w.shape[1]
+        if _fused_ok(dy.shape[1], dy, w, dxa, As16):
+            dx = lora_gemm(dy, w, True, dxa, As16, torch.empty(m, n, device=dy.device, dtype=dy.dtype))
+        else:
+            dx = dy @ w
+            dx.addmm_(dxa, As16)
+    grads = []
+    gA_done = False
+    if group.gradA is not None and group.scaling is not None and all(
+            need_params[2 * j] and group.members[j].lora_A.grad is not None
+            and group.members[j].lora_A.grad.data_ptr() == group.gradA[group.rank_off[j]].data_ptr()
+            for j in range(len(group.members))):
+        torch.addmm(group.gradA, dxa.t(), x2, alpha=group.scaling, out_dtype=torch.float32, out=group.gradA)
+        gA_done = True
+    for j, mem in enumerate(group.members):
+        r0, r1 = group.rank_off[j], group.rank_off[j + 1]
+        o0, o1 = group.out_off[j], group.out_off[j + 1]
+        gA = gB = None
+        if need_params[2 * j] and not gA_done:
+            gA = _accumulate_grad(mem.lora_A, dxa[:, r0:r1].t(), x2, mem.scaling)
+        if need_params[2 * j + 1]:
+            gB = _accumulate_grad(mem.lora_B, dy[:, o0:o1].t(), xa[:, r0:r1], 1.0)
+        grads += [gA, gB]
+    return dx, grads
+
+
+class _LoRAGroupFn(torch.autograd.Function):
+    """Outputs of a projection group (see LoRAProjectionGroup) for input x."""
+
+    @staticmethod
+    def forward(ctx, x, group, *params):
+        k = group.in_features
+        x2 = x.reshape(-1, k)
+        w = group.base_weight(x.dtype)
+        As16, Bblk = group.factors(x.dtype)
+        y, xa = _group_gemm(group, x2, w, As16, Bblk)
+        ctx.save_for_backward(x2, xa, As16, Bblk)
+        ctx.group = group
+        ctx.lead = x.shape[:-1]
+        outs = tuple(y[:, a:b].view(*x.shape[:-1], b - a)
+                     for a, b in zip(group.out_off[:-1], group.out_off[1:]))
+        return outs
+
+    @staticmethod
+    def backward(ctx, *douts):
+        x2, xa, As16, Bblk = ctx.saved_tensors
+        group = ctx.group
+        m = x2.shape[0]
+        parts = [d.reshape(m, n) if d is not None else torch.zeros(m, n, device=x2.device, dtype=x2.dtype)
+                 for d, n in zip(douts, group.outs)]
+        dy = torch.cat(parts, dim=1)
+        w = group.base_weight(dy.dtype) if ctx.needs_input_grad[0] else None
+        dx, grads = _group_backward(group, dy, x2, xa, w, As16, Bblk, ctx.needs_input_grad[0],
+                                    ctx.needs_input_grad[2:])
+        if dx is not None:
+            dx = dx.view(*ctx.lead, x2.shape[1])
+        return (dx, None, *grads)
+
+
+class _LoRAGateUpFn(torch.autograd.Function):
+    """h = silu(g) * u with [g | u] = one group GEMM of x (gate/up group).
+
+    With ``recompute`` the forward keeps only x and the rank-R product xa; the
+    backward dequantises the weights once, recomputes [g | u] and uses the
+    same weights for dx. Without it [g | u] is kept from the forward.
+    """
+
+    @staticmethod
+    def forward(ctx, x, group, recompute, *params):
+        from .kernels.swiglu import swiglu_forward
+
+        k = group.in_features
+        x2 = x.reshape(-1, k)
+        w = group.base_weight(x.dtype)
+        As16, Bblk = group.factors(x.dtype)
+        y, xa = _group_gemm(group, x2, w, As16, Bblk)
+        inter = group.outs[0]
+        h = swiglu_forward(y[:, :inter], y[:, inter:])
+        ctx.recompute = recompute
+        if recompute:
+            ctx.save_for_backward(x2, xa, As16, Bblk)
+        else:
+            ctx.save_for_backward(x2, xa, As16, Bblk, y)
+        ctx.group = group
+        ctx.lead = x.shape[:-1]
+        return h.view(*x.shape[:-1], inter)
+
+    @staticmethod
+    def backward(ctx, dh):
+        from .kernels.swiglu import swiglu_backward
+
+        group = ctx.group
+        saved = ctx.saved_tensors
+        x2, xa, As16, Bblk = saved[:4]
+        inter = group.outs[0]
+        w = group.base_weight(x2.dtype)
+        if ctx.recompute:
+            y, _ = _group_gemm(group, x2, w, As16, Bblk)
+        else:
+            y = saved[4]
+        dh2 = dh.reshape(-1, inter)
+        if dh2.stride(1) != 1:
+            dh2 = dh2.contiguous()
+        if dh2.dtype != y.dtype:
+            dh2 = dh2.to(y.dtype)
+        dy = torch.empty_like(y)
+        swiglu_backward(dh2, y[:, :inter], y[:, inter:], dg=dy[:, :inter], du=dy[:, inter:])
+        dx, grads = _group_backward(group, dy, x2, xa, w, As16, Bblk, ctx.needs_input_grad[0],
+                                    ctx.needs_input_grad[3:])
+        if dx is not None:
+            dx = dx.view(*ctx.lead, x2.shape[1])
+        return (dx, None, None, *grads)
+
+
+def group_projections(model, kinds=("qkv", "gate_up")):
+    """Group each decoder layer's q/k/v and gate/up LoRA projections (see
+    LoRAProjectionGroup). Returns the groups."""
+    groups = []
+    for layer in model.model.layers:
+        sets = []
+        if "qkv" in kinds:
+            sets.append(("qkv", [getattr(layer.self_attn, n, None) for n in ("q_proj", "k_proj", "v_proj")]))
+        if "gate_up" in kinds:
+            sets.append(("gate_up", [getattr(layer.mlp, n, None) for n in ("gate_proj", "up_proj")]))
+        for kind, mods in sets:
+            if all(isinstance(m, (LoRANF4Linear, LoRADenseLinear)) for m in mods) and \
+                    len({type(m) for m in mods}) == 1 and \
+                    len({m.in_features for m in mods}) == 1 and \
+                    all(getattr(m, "lora_group", None) is None for m in mods):
+                groups.append(LoRAProjectionGroup(mods, kind))
+    return groups
+
+
 def qwen2_1p5b_config(num_layers: int = 28, **overrides):
     from transformers import Qwen2Config
 
@@ -281,10 +575,12 @@ def qwen2_1p5b_config(num_layers: int = 28, **overrides):
 
 def build_qwen2_qlora(config=None, device="cuda", seed: int = 0, r: int = 16, alpha: int = 32,
                       targets: Iterable[str] = LORA_TARGETS, quantize: bool = True,
-                      dtype: torch.dtype = torch.bfloat16):
+                      dtype: torch.dtype = torch.bfloat16, group: bool = True):
     """Randomly initialised Qwen2 model with (NF4 +) LoRA on the target linears.
 
     quantize=False keeps dense frozen base weights (CPU runs and tests).
+    group=True computes each layer's q/k/v and gate/up projections as one GEMM
+    each on CUDA (LoRAProjectionGroup); parameters and names are unchanged.
     """
     from transformers import Qwen2ForCausalLM
 
@@ -307,6 +603,8 @@ def build_qwen2_qlora(config=None, device="cuda", seed: int = 0, r: int = 16, al
                 lin = getattr(parent, name, None)
                 if isinstance(lin, torch.nn.Linear):
                     setattr(parent, name, wrap(lin, r, alpha))
+    if group:
+        group_projections(model)
     if torch.cuda.is_available():
         torch.cuda.empty_cache()
     return model
@@ -374,20 +672,24 @@ class QLoRATrainer:
                              if act_dtype in (torch.bfloat16, torch.float16) and self.scaling is not None
                              else None)
         views16 = {}
+        offsets = {}
         off = 0
         for p in order:
             n = p.numel()
             self.flat_param[off:off + n].copy_(p.data.reshape(-1))
             p.data = self.flat_param[off:off + n].view_as(p)
             p.grad = self.flat_grad[off:off + n].view_as(p)
+            offsets[id(p)] = off
             if self.flat_param16 is not None:
                 views16[id(p)] = self.flat_param16[off:off + n].view_as(p)
             off += n
+        self._bblk_copies = []
         if self.flat_param16 is not None:
             for m in lora:
                 if id(m.lora_B) in views16:
                     m.lora_As16 = views16[id(m.lora_A)]
                     m.lora_B16 = views16[id(m.lora_B)]
+            self._setup_groups(lora, offsets)
             self._refresh_param16()
         on_cuda = self.params[0].is_cuda
         fused = on_cuda if fused_adamw is None else fused_adamw
@@ -431,11 +733,58 @@ class QLoRATrainer:
         self._refresh_param16()  # forwards outside the trainer see the updated factors
         return loss.detach(), correct
 
+    def _setup_groups(self, lora, offsets):
+        """Give every projection group (LoRAProjectionGroup) views of the flat
+        buffers: its stacked 16-bit scaled A factors and their fp32 gradient
+        (the members' A factors are adjacent in the flat order), and a
+        block-diagonal 16-bit B. Groups of one structure (every decoder layer's
+        q/k/v, every layer's gate/up) share one [layers, N, R] buffer, and when
+        their members' B factors sit at a fixed stride in the flat buffer the
+        refresh is one strided copy per member position for all layers."""
+        groups = []
+        for m in lora:
+            g = m.lora_group
+            if g is not None and all(x is not g for x in groups):
+                groups.append(g)
+        dev = self.flat_param.device
+        self._bblk_copies = []
+        kinds = {}
+        for g in groups:
+            a_offs = [offsets.get(id(mm.lora_A)) for mm in g.members]
+            b_offs = [offsets.get(id(mm.lora_B)) for mm in g.members]
+            if any(o is None for o in a_offs + b_offs) or any(
+                    a_offs[j + 1] != a_offs[j] + g.members[j].lora_A.numel() for j in range(len(a_offs) - 1)):
+                continue
+            n_a = g.r_total * g.in_features
+            g.As16 = self.flat_param16[a_offs[0]:a_offs[0] + n_a].view(g.r_total, g.in_features)
+            g.gradA = self.flat_grad[a_offs[0]:a_offs[0] + n_a].view(g.r_total, g.in_features)
+            key = (g.kind, tuple(g.outs), tuple(g.ranks), g.in_features)
+            kinds.setdefault(key, []).append((g, b_offs))
+        for key, items in kinds.items():
+            g0 = items[0][0]
+            buf = torch.zeros(len(items), g0.n_total, g0.r_total, dtype=self.flat_param16.dtype, device=dev)
+            for l, (g, _) in enumerate(items):
+                g.Bblk16 = buf[l]
+            for j in range(len(g0.members)):
+                n_j, r_j = g0.outs[j], g0.ranks[j]
+                o0, c0 = g0.out_off[j], g0.rank_off[j]
+                offs = [b[j] for _, b in items]
+                stride = offs[1] - offs[0] if len(offs) > 1 else n_j * r_j
+                if all(offs[l] == offs[0] + l * stride for l in range(len(offs))):
+                    src = self.flat_param16.as_strided((len(offs), n_j, r_j), (stride, r_j, 1), offs[0])
+                    self._bblk_copies.append((buf[:, o0:o0 + n_j, c0:c0 + r_j], src))
+                else:
+                    for l, off in enumerate(offs):
+                        src = self.flat_param16[off:off + n_j * r_j].view(n_j, r_j)
+                        self._bblk_copies.append((buf[l, o0:o0 + n_j, c0:c0 + r_j], src))
+
     def _refresh_param16(self):
         if self.flat_param16 is not None:
             na = self.n_a
             torch.mul(self.flat_param[:na], self.scaling, out=self.flat_param16[:na])
             self.flat_param16[na:].copy_(self.flat_param[na:])
+            for dst, src in self._bblk_copies:
+                dst.copy_(src)
 
     def capture(self, input_ids: torch.Tensor, labels: torch.Tensor, denominator: float,
                 warmup: int = 3):

@@ -210,3 +210,52 @@ def test_captured_step_matches_eager_steps():
     for n, p in graphed.model.named_parameters():
         if p.requires_grad:  # the 6 updates agree in direction
             assert cosine(p - init[n], pa[n] - init[n]) > 0.99, n
+
+
+def _small_model_grouped(seed, group):
+    cfg = qlora.qwen2_1p5b_config(num_layers=2, hidden_size=256, intermediate_size=640,
+                                  num_attention_heads=4, num_key_value_heads=2, vocab_size=2048)
+    model = qlora.build_qwen2_qlora(cfg, device="cuda", seed=seed, group=group)
+    torch.manual_seed(seed + 7)
+    for m in model.modules():
+        if isinstance(m, qlora.LoRANF4Linear):
+            torch.nn.init.normal_(m.lora_B, std=0.02)
+    return model
+
+
+@pytest.mark.parametrize("recompute", [True, False])
+def test_grouped_projections_match_separate_modules(recompute, monkeypatch):
+    # q/k/v and gate/up as one GEMM each (LoRAProjectionGroup) vs every projection
+    # on its own: same loss and LoRA gradients up to bf16 accumulation order
+    from auspex_soup_demo_b200.kernels import make_triton_chunked_loss_function
+    from auspex_soup_demo_b200.kernels import swiglu as sw
+
+    apply()
+    monkeypatch.setattr(sw, "RECOMPUTE", recompute)
+    g = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, 2048, (2, 96), generator=g).cuda()
+    labels = qlora.causal_labels(ids)
+    fn = make_triton_chunked_loss_function()
+    grouped = _small_model_grouped(5, True)
+    assert grouped.model.layers[0].self_attn.k_proj.lora_group is not None
+    separate = _small_model_grouped(5, False)
+    grouped.train()
+    separate.train()
+    l1, g1 = _grads(grouped, ids, labels, fn)
+    l2, g2 = _grads(separate, ids, labels, fn)
+    assert abs(l1 - l2) <= 1e-3 * abs(l2), (l1, l2)
+    worst = min(cosine(g1[k], g2[k]) for k in g2)
+    assert worst > 0.999, worst
+    # through the trainer (stacked As, block-diagonal B and gradient views of the flat buffers)
+    den = float((labels != -100).sum())
+    t1 = qlora.QLoRATrainer(_small_model_grouped(6, True), lr=1e-3)
+    t2 = qlora.QLoRATrainer(_small_model_grouped(6, False), lr=1e-3)
+    a = [float(t1.step(ids, labels, den)[0]) for _ in range(3)]
+    b = [float(t2.step(ids, labels, den)[0]) for _ in range(3)]
+    for x, y in zip(a, b):
+        assert abs(x - y) <= 2e-3 * abs(y), (a, b)
+    assert a[-1] < a[0]
+    p1 = dict(t1.model.named_parameters())
+    for n, p in t2.model.named_parameters():
+        if p.requires_grad:
+            assert cosine(p1[n].grad, p.grad) > 0.99, n

@@ -130,3 +130,45 @@ def test_data_parallel_lora_step_matches_single_process(tmp_path):
     for k, v in s0.items():
         kk = k.replace("module.", "")
         torch.testing.assert_close(v, ref[kk], rtol=1e-3, atol=1e-4)
+
+
+def test_projection_groups_share_buffers_and_trainer_views():
+    # q/k/v and gate/up groups: the members' base weights and biases are views of
+    # the group's concatenated buffers, and the trainer's stacked As / gradient
+    # views and block-diagonal B equal what the group builds from its members
+    cfg = qlora.qwen2_1p5b_config(num_layers=2, hidden_size=256, intermediate_size=640,
+                                  num_attention_heads=4, num_key_value_heads=2, vocab_size=512)
+    model = qlora.build_qwen2_qlora(cfg, device="cpu", quantize=False, seed=0)
+    for m in model.modules():
+        if isinstance(m, qlora.LoRADenseLinear):
+            torch.nn.init.normal_(m.lora_B, std=0.02)
+    layer = model.model.layers[1]
+    qkv = layer.self_attn.q_proj.lora_group
+    gu = layer.mlp.gate_proj.lora_group
+    assert qkv.kind == "qkv" and qkv.members == [layer.self_attn.q_proj, layer.self_attn.k_proj,
+                                                 layer.self_attn.v_proj]
+    assert gu.kind == "gate_up" and gu.n_total == 2 * 640 and gu.bias is None
+    assert layer.self_attn.o_proj.lora_group is None and layer.mlp.down_proj.lora_group is None
+    assert layer.self_attn.k_proj.weight.data_ptr() == qkv.weight[256].data_ptr()
+    assert layer.self_attn.v_proj.bias.data_ptr() == qkv.bias[384:].data_ptr()
+    As_ref, B_ref = qkv.factors(torch.bfloat16)  # built from the members (no trainer yet)
+    trainer = qlora.QLoRATrainer(model, lr=1e-3, loss_fn=EagerChunkedLoss)
+    for g in (qkv, gu):
+        assert g.As16 is not None and g.Bblk16.shape == (g.n_total, g.r_total)
+        g_as, g_b = g.As16, g.Bblk16
+        g.As16 = None  # rebuild from the members for comparison
+        a2, b2 = g.factors(torch.bfloat16)
+        g.As16 = g_as
+        assert torch.equal(g_as, a2) and torch.equal(g_b, b2)
+        assert g.gradA.data_ptr() == g.members[0].lora_A.grad.data_ptr()
+    assert torch.equal(qkv.As16, As_ref) and torch.equal(qkv.Bblk16, B_ref)
+    # after an optimiser step the copies follow the fp32 factors
+    ids = torch.randint(0, 512, (2, 16))
+    labels = qlora.causal_labels(ids)
+    trainer.step(ids, labels, float((labels != -100).sum()))
+    g_b = gu.Bblk16.clone()
+    gu_as = gu.As16
+    gu.As16 = None
+    _, b2 = gu.factors(torch.bfloat16)
+    gu.As16 = gu_as
+    assert torch.equal(g_b, b2)

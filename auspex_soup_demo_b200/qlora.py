@@ -404,9 +404,11 @@ class LoRAProjectionGroup:
         return _LoRAGateUpFn.apply(x, self, bool(recompute), *self.params())
 
 
-def _group_gemm(group: LoRAProjectionGroup, x2: torch.Tensor, w: torch.Tensor, As16, Bblk):
-    """(y = x2 W^T + (x2 As^T) Bblk^T + bias [M, N], xa = x2 As^T)."""
-    xa = x2 @ As16.t()
+def _group_gemm(group: LoRAProjectionGroup, x2: torch.Tensor, w: torch.Tensor, As16, Bblk,
+                xa: Optional[torch.Tensor] = None):
+    """(y = x2 W^T + (x2 As^T) Bblk^T + bias [M, N], xa = x2 As^T); a given xa is reused."""
+    if xa is None:
+        xa = x2 @ As16.t()
     m = x2.shape[0]
     n = group.n_total
     bias = None if group.bias is None else group.bias.to(x2.dtype)
@@ -523,7 +525,7 @@ class _LoRAGateUpFn(torch.autograd.Function):
         inter = group.outs[0]
         w = group.base_weight(x2.dtype)
         if ctx.recompute:
-            y, _ = _group_gemm(group, x2, w, As16, Bblk)
+            y, _ = _group_gemm(group, x2, w, As16, Bblk, xa)
         else:
             y = saved[4]
         dh2 = dh.reshape(-1, inter)
@@ -636,7 +638,8 @@ class QLoRATrainer:
     """
 
     def __init__(self, model, lr: float = 2e-4, chunk: int = 64, ddp: bool = False,
-                 loss_fn=None, fused_adamw: Optional[bool] = None):
+                 loss_fn=None, fused_adamw: Optional[bool] = None, weight_decay: float = 0.0,
+                 optimizer: str = "auto"):
         from .kernels import make_triton_chunked_loss_function
 
         self.model = model
@@ -692,8 +695,23 @@ class QLoRATrainer:
             self._setup_groups(lora, offsets)
             self._refresh_param16()
         on_cuda = self.params[0].is_cuda
-        fused = on_cuda if fused_adamw is None else fused_adamw
-        self.opt = torch.optim.AdamW(self.params, lr=lr, fused=fused, capturable=on_cuda)
+        # AdamW (HF Trainer defaults: betas 0.9 / 0.999, eps 1e-8, weight decay 0).
+        # "soup": one soup_adamw_flat launch over the flat buffers that also
+        # writes the 16-bit copies; "torch": torch.optim.AdamW; "auto": soup on CUDA.
+        if optimizer not in ("auto", "soup", "torch"):
+            raise ValueError(f"optimizer must be auto, soup or torch, not {optimizer!r}")
+        self.lr, self.betas, self.eps, self.weight_decay = lr, (0.9, 0.999), 1e-8, weight_decay
+        if optimizer == "soup" or (optimizer == "auto" and on_cuda):
+            if not on_cuda:
+                raise ValueError("optimizer='soup' needs CUDA parameters")
+            self.exp_avg = torch.zeros_like(self.flat_param)
+            self.exp_avg_sq = torch.zeros_like(self.flat_param)
+            self.step_t = torch.zeros((), dtype=torch.float32, device=dev)
+            self.opt = None
+        else:
+            fused = on_cuda if fused_adamw is None else fused_adamw
+            self.opt = torch.optim.AdamW(self.params, lr=lr, betas=self.betas, eps=self.eps,
+                                         weight_decay=weight_decay, fused=fused, capturable=on_cuda)
         # loss_fn: an autograd Function with the reference's chunked-loss signature
         self.loss_fn = loss_fn or make_triton_chunked_loss_function()
         self.chunk = chunk
@@ -729,9 +747,26 @@ class QLoRATrainer:
         loss.backward()
         if self.ddp:
             self._allreduce_grads()
-        self.opt.step()
-        self._refresh_param16()  # forwards outside the trainer see the updated factors
+        if self.opt is None:
+            self._adamw_step()  # also rewrites the 16-bit copies
+            self._refresh_bblk()
+        else:
+            self.opt.step()
+            self._refresh_param16()  # forwards outside the trainer see the updated factors
         return loss.detach(), correct
+
+    def _adamw_step(self):
+        self.step_t.add_(1.0)
+        p16 = self.flat_param16
+        b1, b2 = self.betas
+        dev = self.flat_param.device
+        _lib.call("soup_adamw_flat", dev, self.flat_param.data_ptr(), self.flat_grad.data_ptr(),
+                  self.exp_avg.data_ptr(), self.exp_avg_sq.data_ptr(), self.flat_param.numel(),
+                  self.step_t.data_ptr(), self.lr, b1, b2, self.eps, self.weight_decay,
+                  None if p16 is None else p16.data_ptr(),
+                  _lib.dtype_code(p16.dtype) if p16 is not None else _lib.BF16,
+                  self.n_a if p16 is not None else 0, float(self.scaling or 1.0),
+                  _lib.stream_of(self.flat_param))
 
     def _setup_groups(self, lora, offsets):
         """Give every projection group (LoRAProjectionGroup) views of the flat
@@ -783,8 +818,11 @@ class QLoRATrainer:
             na = self.n_a
             torch.mul(self.flat_param[:na], self.scaling, out=self.flat_param16[:na])
             self.flat_param16[na:].copy_(self.flat_param[na:])
-            for dst, src in self._bblk_copies:
-                dst.copy_(src)
+            self._refresh_bblk()
+
+    def _refresh_bblk(self):
+        for dst, src in self._bblk_copies:
+            dst.copy_(src)
 
     def capture(self, input_ids: torch.Tensor, labels: torch.Tensor, denominator: float,
                 warmup: int = 3):

@@ -226,6 +226,20 @@ int soup_gemm_bf16_lora(const void* a, int64_t lda, int a_mn_major, const void* 
                         int64_t r, const void* bias, void* c, int64_t ldc, int c_dtype, int64_t m,
                         int64_t n, int64_t k, float alpha, int accumulate, void* stream);
 
+/* ---- AdamW over flat fp32 buffers (the QLoRA step's optimiser) ------------
+ * One pass over n elements: param, exp_avg, exp_avg_sq updated in place from
+ * grad with torch.optim.AdamW's decoupled weight decay; `step` is a device
+ * fp32 scalar holding the step count t including this update (so the call can
+ * be recorded in a CUDA graph). With param16 != NULL (BF16 or F16) the updated
+ * parameters are also written in 16 bits, the first n_scaled of them
+ * multiplied by `scale`. Replaces the reference trainer's optimiser step (HF
+ * Trainer AdamW over the peft LoRA parameters; `soup train` with
+ * task/task.yaml:10-22); the reference has no kernel of its own for it. */
+int soup_adamw_flat(float* param, const float* grad, float* exp_avg, float* exp_avg_sq, int64_t n,
+                    const float* step, float lr, float beta1, float beta2, float eps,
+                    float weight_decay, void* param16, int param16_dtype, int64_t n_scaled,
+                    float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -259,3 +259,34 @@ def test_grouped_projections_match_separate_modules(recompute, monkeypatch):
     for n, p in t2.model.named_parameters():
         if p.requires_grad:
             assert cosine(p1[n].grad, p.grad) > 0.99, n
+
+
+@pytest.mark.parametrize("n,n_scaled,wd", [(4096 * 37, 4096 * 5, 0.0), (100003, 77, 0.01)])
+def test_adamw_flat_matches_torch_adamw(n, n_scaled, wd):
+    # the fused flat-buffer AdamW (vector path for n % 4 == 0, scalar otherwise)
+    # against torch.optim.AdamW on the same parameters and gradients, 3 steps
+    g = torch.Generator(device="cuda").manual_seed(21)
+    p0 = torch.randn(n, device="cuda", generator=g)
+    grads = [torch.randn(n, device="cuda", generator=g) * (i + 1) for i in range(3)]
+    lr, scale = 2e-3, 2.0
+    ref = p0.clone().requires_grad_(True)
+    opt = torch.optim.AdamW([ref], lr=lr, weight_decay=wd, foreach=False, fused=False)
+    p, m, v = p0.clone(), torch.zeros_like(p0), torch.zeros_like(p0)
+    p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    step = torch.zeros((), device="cuda")
+    for gr in grads:
+        ref.grad = gr.clone()
+        opt.step()
+        step.add_(1.0)
+        _lib.call("soup_adamw_flat", p.device, p.data_ptr(), gr.data_ptr(), m.data_ptr(), v.data_ptr(), n,
+                  step.data_ptr(), lr, 0.9, 0.999, 1e-8, wd, p16.data_ptr(), _lib.BF16, n_scaled, scale,
+                  _lib.stream_of(p))
+    torch.cuda.synchronize()
+    st = opt.state[ref]
+    torch.testing.assert_close(p, ref.detach(), rtol=1e-5, atol=1e-7)
+    # the kernel rounds m + (1 - beta1) (g - m) once (FMA), torch twice: moments of
+    # O(1) differ by up to an ulp of their inputs where the update nearly cancels
+    torch.testing.assert_close(m, st["exp_avg"], rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(v, st["exp_avg_sq"], rtol=1e-5, atol=1e-6)
+    want16 = torch.cat([p[:n_scaled] * scale, p[n_scaled:]]).to(torch.bfloat16)
+    assert torch.equal(p16, want16)

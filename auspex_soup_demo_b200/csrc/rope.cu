@@ -50,21 +50,43 @@ __global__ void __launch_bounds__(256) rope_rows_kernel(RopeTensor q, RopeTensor
     const CT* cbp = cos + b * cb + d;
     const CT* sbp = sin + b * cb + d;
     Vec16<T> x1[P], x2[P];
-    float c[P][NE], sn[P][NE];
+    if constexpr (sizeof(CT) == sizeof(T)) {
+      // cos/sin rows stay packed until use (fewer registers, more CTAs per SM)
+      Vec16<CT> cv[P], sv[P];
 #pragma unroll
-    for (int p = 0; p < P; ++p) {
-      const int s = s0 + p;
-      if (s < S) {
-        x1[p] = ld16_stream(xb + s * t.ss);
-        x2[p] = ld16_stream(xb + s * t.ss + half);
-        if constexpr (sizeof(CT) == sizeof(T)) {
-          Vec16<CT> cv = ld16(cbp + s * cs), sv = ld16(sbp + s * cs);
+      for (int p = 0; p < P; ++p) {
+        const int s = s0 + p;
+        if (s < S) {
+          x1[p] = ld16_stream(xb + s * t.ss);
+          x2[p] = ld16_stream(xb + s * t.ss + half);
+          cv[p] = ld16(cbp + s * cs);
+          sv[p] = ld16(sbp + s * cs);
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        const int s = s0 + p;
+        if (s < S) {
+          Vec16<T> y1, y2;
 #pragma unroll
           for (int e = 0; e < NE; ++e) {
-            c[p][e] = Cvt<CT>::to_f(cv.v[e]);
-            sn[p][e] = sign * Cvt<CT>::to_f(sv.v[e]);
+            const float a = Cvt<T>::to_f(x1[p].v[e]), bb = Cvt<T>::to_f(x2[p].v[e]);
+            const float c = Cvt<CT>::to_f(cv[p].v[e]), sn = sign * Cvt<CT>::to_f(sv[p].v[e]);
+            y1.v[e] = Cvt<T>::from_f(a * c - bb * sn);
+            y2.v[e] = Cvt<T>::from_f(a * sn + bb * c);
           }
-        } else {
+          st16_stream(ob + s * t.os, y1);
+          st16_stream(ob + s * t.os + half, y2);
+        }
+      }
+    } else {
+      float c[P][NE], sn[P][NE];
+#pragma unroll
+      for (int p = 0; p < P; ++p) {
+        const int s = s0 + p;
+        if (s < S) {
+          x1[p] = ld16_stream(xb + s * t.ss);
+          x2[p] = ld16_stream(xb + s * t.ss + half);
 #pragma unroll
           for (int e = 0; e < NE; ++e) {
             c[p][e] = Cvt<CT>::to_f(cbp[s * cs + e]);
@@ -72,20 +94,20 @@ __global__ void __launch_bounds__(256) rope_rows_kernel(RopeTensor q, RopeTensor
           }
         }
       }
-    }
 #pragma unroll
-    for (int p = 0; p < P; ++p) {
-      const int s = s0 + p;
-      if (s < S) {
-        Vec16<T> y1, y2;
+      for (int p = 0; p < P; ++p) {
+        const int s = s0 + p;
+        if (s < S) {
+          Vec16<T> y1, y2;
 #pragma unroll
-        for (int e = 0; e < NE; ++e) {
-          const float a = Cvt<T>::to_f(x1[p].v[e]), bb = Cvt<T>::to_f(x2[p].v[e]);
-          y1.v[e] = Cvt<T>::from_f(a * c[p][e] - bb * sn[p][e]);
-          y2.v[e] = Cvt<T>::from_f(a * sn[p][e] + bb * c[p][e]);
+          for (int e = 0; e < NE; ++e) {
+            const float a = Cvt<T>::to_f(x1[p].v[e]), bb = Cvt<T>::to_f(x2[p].v[e]);
+            y1.v[e] = Cvt<T>::from_f(a * c[p][e] - bb * sn[p][e]);
+            y2.v[e] = Cvt<T>::from_f(a * sn[p][e] + bb * c[p][e]);
+          }
+          st16_stream(ob + s * t.os, y1);
+          st16_stream(ob + s * t.os + half, y2);
         }
-        st16_stream(ob + s * t.os, y1);
-        st16_stream(ob + s * t.os + half, y2);
       }
     }
   }

@@ -154,6 +154,140 @@ struct EpiStore {
   }
 };
 
+// A 32 x 32 bf16 block of C (rows [row0, row0+32), cols [col0, col0+32),
+// 16-byte aligned rows) in two steps, so the global loads can be in flight
+// while the warp does other work: load_block_bf16 issues the loads (lane l
+// takes rows 4i + l/8, columns 4 (l%8) .. +3; rows beyond M read as 0),
+// stage_block_bf16 puts them into the warp's staging block as fp32 (the
+// inverse of write_block's access pattern).
+__device__ __forceinline__ void load_block_bf16(uint2 (&r)[8], int lane, const bf16* C, int64_t ldc,
+                                                int row0, int M, int col0) {
+  const int cv = lane & 7;
+  const int rsub = lane >> 3;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int grow = row0 + i * 4 + rsub;
+    r[i] = grow < M ? *reinterpret_cast<const uint2*>(C + (int64_t)grow * ldc + col0 + cv * 4)
+                    : make_uint2(0u, 0u);
+  }
+}
+__device__ __forceinline__ void stage_block_bf16(uint8_t* stage, int lane, const uint2 (&r)[8]) {
+  const int cv = lane & 7;
+  const int rsub = lane >> 3;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r[i]);
+    const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    *reinterpret_cast<float4*>(stage + stage_off(i * 4 + rsub, cv)) = make_float4(a.x, a.y, b.x, b.y);
+  }
+}
+
+// SwiGLU epilogue of a gate/up GEMM whose weight rows are interleaved in
+// blocks of 128 (rows [256 c, 256 c + 128) = gate rows [128 c, 128 c + 128),
+// the next 128 = the same up rows): tile nt's 256 columns hold g (0-127) and
+// u (128-255) for intermediate columns [128 nt, 128 nt + 128). g and u are
+// first rounded to bf16 (+ bias) exactly as a plain bf16 GEMM output would be,
+// so the results equal the unfused GEMM + SwiGLU kernels bit for bit.
+//   mode 0: h = silu(g) u -> h [M, N/2]; with y != nullptr also g, u -> y [M, N]
+//   mode 1: dh from h [M, N/2]; dg, du -> y [M, N] at the tile's g / u columns
+template <int BN>
+struct EpiSwiGLU {
+  struct Params {
+    int mode;
+    bf16* h;  // mode 0: output h; mode 1: input dh
+    int64_t ldh;
+    bf16* y;  // mode 0: optional [g | u] copy; mode 1: output [dg | du]
+    int64_t ldy;
+    const bf16* bias;  // [N] in the interleaved order, or nullptr
+    int M, N;
+  };
+  // mode 1: the dh block of a warp's next chunk is in flight while the warp
+  // waits (for the tile's accumulator, or on the previous chunk's work)
+  struct Carry {
+    uint2 d[8];
+  };
+  static __device__ __forceinline__ void prefetch(const Params& p, int row_base, int nt, int quarter,
+                                                  int lane, int group, int ngroups, Carry& c) {
+    constexpr int kHalf = BN / 2;
+    if (p.mode == 1)
+      load_block_bf16(c.d, lane, p.h, p.ldh, row_base + quarter * 32, p.M,
+                      nt * kHalf + group * (kHalf / 32 / ngroups) * 32);
+  }
+  static __device__ __forceinline__ void tile(const Params& p, int row_base, int nt, int ks,
+                                              int quarter, int lane, uint32_t taddr, uint8_t* stage,
+                                              int group, int ngroups, Carry& carry) {
+    constexpr int kHalf = BN / 2;
+    const int row0 = row_base + quarter * 32;
+    const int nch = kHalf / 32 / ngroups;
+    const int inter = p.N / 2;
+    uint2 (&dnext)[8] = carry.d;
+#pragma unroll 1
+    for (int cc = group * nch; cc < (group + 1) * nch; ++cc) {
+      float g[32], u[32];
+      tmem_ld32(taddr + cc * 32, g);
+      tmem_ld32(taddr + kHalf + cc * 32, u);
+      const int gcol = nt * BN + cc * 32;  // g's columns in [M, N]; u's are kHalf further
+      const int icol = nt * kHalf + cc * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float bg = p.bias ? __bfloat162float(p.bias[gcol + j]) : 0.f;
+        const float bu = p.bias ? __bfloat162float(p.bias[gcol + kHalf + j]) : 0.f;
+        g[j] = __bfloat162float(__float2bfloat16_rn(p.bias ? fmaf(1.f, g[j], bg) : g[j]));
+        u[j] = __bfloat162float(__float2bfloat16_rn(p.bias ? fmaf(1.f, u[j], bu) : u[j]));
+      }
+      if (p.mode == 0) {
+        if (p.y) {
+          stage_row(stage, lane, g, 1.f);
+          __syncwarp();
+          write_block<true>(stage, lane, p.y, p.ldy, row0, p.M, gcol, p.N, true, false);
+          __syncwarp();
+          stage_row(stage, lane, u, 1.f);
+          __syncwarp();
+          write_block<true>(stage, lane, p.y, p.ldy, row0, p.M, gcol + kHalf, p.N, true, false);
+          __syncwarp();
+        }
+        float hv[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) hv[j] = swiglu_fwd_f(g[j], u[j]);
+        stage_row(stage, lane, hv, 1.f);
+        __syncwarp();
+        write_block<true>(stage, lane, p.h, p.ldh, row0, p.M, icol, inter, true, false);
+        __syncwarp();
+      } else {
+        stage_block_bf16(stage, lane, dnext);
+        if (cc + 1 < (group + 1) * nch)
+          load_block_bf16(dnext, lane, p.h, p.ldh, row0, p.M, icol + 32);
+        __syncwarp();
+        float d[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 x = *reinterpret_cast<const float4*>(stage + stage_off(lane, q));
+          d[4 * q] = x.x;
+          d[4 * q + 1] = x.y;
+          d[4 * q + 2] = x.z;
+          d[4 * q + 3] = x.w;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float dg, du;
+          swiglu_bwd_f(d[j], g[j], u[j], dg, du);
+          g[j] = dg;
+          u[j] = du;
+        }
+        stage_row(stage, lane, g, 1.f);
+        __syncwarp();
+        write_block<true>(stage, lane, p.y, p.ldy, row0, p.M, gcol, p.N, true, false);
+        __syncwarp();
+        stage_row(stage, lane, u, 1.f);
+        __syncwarp();
+        write_block<true>(stage, lane, p.y, p.ldy, row0, p.M, gcol + kHalf, p.N, true, false);
+        __syncwarp();
+      }
+    }
+  }
+};
+
 // Logits epilogue of the CE forward: online-softmax state per (row, tile),
 // target logit capture, bf16 logits store.
 template <int BN>
@@ -1055,6 +1189,49 @@ int soup_gemm_bf16_lora(const void* a, int64_t lda, int a_mn_major, const void* 
   if (!a_mn_major && b_mn_major) return launch_gemm<false, true, E>(ma, mb, ma2, mb2, sc, ep, stream);
   if (a_mn_major && !b_mn_major) return launch_gemm<true, false, E>(ma, mb, ma2, mb2, sc, ep, stream);
   return launch_gemm<true, true, E>(ma, mb, ma2, mb2, sc, ep, stream);
+}
+
+int soup_gemm_bf16_lora_swiglu(const void* a, int64_t lda, const void* b, int64_t ldb,
+                               const void* a2, int64_t lda2, const void* b2, int64_t ldb2, int64_t r,
+                               const void* bias, int mode, void* h, int64_t ldh, void* y, int64_t ldy,
+                               int64_t m, int64_t inter, int64_t k, void* stream_) {
+  const int64_t n = 2 * inter;
+  if (!a || !b || !h || m <= 0 || inter <= 0 || k <= 0 || m > (1 << 30) || n > (1 << 30) ||
+      k > (1 << 30) || r < 0 || r > 4096 || (r > 0 && (!a2 || !b2)) || (mode != 0 && mode != 1) ||
+      (mode == 1 && !y)) {
+    set_last_error("soup_gemm_bf16_lora_swiglu: bad arguments");
+    return SOUP_ERR_INVALID;
+  }
+  if (inter % (kBN / 2) != 0) {
+    set_last_error("soup_gemm_bf16_lora_swiglu: the intermediate size must be a multiple of 128");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  if (lda < k || ldb < k || ldh < inter || (y && ldy < n) || (r > 0 && (lda2 < r || ldb2 < r))) {
+    set_last_error("soup_gemm_bf16_lora_swiglu: leading dimension too small");
+    return SOUP_ERR_INVALID;
+  }
+  if (!tma_ok(a, lda) || !tma_ok(b, ldb) || (r > 0 && (!tma_ok(a2, lda2) || !tma_ok(b2, ldb2))) ||
+      !aligned16(h) || (ldh * 2) % 16 != 0 || (y && (!aligned16(y) || (ldy * 2) % 16 != 0))) {
+    set_last_error("soup_gemm_bf16_lora_swiglu: operands need 16-byte aligned rows");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  CUtensorMap ma, mb, ma2, mb2;
+  int rc;
+  if ((rc = make_operand_map(&ma, a, false, m, k, lda, BM))) return rc;
+  if ((rc = make_operand_map(&mb, b, false, n, k, ldb, b_box_rows()))) return rc;
+  if (r > 0) {
+    if ((rc = make_operand_map(&ma2, a2, false, m, r, lda2, BM))) return rc;
+    if ((rc = make_operand_map(&mb2, b2, false, n, r, ldb2, b_box_rows()))) return rc;
+  } else {
+    ma2 = ma;
+    mb2 = mb;
+  }
+  EpiSwiGLU<kBN>::Params ep{mode, static_cast<bf16*>(h), ldh, static_cast<bf16*>(y), ldy,
+                            static_cast<const bf16*>(bias), (int)m, (int)n};
+  const int mt = m_tiles(m), nt = (int)(n / kBN);
+  const int kb1 = (int)((k + BK - 1) / BK), kb2 = (int)((r + BK - 1) / BK);
+  Sched sc{mt, nt, 1, kb1 + kb2, nt > mt ? 0 : 1, kb2};
+  return launch_gemm<false, false, EpiSwiGLU<kBN>>(ma, mb, ma2, mb2, sc, ep, as_stream(stream_));
 }
 
 }  // extern "C"

@@ -114,6 +114,24 @@ __device__ __forceinline__ float fast_exp2(float x) {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
+// SwiGLU arithmetic shared by the elementwise kernels and the gate/up GEMM
+// epilogue, so both give identical results (solution/kernels/swiglu.py:20-95):
+// out = silu(g) u, du = dy silu(g), dg = dy u sigmoid(g) (1 + g (1 - sigmoid(g))).
+// The sigmoid uses the hardware exponential and an approximate reciprocal
+// division (like the reference's Triton sigmoid): the epilogue evaluates it on
+// only 8 warps per SM, where an IEEE division would outlast the MMA of a tile.
+// For g -> -inf the divisor overflows and the result is the limit 0.
+__device__ __forceinline__ float swiglu_sigmoid(float g) { return __fdividef(1.0f, 1.0f + __expf(-g)); }
+__device__ __forceinline__ float swiglu_fwd_f(float g, float u) {
+  const float sg = swiglu_sigmoid(g);
+  return (g * sg) * u;
+}
+__device__ __forceinline__ void swiglu_bwd_f(float d, float g, float u, float& dg, float& du) {
+  const float sg = swiglu_sigmoid(g);
+  du = d * (g * sg);
+  dg = d * u * sg * (1.0f + g * (1.0f - sg));
+}
+
 // Online-softmax state of one row segment: running max m, s = sum exp(z-m),
 // w = sum z*exp(z-m), first index of the maximum.
 struct SoftmaxState {

@@ -10,15 +10,11 @@
 namespace soup {
 namespace {
 
-__device__ __forceinline__ float sigmoidf_(float g) { return 1.0f / (1.0f + __expf(-g)); }
-
 template <typename T>
 struct FwdOp {
   static constexpr int kIn = 2, kOut = 1;
   __device__ __forceinline__ static void apply(const float (&in)[kIn], float (&out)[kOut]) {
-    const float g = in[0], u = in[1];
-    const float sg = sigmoidf_(g);
-    out[0] = (g * sg) * u;
+    out[0] = swiglu_fwd_f(in[0], in[1]);
   }
 };
 
@@ -26,10 +22,7 @@ template <typename T>
 struct BwdOp {
   static constexpr int kIn = 3, kOut = 2;  // (dy, g, u) -> (dg, du)
   __device__ __forceinline__ static void apply(const float (&in)[kIn], float (&out)[kOut]) {
-    const float d = in[0], g = in[1], u = in[2];
-    const float sg = sigmoidf_(g);
-    out[1] = d * (g * sg);
-    out[0] = d * u * sg * (1.0f + g * (1.0f - sg));
+    swiglu_bwd_f(in[0], in[1], in[2], out[0], out[1]);
   }
 };
 

@@ -35,10 +35,29 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "soup_common.cuh"
 
 namespace soup {
 namespace tc {
+
+// An epilogue may declare `struct Carry` and
+//   static void prefetch(const Params&, int row_base, int nt, int quarter, int lane,
+//                        int group, int ngroups, Carry&);
+// the kernel then calls prefetch for each tile before waiting for its
+// accumulator (to start global loads the epilogue will need) and passes the
+// Carry to tile() as its last argument.
+template <class Epi, class = void>
+struct EpiCarry {
+  struct type {};
+  static constexpr bool kHas = false;
+};
+template <class Epi>
+struct EpiCarry<Epi, std::void_t<typename Epi::Carry>> {
+  using type = typename Epi::Carry;
+  static constexpr bool kHas = true;
+};
 
 constexpr int BM = 128;
 constexpr int BK = 64;
@@ -423,10 +442,13 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     constexpr int kGroups = EPI_WARPS / 4;
     const int group = e >> 2;
     uint8_t* stage = smem + L::kEpiOff + e * kEpiWarpBytes;
+    typename EpiCarry<Epi>::type carry{};
     uint32_t lt = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++lt) {
       int mt, nt, ks;
       sched.decode(u, mt, nt, ks);
+      if constexpr (EpiCarry<Epi>::kHas)
+        Epi::prefetch(ep, mt * BM, nt, quarter, lane, group, kGroups, carry);
       const uint32_t acc = lt & 1u;
       const uint32_t acc_ph = (lt >> 1) & 1u;
       bool ok = true;
@@ -435,7 +457,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      Epi::tile(ep, mt * BM, nt, ks, quarter, lane, taddr, stage, group, kGroups);
+      if constexpr (EpiCarry<Epi>::kHas)
+        Epi::tile(ep, mt * BM, nt, ks, quarter, lane, taddr, stage, group, kGroups, carry);
+      else
+        Epi::tile(ep, mt * BM, nt, ks, quarter, lane, taddr, stage, group, kGroups);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
@@ -707,10 +732,14 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     constexpr int kGroups = EPI_WARPS / 4;
     const int group = e >> 2;
     uint8_t* stage = smem + L::kEpiOff + e * kEpiWarpBytes;
+    typename EpiCarry<Epi>::type carry{};
     uint32_t lt = 0;
     for (int u = cluster; u < n_units; u += n_clusters, ++lt) {
       int mt, nt, ks;
       sched.decode(u, mt, nt, ks);
+      const int row_base = mt * 2 * BM + static_cast<int>(rank) * BM;
+      if constexpr (EpiCarry<Epi>::kHas)
+        Epi::prefetch(ep, row_base, nt, quarter, lane, group, kGroups, carry);
       const uint32_t acc = lt & 1u;
       const uint32_t acc_ph = (lt >> 1) & 1u;
       bool ok = true;
@@ -719,8 +748,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      Epi::tile(ep, mt * 2 * BM + static_cast<int>(rank) * BM, nt, ks, quarter, lane, taddr, stage,
-                group, kGroups);
+      if constexpr (EpiCarry<Epi>::kHas)
+        Epi::tile(ep, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups, carry);
+      else
+        Epi::tile(ep, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(tempty_bar(acc), 0));

@@ -107,6 +107,9 @@ def _accumulate_grad(param: torch.Tensor, m1: torch.Tensor, m2: torch.Tensor, al
 # the persistent kernel's last wave of 256 x 256 tiles mostly idle.
 FUSED_MAX_K = 4096
 
+# Row-block size of the interleaved gate/up weight layout (half a GEMM tile).
+IL_BLOCK = 128
+
 
 def _fused_ok(k: int, *ts: torch.Tensor) -> bool:
     if k > FUSED_MAX_K:
@@ -252,6 +255,9 @@ class LoRANF4Linear(_LoRABase):
         self._init_lora(linear, r, alpha, lora_dtype)
 
     def dequantized_weight(self, dtype=torch.bfloat16) -> torch.Tensor:
+        g = self.lora_group
+        if g is not None and g.interleaved:  # the packed rows are a strided view
+            return g.member_weight(self, dtype)
         return nf4_dequantize(self.packed, self.absmax, (self.out_features, self.in_features), dtype)
 
     def base_weight(self, dtype) -> torch.Tensor:
@@ -268,7 +274,7 @@ class LoRADenseLinear(_LoRABase):
         self._init_lora(linear, r, alpha, lora_dtype)
 
     def base_weight(self, dtype) -> torch.Tensor:
-        return self.weight.to(dtype)
+        return self.weight.reshape(self.out_features, self.in_features).to(dtype)
 
 
 class LoRAProjectionGroup:
@@ -310,7 +316,14 @@ class LoRAProjectionGroup:
         scal = {m.scaling for m in self.members}
         self.scaling = scal.pop() if len(scal) == 1 else None
         self.nf4 = all(isinstance(m, LoRANF4Linear) for m in self.members)
-        if self.nf4:
+        # gate/up rows interleaved in blocks of IL_BLOCK (gate block c, then up block
+        # c) so every 256-column GEMM tile holds g and u of the same 128 columns and
+        # SwiGLU runs in the GEMM epilogue (soup_gemm_bf16_lora_swiglu)
+        self.interleaved = (kind == "gate_up" and len(self.members) == 2 and self.outs[0] == self.outs[1]
+                            and self.outs[0] % IL_BLOCK == 0 and self.in_features % 64 == 0)
+        if self.interleaved:
+            self._init_interleaved()
+        elif self.nf4:
             self.packed = torch.cat([m.packed for m in self.members])
             self.absmax = torch.cat([m.absmax for m in self.members])
             po = ao = 0
@@ -325,7 +338,9 @@ class LoRAProjectionGroup:
             self.weight = torch.cat([m.weight for m in self.members])
             for m, a, b in zip(self.members, self.out_off[:-1], self.out_off[1:]):
                 m._buffers["weight"] = self.weight[a:b]
-        if any(m.bias is not None for m in self.members):
+        if self.interleaved:
+            pass  # bias set by _init_interleaved
+        elif any(m.bias is not None for m in self.members):
             self.bias = torch.cat([m.bias if m.bias is not None else
                                    torch.zeros(m.out_features, dtype=self.members[0].lora_A.dtype
                                                if self.members[0].bias is None else self.members[0].bias.dtype,
@@ -345,6 +360,44 @@ class LoRAProjectionGroup:
         for m in self.members:
             m.lora_group = self
 
+    def _il_view(self, t: torch.Tensor, width: int) -> torch.Tensor:
+        """[2 * inter, width] rows in interleaved order viewed as [blocks, 2, IL_BLOCK, width]."""
+        return t.view(self.outs[0] // IL_BLOCK, 2, IL_BLOCK, width)
+
+    def _init_interleaved(self):
+        nb = self.outs[0] // IL_BLOCK
+        k = self.in_features
+
+        def inter(ts, width):
+            return torch.stack([t.reshape(nb, IL_BLOCK, width) for t in ts], dim=1).reshape(-1)
+
+        if self.nf4:
+            self.packed = inter([m.packed for m in self.members], k // 2)
+            self.absmax = inter([m.absmax for m in self.members], k // 64)
+            pv, av = self._il_view(self.packed, k // 2), self._il_view(self.absmax, k // 64)
+            for j, m in enumerate(self.members):
+                m._buffers["packed"] = pv[:, j]
+                m._buffers["absmax"] = av[:, j]
+        else:
+            self.weight = inter([m.weight for m in self.members], k).view(2 * self.outs[0], k)
+            wv = self._il_view(self.weight, k)
+            for j, m in enumerate(self.members):
+                m._buffers["weight"] = wv[:, j]
+        if any(m.bias is not None for m in self.members):
+            ref = next(m.bias for m in self.members if m.bias is not None)
+            self.bias = inter([m.bias if m.bias is not None else torch.zeros_like(ref)
+                               for m in self.members], 1)
+        else:
+            self.bias = None
+
+    def member_weight(self, member, dtype) -> torch.Tensor:
+        """One member's base weight [out, in] (dequantised from the group's buffer)."""
+        j = self.members.index(member)
+        w = self.base_weight(dtype)
+        if self.interleaved:
+            return self._il_view(w, self.in_features)[:, j].reshape(self.outs[j], self.in_features)
+        return w[self.out_off[j]:self.out_off[j + 1]]
+
     # -- operands ---------------------------------------------------------------
     def base_weight(self, dtype) -> torch.Tensor:
         if self.nf4:
@@ -358,8 +411,12 @@ class LoRAProjectionGroup:
         As = torch.cat([(m.lora_A.detach() * m.scaling).to(dtype) for m in self.members])
         Bblk = torch.zeros(self.n_total, self.r_total, dtype=dtype, device=As.device)
         for j, m in enumerate(self.members):
-            Bblk[self.out_off[j]:self.out_off[j + 1], self.rank_off[j]:self.rank_off[j + 1]] = \
-                m.lora_B.detach().to(dtype)
+            r0, r1 = self.rank_off[j], self.rank_off[j + 1]
+            if self.interleaved:
+                self._il_view(Bblk, self.r_total)[:, j, :, r0:r1] = \
+                    m.lora_B.detach().to(dtype).view(-1, IL_BLOCK, r1 - r0)
+            else:
+                Bblk[self.out_off[j]:self.out_off[j + 1], r0:r1] = m.lora_B.detach().to(dtype)
         return As, Bblk
 
     def out_features_of(self, j: int) -> int:
@@ -442,6 +499,11 @@ def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tens
             for j in range(len(group.members))):
         torch.addmm(group.gradA, dxa.t(), x2, alpha=group.scaling, out_dtype=torch.float32, out=group.gradA)
         gA_done = True
+    # interleaved rows: one product G = dy^T xa [N, R], member j's gradient is its
+    # row blocks and rank columns of G
+    G = None
+    if group.interleaved and any(need_params[2 * j + 1] for j in range(len(group.members))):
+        G = torch.mm(dy.t(), xa, out_dtype=torch.float32)
     for j, mem in enumerate(group.members):
         r0, r1 = group.rank_off[j], group.rank_off[j + 1]
         o0, o1 = group.out_off[j], group.out_off[j + 1]
@@ -449,7 +511,15 @@ def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tens
         if need_params[2 * j] and not gA_done:
             gA = _accumulate_grad(mem.lora_A, dxa[:, r0:r1].t(), x2, mem.scaling)
         if need_params[2 * j + 1]:
-            gB = _accumulate_grad(mem.lora_B, dy[:, o0:o1].t(), xa[:, r0:r1], 1.0)
+            if G is not None:
+                part = group._il_view(G, group.r_total)[:, j, :, r0:r1]
+                g = mem.lora_B.grad
+                if g is not None and g.is_cuda and g.dtype == torch.float32 and g.is_contiguous():
+                    g.view(part.shape).add_(part)
+                else:
+                    gB = part.reshape(group.outs[j], r1 - r0).to(mem.lora_B.dtype)
+            else:
+                gB = _accumulate_grad(mem.lora_B, dy[:, o0:o1].t(), xa[:, r0:r1], 1.0)
         grads += [gA, gB]
     return dx, grads
 
@@ -487,12 +557,43 @@ class _LoRAGroupFn(torch.autograd.Function):
         return (dx, None, *grads)
 
 
+def _gu_views(group: LoRAProjectionGroup, y: torch.Tensor):
+    """(g, u) row views of a gate/up output [M, 2 * inter]: column halves, or, with
+    interleaved rows, [M * blocks, 2 * IL_BLOCK] rows split in half."""
+    inter = group.outs[0]
+    if group.interleaved:
+        y2 = y.view(-1, 2 * IL_BLOCK)
+        return y2[:, :IL_BLOCK], y2[:, IL_BLOCK:]
+    return y[:, :inter], y[:, inter:]
+
+
+def swiglu_gemm(x2, w, xa, Bblk, bias, mode: int, h, y=None):
+    """soup_gemm_bf16_lora_swiglu: the interleaved gate/up GEMM with SwiGLU (mode 0:
+    h = silu(g) u, optionally [g | u] into y) or its backward (mode 1: h holds dh,
+    dg / du into y) in the epilogue."""
+    m, k = x2.shape
+    inter = w.shape[0] // 2
+    _lib.call("soup_gemm_bf16_lora_swiglu", x2.device, x2.data_ptr(), x2.stride(0), w.data_ptr(),
+              w.stride(0), xa.data_ptr(), xa.stride(0), Bblk.data_ptr(), Bblk.stride(0), xa.shape[1],
+              None if bias is None else bias.data_ptr(), mode, h.data_ptr(), h.stride(0),
+              None if y is None else y.data_ptr(), 0 if y is None else y.stride(0), m, inter, k,
+              _lib.stream_of(x2))
+
+
+def _swiglu_fused_ok(group, x2, w, xa, Bblk, bias, *outs) -> bool:
+    return (group.interleaved and _fused_ok(x2.shape[1], x2, w, xa, Bblk,
+                                            bias.view(1, -1) if bias is not None else None, *outs))
+
+
 class _LoRAGateUpFn(torch.autograd.Function):
     """h = silu(g) * u with [g | u] = one group GEMM of x (gate/up group).
 
+    With interleaved gate/up rows the SwiGLU runs in the GEMM epilogue
+    (soup_gemm_bf16_lora_swiglu): the forward writes only h, and the
+    recompute-backward turns dh straight into [dg | du] without storing g, u.
     With ``recompute`` the forward keeps only x and the rank-R product xa; the
-    backward dequantises the weights once, recomputes [g | u] and uses the
-    same weights for dx. Without it [g | u] is kept from the forward.
+    backward dequantises the weights once for the recompute and dx. Without it
+    [g | u] is kept from the forward.
     """
 
     @staticmethod
@@ -500,12 +601,23 @@ class _LoRAGateUpFn(torch.autograd.Function):
         from .kernels.swiglu import swiglu_forward
 
         k = group.in_features
+        inter = group.outs[0]
         x2 = x.reshape(-1, k)
+        m = x2.shape[0]
         w = group.base_weight(x.dtype)
         As16, Bblk = group.factors(x.dtype)
-        y, xa = _group_gemm(group, x2, w, As16, Bblk)
-        inter = group.outs[0]
-        h = swiglu_forward(y[:, :inter], y[:, inter:])
+        bias = None if group.bias is None else group.bias.to(x2.dtype)
+        h = torch.empty(m, inter, device=x.device, dtype=x.dtype)
+        y = None
+        xa = x2 @ As16.t()
+        if _swiglu_fused_ok(group, x2, w, xa, Bblk, bias, h):
+            if not recompute:
+                y = torch.empty(m, group.n_total, device=x.device, dtype=x.dtype)
+            swiglu_gemm(x2, w, xa, Bblk, bias, 0, h, y)
+        else:
+            y, _ = _group_gemm(group, x2, w, As16, Bblk, xa)
+            g, u = _gu_views(group, y)
+            swiglu_forward(g, u, out=h.view(g.shape[0], g.shape[1]))
         ctx.recompute = recompute
         if recompute:
             ctx.save_for_backward(x2, xa, As16, Bblk)
@@ -524,17 +636,23 @@ class _LoRAGateUpFn(torch.autograd.Function):
         x2, xa, As16, Bblk = saved[:4]
         inter = group.outs[0]
         w = group.base_weight(x2.dtype)
-        if ctx.recompute:
-            y, _ = _group_gemm(group, x2, w, As16, Bblk, xa)
-        else:
-            y = saved[4]
         dh2 = dh.reshape(-1, inter)
-        if dh2.stride(1) != 1:
+        if dh2.stride(1) != 1 or dh2.stride(0) != inter:
             dh2 = dh2.contiguous()
-        if dh2.dtype != y.dtype:
-            dh2 = dh2.to(y.dtype)
-        dy = torch.empty_like(y)
-        swiglu_backward(dh2, y[:, :inter], y[:, inter:], dg=dy[:, :inter], du=dy[:, inter:])
+        if dh2.dtype != x2.dtype:
+            dh2 = dh2.to(x2.dtype)
+        bias = None if group.bias is None else group.bias.to(x2.dtype)
+        dy = torch.empty(x2.shape[0], group.n_total, device=x2.device, dtype=x2.dtype)
+        if ctx.recompute and _swiglu_fused_ok(group, x2, w, xa, Bblk, bias, dh2, dy):
+            swiglu_gemm(x2, w, xa, Bblk, bias, 1, dh2, dy)
+        else:
+            if ctx.recompute:
+                y, _ = _group_gemm(group, x2, w, As16, Bblk, xa)
+            else:
+                y = saved[4]
+            g, u = _gu_views(group, y)
+            dg, du = _gu_views(group, dy)
+            swiglu_backward(dh2.view(g.shape[0], g.shape[1]), g, u, dg=dg, du=du)
         dx, grads = _group_backward(group, dy, x2, xa, w, As16, Bblk, ctx.needs_input_grad[0],
                                     ctx.needs_input_grad[3:])
         if dx is not None:
@@ -793,25 +911,36 @@ class QLoRATrainer:
             n_a = g.r_total * g.in_features
             g.As16 = self.flat_param16[a_offs[0]:a_offs[0] + n_a].view(g.r_total, g.in_features)
             g.gradA = self.flat_grad[a_offs[0]:a_offs[0] + n_a].view(g.r_total, g.in_features)
-            key = (g.kind, tuple(g.outs), tuple(g.ranks), g.in_features)
+            key = (g.kind, tuple(g.outs), tuple(g.ranks), g.in_features, g.interleaved)
             kinds.setdefault(key, []).append((g, b_offs))
         for key, items in kinds.items():
             g0 = items[0][0]
             buf = torch.zeros(len(items), g0.n_total, g0.r_total, dtype=self.flat_param16.dtype, device=dev)
             for l, (g, _) in enumerate(items):
                 g.Bblk16 = buf[l]
+            L, R = len(items), g0.r_total
             for j in range(len(g0.members)):
                 n_j, r_j = g0.outs[j], g0.ranks[j]
                 o0, c0 = g0.out_off[j], g0.rank_off[j]
                 offs = [b[j] for _, b in items]
                 stride = offs[1] - offs[0] if len(offs) > 1 else n_j * r_j
+                # member j's rows of the block-diagonal B: a contiguous row range, or
+                # (interleaved gate/up) every other block of IL_BLOCK rows
+                if g0.interleaved:
+                    nb = n_j // IL_BLOCK
+                    dst_all = buf.view(L, nb, 2, IL_BLOCK, R)[:, :, j, :, c0:c0 + r_j]
+                    src_shape = (nb, IL_BLOCK, r_j)
+                else:
+                    dst_all = buf[:, o0:o0 + n_j, c0:c0 + r_j]
+                    src_shape = (n_j, r_j)
                 if all(offs[l] == offs[0] + l * stride for l in range(len(offs))):
-                    src = self.flat_param16.as_strided((len(offs), n_j, r_j), (stride, r_j, 1), offs[0])
-                    self._bblk_copies.append((buf[:, o0:o0 + n_j, c0:c0 + r_j], src))
+                    src = self.flat_param16.as_strided((L, *src_shape), (stride, *torch.empty(src_shape).stride()),
+                                                       offs[0])
+                    self._bblk_copies.append((dst_all, src))
                 else:
                     for l, off in enumerate(offs):
-                        src = self.flat_param16[off:off + n_j * r_j].view(n_j, r_j)
-                        self._bblk_copies.append((buf[l, o0:o0 + n_j, c0:c0 + r_j], src))
+                        src = self.flat_param16[off:off + n_j * r_j].view(src_shape)
+                        self._bblk_copies.append((dst_all[l], src))
 
     def _refresh_param16(self):
         if self.flat_param16 is not None:

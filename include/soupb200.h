@@ -226,6 +226,27 @@ int soup_gemm_bf16_lora(const void* a, int64_t lda, int a_mn_major, const void* 
                         int64_t r, const void* bias, void* c, int64_t ldc, int c_dtype, int64_t m,
                         int64_t n, int64_t k, float alpha, int accumulate, void* stream);
 
+/* ---- Gate/up GEMM of a SwiGLU MLP with the activation in its epilogue ------
+ * B = gate and up weights [2*inter, k] (K-major, bf16) with their rows
+ * interleaved in blocks of 128: rows [256c, 256c+128) are gate rows
+ * [128c, 128c+128) and the next 128 the same up rows; A = x [m, k]; the
+ * optional rank-r segment (a2 [m, r], b2 [2*inter, r], same row order as B)
+ * and bias ([2*inter], same order) as in soup_gemm_bf16_lora. Each 256-column
+ * tile holds g and u for 128 intermediate columns; they are rounded to bf16
+ * as a plain GEMM output would be, then
+ *   mode 0: h = silu(g) * u -> h [m, inter] (row stride ldh); with y != NULL
+ *           g and u also go to y [m, 2*inter] (row stride ldy, B's row order)
+ *   mode 1: h holds dh [m, inter]; dg, du -> y [m, 2*inter] (B's row order)
+ * with the arithmetic of soup_swiglu_fwd / soup_swiglu_bwd (bit-identical to
+ * the unfused GEMM + SwiGLU kernels). inter % 128 == 0; rows 16-byte aligned.
+ * Replaces the reference MLP's gate_proj / up_proj GEMMs plus its SwiGLU
+ * kernels (solution/kernels/swiglu.py:20-95, 173-221), where the gate/up
+ * outputs make a round trip through memory. */
+int soup_gemm_bf16_lora_swiglu(const void* a, int64_t lda, const void* b, int64_t ldb,
+                               const void* a2, int64_t lda2, const void* b2, int64_t ldb2, int64_t r,
+                               const void* bias, int mode, void* h, int64_t ldh, void* y, int64_t ldy,
+                               int64_t m, int64_t inter, int64_t k, void* stream);
+
 /* ---- AdamW over flat fp32 buffers (the QLoRA step's optimiser) ------------
  * One pass over n elements: param, exp_avg, exp_avg_sq updated in place from
  * grad with torch.optim.AdamW's decoupled weight decay; `step` is a device

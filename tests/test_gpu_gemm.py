@@ -183,3 +183,40 @@ def test_gemm_single_cta_mode():
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "single-cta ok" in r.stdout
+
+
+@pytest.mark.parametrize("m,inter,k,with_bias", [(300, 384, 192, True), (2048, 8960, 1536, False)])
+def test_swiglu_epilogue_gemm_equals_gemm_plus_swiglu_kernels(m, inter, k, with_bias):
+    # soup_gemm_bf16_lora_swiglu (SwiGLU in the tcgen05 GEMM epilogue, interleaved
+    # gate/up rows) against the same GEMM with a plain store followed by the SwiGLU
+    # kernels: bit-identical h, [g | u] and [dg | du]
+    from auspex_soup_demo_b200 import qlora
+    from auspex_soup_demo_b200.kernels.swiglu import swiglu_backward, swiglu_forward
+
+    g = torch.Generator(device="cuda").manual_seed(m + k)
+    x = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (0.05 * torch.randn(2 * inter, k, device="cuda", generator=g)).bfloat16()
+    xa = torch.randn(m, 32, device="cuda", generator=g).bfloat16()
+    bblk = (0.05 * torch.randn(2 * inter, 32, device="cuda", generator=g)).bfloat16()
+    bias = (0.1 * torch.randn(2 * inter, device="cuda", generator=g)).bfloat16() if with_bias else None
+    dh = torch.randn(m, inter, device="cuda", generator=g).bfloat16()
+    y_ref = qlora.lora_gemm(x, w, False, xa, bblk, torch.empty(m, 2 * inter, device="cuda",
+                                                               dtype=torch.bfloat16), bias)
+    y2 = y_ref.view(-1, 256)
+    gv, uv = y2[:, :128], y2[:, 128:]
+    h_ref = swiglu_forward(gv, uv).view(m, inter)
+    dy_ref = torch.empty_like(y_ref)
+    d2 = dy_ref.view(-1, 256)
+    swiglu_backward(dh.view(-1, 128), gv, uv, dg=d2[:, :128], du=d2[:, 128:])
+    h = torch.empty(m, inter, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty_like(y_ref)
+    qlora.swiglu_gemm(x, w, xa, bblk, bias, 0, h, y)
+    h_only = torch.empty_like(h)
+    qlora.swiglu_gemm(x, w, xa, bblk, bias, 0, h_only)
+    dy = torch.empty_like(y_ref)
+    qlora.swiglu_gemm(x, w, xa, bblk, bias, 1, dh, dy)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
+    assert torch.equal(h, h_ref) and torch.equal(h_only, h_ref)
+    assert torch.equal(dy, dy_ref)
+    assert _lib.device_error(torch.device("cuda")) == 0

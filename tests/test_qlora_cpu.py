@@ -172,3 +172,22 @@ def test_projection_groups_share_buffers_and_trainer_views():
     _, b2 = gu.factors(torch.bfloat16)
     gu.As16 = gu_as
     assert torch.equal(g_b, b2)
+
+
+def test_interleaved_gate_up_members_keep_their_weights():
+    # gate/up rows are stored interleaved in blocks of 128 inside the group; each
+    # member still returns its own [out, in] base weight
+    cfg = qlora.qwen2_1p5b_config(num_layers=1, hidden_size=256, intermediate_size=384,
+                                  num_attention_heads=4, num_key_value_heads=2, vocab_size=512)
+    grouped = qlora.build_qwen2_qlora(cfg, device="cpu", quantize=False, seed=3)
+    plain = qlora.build_qwen2_qlora(cfg, device="cpu", quantize=False, seed=3, group=False)
+    g = grouped.model.layers[0].mlp.gate_proj.lora_group
+    assert g.interleaved and g.weight.shape == (768, 256)
+    for name in ("gate_proj", "up_proj"):
+        a = getattr(grouped.model.layers[0].mlp, name).base_weight(torch.float32)
+        b = getattr(plain.model.layers[0].mlp, name).base_weight(torch.float32)
+        assert torch.equal(a, b), name
+    # block c of the group's rows: gate rows [128c, 128c+128), then the same up rows
+    gw = plain.model.layers[0].mlp.gate_proj.weight
+    uw = plain.model.layers[0].mlp.up_proj.weight
+    assert torch.equal(g.weight[128:256], uw[:128]) and torch.equal(g.weight[256:384], gw[128:256])

@@ -46,12 +46,39 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// bf16 store of a whole staged 32 x 32 block with 16-byte stores: 4 lanes per
+// 64-byte row segment, 8 rows per instruction (lane l: row 8i + l/4, columns
+// 8 (l%4) .. +7, read as granules 2 (l%4) and 2 (l%4) + 1 of that row -- the
+// XOR layout keeps the 8 lanes of each 128-bit access phase on distinct banks).
+__device__ __forceinline__ void write_block_bf16_v16(const uint8_t* stage, int lane, bf16* C,
+                                                     int64_t ldc, int row0, int M, int col0) {
+  const int c8 = lane & 3;
+  const int rsub = lane >> 2;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + rsub;
+    const int grow = row0 + r;
+    if (grow >= M) continue;
+    const float4 a = *reinterpret_cast<const float4*>(stage + stage_off(r, 2 * c8));
+    const float4 b = *reinterpret_cast<const float4*>(stage + stage_off(r, 2 * c8 + 1));
+    *reinterpret_cast<uint4*>(C + (int64_t)grow * ldc + col0 + c8 * 8) =
+        make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                   pack_bf16x2(b.z, b.w));
+  }
+}
+
 // Write the staged block to C rows [row0, row0+32) x cols [col0, col0+32),
 // clipped to M x N. `vec`: rows are 16-byte aligned (vector stores allowed).
 template <bool BF16>
 __device__ __forceinline__ void write_block(const uint8_t* stage, int lane, void* C, int64_t ldc,
                                             int row0, int M, int col0, int N, bool vec,
                                             bool accumulate) {
+  if constexpr (BF16) {
+    if (vec && !accumulate && col0 + 32 <= N) {
+      write_block_bf16_v16(stage, lane, reinterpret_cast<bf16*>(C), ldc, row0, M, col0);
+      return;
+    }
+  }
   const int cv = lane & 7;
   const int rsub = lane >> 3;
   const int gcol = col0 + cv * 4;
@@ -105,6 +132,39 @@ __device__ __forceinline__ void write_block(const uint8_t* stage, int lane, void
   }
 }
 
+// A warp's 32 x 32 bf16 output block (thread t: row row0 + t, values a * v)
+// stored by TMA: written into half (nstore & 1) of the warp's staging block in
+// the store map's 64-byte swizzle (16-byte chunk q of row r at chunk
+// q ^ ((r >> 1) & 3): the 8 lanes of every 128-bit access phase hit distinct
+// banks), fenced for the async proxy, then one lane issues the store. Before a
+// half is rewritten its store from two blocks earlier must have finished
+// reading it (at most one bulk group still reading). Rows / columns outside
+// the map are not written.
+__device__ __forceinline__ void tma_store_block_bf16(const CUtensorMap* map, uint8_t* stage, int lane,
+                                                     int& nstore, const float (&v)[32], float a,
+                                                     int col0, int row0, int M) {
+  if (row0 >= M) return;  // all 32 rows outside the output (warp-uniform)
+  uint8_t* buf = stage + (nstore & 1) * 2048;
+  if (lane == 0) bulk_wait_read1();
+  __syncwarp();
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 w = make_uint4(pack_bf16x2(a * v[8 * q], a * v[8 * q + 1]),
+                               pack_bf16x2(a * v[8 * q + 2], a * v[8 * q + 3]),
+                               pack_bf16x2(a * v[8 * q + 4], a * v[8 * q + 5]),
+                               pack_bf16x2(a * v[8 * q + 6], a * v[8 * q + 7]));
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((q ^ sw) << 4)) = w;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, smem_u32(buf), col0, row0);
+    bulk_commit();
+  }
+  ++nstore;
+}
+
 // Plain store: C = alpha * scale * acc (+ C). `scale` is an optional device
 // scalar (e.g. the upstream gradient of the loss). `split_stride` > 0 writes
 // k-split partial slices (fp32) at C + ks * split_stride.
@@ -121,8 +181,9 @@ struct EpiStore {
     int vec_ok;  // 16-byte aligned rows
     int M, N;
     const bf16* bias;  // optional [N] added to every row after scaling
+    int tma;           // bf16, no accumulate, no k split: store through tma_c
   };
-  static __device__ __forceinline__ void tile(const Params& p, int row_base, int nt, int ks,
+  static __device__ __forceinline__ void tile(const Params& p, const CUtensorMap* tmc, int row_base, int nt, int ks,
                                               int quarter, int lane, uint32_t taddr, uint8_t* stage,
                                               int group, int ngroups) {
     const int row0 = row_base + quarter * 32;
@@ -130,20 +191,25 @@ struct EpiStore {
     const size_t es = p.c_bf16 ? 2 : 4;
     void* C = static_cast<uint8_t*>(p.c) + (size_t)ks * p.split_stride * es;
     const int nch = BN / 32 / ngroups;
+    int nstore = 0;
 #pragma unroll 1
     for (int c = group * nch; c < (group + 1) * nch; ++c) {
       float v[32];
       tmem_ld32(taddr + c * 32, v);
       const int col0 = nt * BN + c * 32;
       if (col0 >= p.N) continue;
+      float sa = a;
       if (p.bias) {  // every lane reads the same 32 values (broadcast)
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           v[j] = fmaf(a, v[j], col0 + j < p.N ? __bfloat162float(p.bias[col0 + j]) : 0.f);
-        stage_row(stage, lane, v, 1.f);
-      } else {
-        stage_row(stage, lane, v, a);
+        sa = 1.f;
       }
+      if (p.tma) {
+        tma_store_block_bf16(tmc, stage, lane, nstore, v, sa, col0, row0, p.M);
+        continue;
+      }
+      stage_row(stage, lane, v, sa);
       __syncwarp();
       if (p.c_bf16)
         write_block<true>(stage, lane, C, p.ldc, row0, p.M, col0, p.N, p.vec_ok, p.accumulate);
@@ -213,7 +279,7 @@ struct EpiSwiGLU {
       load_block_bf16(c.d, lane, p.h, p.ldh, row_base + quarter * 32, p.M,
                       nt * kHalf + group * (kHalf / 32 / ngroups) * 32);
   }
-  static __device__ __forceinline__ void tile(const Params& p, int row_base, int nt, int ks,
+  static __device__ __forceinline__ void tile(const Params& p, const CUtensorMap* tmc, int row_base, int nt, int ks,
                                               int quarter, int lane, uint32_t taddr, uint8_t* stage,
                                               int group, int ngroups, Carry& carry) {
     constexpr int kHalf = BN / 2;
@@ -300,8 +366,9 @@ struct EpiCE {
     int64_t ld_logits;
     int64_t vocab_offset;  // first vocabulary row of this weight shard (0 unsharded)
     int M, N;
+    int tma;  // logits stored through tma_c
   };
-  static __device__ __forceinline__ void tile(const Params& p, int row_base, int nt, int ks,
+  static __device__ __forceinline__ void tile(const Params& p, const CUtensorMap* tmc, int row_base, int nt, int ks,
                                               int quarter, int lane, uint32_t taddr, uint8_t* stage,
                                               int group, int ngroups) {
     const int row0 = row_base + quarter * 32;
@@ -313,6 +380,7 @@ struct EpiCE {
     int bidx = 0x7fffffff;
     float ztv = 0.f;
     bool found = false;
+    int nstore = 0;
 #pragma unroll 1
     for (int c = group * nch; c < (group + 1) * nch; ++c) {
       float v[32];
@@ -326,10 +394,14 @@ struct EpiCE {
           if (j >= nvalid) v[j] = -INFINITY;
       }
       if (p.logits) {
-        stage_row(stage, lane, v, 1.f);
-        __syncwarp();
-        write_block<true>(stage, lane, p.logits, p.ld_logits, row0, p.M, col0, p.N, true, false);
-        __syncwarp();
+        if (p.tma) {
+          tma_store_block_bf16(tmc, stage, lane, nstore, v, 1.f, col0, row0, p.M);
+        } else {
+          stage_row(stage, lane, v, 1.f);
+          __syncwarp();
+          write_block<true>(stage, lane, p.logits, p.ld_logits, row0, p.M, col0, p.N, true, false);
+          __syncwarp();
+        }
       }
       // chunk maximum with its first index
       float cm = v[0];
@@ -421,6 +493,30 @@ static int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t 
   return SOUP_OK;
 }
 
+// Output map for the epilogues' TMA stores: bf16 [outer, inner] with row
+// stride ld (elements), box {32, 32}, 64-byte swizzle (the staging layout of
+// tma_store_block_bf16).
+static int make_store_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer,
+                          uint64_t ld) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_last_error("cuTensorMapEncodeTiled is not available from the driver");
+    return SOUP_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled failed for an output map");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  return SOUP_OK;
+}
+
 // Operand map: K-major operand stored [rows, K]: box {64 (K), rows_box};
 // MN-major operand stored [K, rows]: box {64 (MN), 64 (K)}.
 static int make_operand_map(CUtensorMap* map, const void* ptr, bool mn_major, int64_t rows, int64_t k,
@@ -458,7 +554,7 @@ constexpr int kPairStages = 6;
 
 template <bool A_MN, bool B_MN, class Epi>
 static int launch_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma2,
-                              const CUtensorMap& mb2, Sched sched,
+                              const CUtensorMap& mb2, const CUtensorMap& mc, Sched sched,
                               const typename Epi::Params& ep, cudaStream_t stream, int* err) {
   using L = SmemLayout<kBN, kStages, kEpiWarps>;
   auto kern = gemm_kernel<kBN, kStages, A_MN, B_MN, Epi, kEpiWarps>;
@@ -473,13 +569,13 @@ static int launch_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb, cons
   }
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
   const int grid = units < num_sms() ? units : num_sms();
-  kern<<<grid, gemm_threads(kEpiWarps), L::kBytes, stream>>>(ma, mb, ma2, mb2, sched, ep, err);
+  kern<<<grid, gemm_threads(kEpiWarps), L::kBytes, stream>>>(ma, mb, ma2, mb2, mc, sched, ep, err);
   return launch_status();
 }
 
 template <bool A_MN, bool B_MN, class Epi>
 static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma2,
-                            const CUtensorMap& mb2, Sched sched,
+                            const CUtensorMap& mb2, const CUtensorMap& mc, Sched sched,
                             const typename Epi::Params& ep, cudaStream_t stream, int* err) {
   using L = SmemLayout<kBN / 2, kPairStages, kEpiWarps>;
   static_assert(L::kBytes <= 232448, "pair GEMM shared memory exceeds 227 KB");
@@ -516,15 +612,16 @@ static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const 
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
   const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
   cfg.gridDim = dim3(2 * clusters);
-  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mb, ma2, mb2, sched, ep, err));
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mb, ma2, mb2, mc, sched, ep, err));
 }
 
 // sched.m_tiles counts tile_m() rows. ma2 / mb2 are read for the last
-// sched.kb2 k-blocks (the second K segment).
+// sched.kb2 k-blocks (the second K segment); mc is the output map of an
+// epilogue that stores through TMA (any valid map otherwise).
 template <bool A_MN, bool B_MN, class Epi>
 static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma2,
-                       const CUtensorMap& mb2, Sched sched, const typename Epi::Params& ep,
-                       cudaStream_t stream) {
+                       const CUtensorMap& mb2, const CUtensorMap& mc, Sched sched,
+                       const typename Epi::Params& ep, cudaStream_t stream) {
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
   if (units <= 0) return SOUP_OK;
   int* err = device_err_ptr();
@@ -533,16 +630,16 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
     return SOUP_ERR_CUDA;
   }
   if (use_pairs())
-    return launch_gemm_pair<A_MN, B_MN, Epi>(ma, mb, ma2, mb2, sched, ep, stream, err);
-  return launch_gemm_single<A_MN, B_MN, Epi>(ma, mb, ma2, mb2, sched, ep, stream, err);
+    return launch_gemm_pair<A_MN, B_MN, Epi>(ma, mb, ma2, mb2, mc, sched, ep, stream, err);
+  return launch_gemm_single<A_MN, B_MN, Epi>(ma, mb, ma2, mb2, mc, sched, ep, stream, err);
 }
 
 // One K segment (sched.kb2 must be 0).
 template <bool A_MN, bool B_MN, class Epi>
-static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, Sched sched,
-                       const typename Epi::Params& ep, cudaStream_t stream) {
+static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                       Sched sched, const typename Epi::Params& ep, cudaStream_t stream) {
   sched.kb2 = 0;
-  return launch_gemm<A_MN, B_MN, Epi>(ma, mb, ma, mb, sched, ep, stream);
+  return launch_gemm<A_MN, B_MN, Epi>(ma, mb, ma, mb, mc, sched, ep, stream);
 }
 
 // ------------------------------------------------------ CE row kernels -----
@@ -859,14 +956,16 @@ static int dx_gemm(const bf16* L, int64_t ld_logits, const void* weight, int64_t
   Sched sc{m_tiles(M), (D + kBN - 1) / kBN, splits, (V + BK - 1) / BK, 1};
   const bool bf = dh_dtype == SOUP_BF16;
   if (splits == 1) {
-    EpiStore<kBN>::Params ep{dh, D, 0, nullptr, 1.f, bf ? 1 : 0, 0,
-                             (aligned16(dh) && (D * (bf ? 2 : 4)) % 16 == 0) ? 1 : 0, M, D};
-    rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, sc, ep, stream);
+    const int vec = (aligned16(dh) && (D * (bf ? 2 : 4)) % 16 == 0) ? 1 : 0;
+    CUtensorMap mc = ma;
+    const int tma = (bf && vec && make_store_map(&mc, dh, D, M, D) == SOUP_OK) ? 1 : 0;
+    EpiStore<kBN>::Params ep{dh, D, 0, nullptr, 1.f, bf ? 1 : 0, 0, vec, M, D, nullptr, tma};
+    rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, mc, sc, ep, stream);
     if (!rc && gemm_stage >= 0) mark_stage(gemm_stage, stream);
     return rc;
   }
   EpiStore<kBN>::Params ep{splitk, D, (int64_t)M * D, nullptr, 1.f, 0, 0, 1, M, D};
-  if ((rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, sc, ep, stream))) return rc;
+  if ((rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, ma, sc, ep, stream))) return rc;
   if (gemm_stage >= 0) mark_stage(gemm_stage, stream);
   const int64_t n4 = (int64_t)M * D / 4;
   int blocks = static_cast<int>((n4 + 255) / 256);
@@ -890,10 +989,13 @@ static int dweight_gemm(const bf16* L, int64_t ld_logits, const void* hidden, in
   if ((rc = make_operand_map(&mb, hidden, true, D, M, h_ld, 64))) return rc;
   Sched sc{m_tiles(V), (D + kBN - 1) / kBN, 1, (M + BK - 1) / BK, 1};
   const int es = dw_dtype == SOUP_BF16 ? 2 : 4;
+  const int vec = (aligned16(dweight) && (D * es) % 16 == 0) ? 1 : 0;
+  CUtensorMap mc = ma;
+  const int tma = (dw_dtype == SOUP_BF16 && !accumulate && vec &&
+                   make_store_map(&mc, dweight, D, V, D) == SOUP_OK) ? 1 : 0;
   EpiStore<kBN>::Params ep{dweight, D, 0, scale, 1.f, dw_dtype == SOUP_BF16 ? 1 : 0,
-                           accumulate ? 1 : 0,
-                           (aligned16(dweight) && (D * es) % 16 == 0) ? 1 : 0, V, D};
-  return launch_gemm<true, true, EpiStore<kBN>>(ma, mb, sc, ep, stream);
+                           accumulate ? 1 : 0, vec, V, D, nullptr, tma};
+  return launch_gemm<true, true, EpiStore<kBN>>(ma, mb, mc, sc, ep, stream);
 }
 
 }  // namespace tc
@@ -952,8 +1054,10 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
     if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
     if ((rc = make_operand_map(&mb, weight, false, vocab, dim, w_ld, b_box_rows()))) return rc;
     Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
-    EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, 0, M, V};
-    if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, sc, ep, stream))) return rc;
+    CUtensorMap mc = ma;
+    const int tma = (need_grad && make_store_map(&mc, L, V, M, w.ld_logits) == SOUP_OK) ? 1 : 0;
+    EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, 0, M, V, tma};
+    if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, mc, sc, ep, stream))) return rc;
     mark_stage(0, stream);
   }
   const float inv_den = 1.f / (denominator > 0.f ? denominator : 1.f);
@@ -1052,8 +1156,10 @@ int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shar
   if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, b_box_rows())))
     return rc;
   Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
-  EpiCE<kBN>::Params ep{targets, partials, zt, L, w.ld_logits, vocab_offset, M, V};
-  if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, sc, ep, stream))) return rc;
+  CUtensorMap mc = ma;
+  const int tma = make_store_map(&mc, L, V, M, w.ld_logits) == SOUP_OK ? 1 : 0;
+  EpiCE<kBN>::Params ep{targets, partials, zt, L, w.ld_logits, vocab_offset, M, V, tma};
+  if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, mc, sc, ep, stream))) return rc;
   ce_shard_state_kernel<<<(M + 7) / 8, 256, 0, stream>>>(partials, w.n_parts, zt, targets, M, V,
                                                          vocab_offset, states);
   return launch_status();
@@ -1177,18 +1283,21 @@ int soup_gemm_bf16_lora(const void* a, int64_t lda, int a_mn_major, const void* 
     mb2 = mb;
   }
   const int es = c_dtype == SOUP_BF16 ? 2 : 4;
+  const int vec = (aligned16(c) && (ldc * es) % 16 == 0) ? 1 : 0;
+  CUtensorMap mc = ma;
+  const int tma = (c_dtype == SOUP_BF16 && !accumulate && vec &&
+                   make_store_map(&mc, c, n, m, ldc) == SOUP_OK) ? 1 : 0;
   EpiStore<kBN>::Params ep{c, ldc, 0, nullptr, alpha, c_dtype == SOUP_BF16 ? 1 : 0, accumulate ? 1 : 0,
-                           (aligned16(c) && (ldc * es) % 16 == 0) ? 1 : 0, (int)m, (int)n,
-                           static_cast<const bf16*>(bias)};
+                           vec, (int)m, (int)n, static_cast<const bf16*>(bias), tma};
   const int mt = m_tiles(m), nt = (int)((n + kBN - 1) / kBN);
   const int kb1 = (int)((k + BK - 1) / BK), kb2 = (int)((r + BK - 1) / BK);
   Sched sc{mt, nt, 1, kb1 + kb2, nt > mt ? 0 : 1, kb2};
   cudaStream_t stream = as_stream(stream_);
   using E = EpiStore<kBN>;
-  if (!a_mn_major && !b_mn_major) return launch_gemm<false, false, E>(ma, mb, ma2, mb2, sc, ep, stream);
-  if (!a_mn_major && b_mn_major) return launch_gemm<false, true, E>(ma, mb, ma2, mb2, sc, ep, stream);
-  if (a_mn_major && !b_mn_major) return launch_gemm<true, false, E>(ma, mb, ma2, mb2, sc, ep, stream);
-  return launch_gemm<true, true, E>(ma, mb, ma2, mb2, sc, ep, stream);
+  if (!a_mn_major && !b_mn_major) return launch_gemm<false, false, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
+  if (!a_mn_major && b_mn_major) return launch_gemm<false, true, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
+  if (a_mn_major && !b_mn_major) return launch_gemm<true, false, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
+  return launch_gemm<true, true, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
 }
 
 int soup_gemm_bf16_lora_swiglu(const void* a, int64_t lda, const void* b, int64_t ldb,
@@ -1231,7 +1340,7 @@ int soup_gemm_bf16_lora_swiglu(const void* a, int64_t lda, const void* b, int64_
   const int mt = m_tiles(m), nt = (int)(n / kBN);
   const int kb1 = (int)((k + BK - 1) / BK), kb2 = (int)((r + BK - 1) / BK);
   Sched sc{mt, nt, 1, kb1 + kb2, nt > mt ? 0 : 1, kb2};
-  return launch_gemm<false, false, EpiSwiGLU<kBN>>(ma, mb, ma2, mb2, sc, ep, as_stream(stream_));
+  return launch_gemm<false, false, EpiSwiGLU<kBN>>(ma, mb, ma2, mb2, ma, sc, ep, as_stream(stream_));
 }
 
 }  // extern "C"

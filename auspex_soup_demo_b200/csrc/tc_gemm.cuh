@@ -121,6 +121,25 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
+// 2-D TMA store of a tile from this CTA's shared memory (bulk async-group of
+// the issuing thread; out-of-bounds parts of the box are not written).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x,
+                                             int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// at most one of this thread's bulk groups still reading shared memory
+__device__ __forceinline__ void bulk_wait_read1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// generic-proxy shared-memory writes -> visible to the async proxy (TMA)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -268,7 +287,9 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity,
 
 // Epi must provide:
 //   struct Params;
-//   static __device__ void tile(const Params&, int row_base /* first row of the CTA's
+//   static __device__ void tile(const Params&, const CUtensorMap* tma_c /* the kernel's
+//                               output map (valid when the launcher encoded one) */,
+//                               int row_base /* first row of the CTA's
 //                               128-row block */, int nt, int ks, int quarter,
 //                               int lane, uint32_t tmem_acc /* lane base applied */,
 //                               uint8_t* stage /* this warp's kEpiWarpBytes of smem */,
@@ -277,7 +298,8 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS>
 __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                 const __grid_constant__ CUtensorMap tma_a2,
-                const __grid_constant__ CUtensorMap tma_b2, Sched sched,
+                const __grid_constant__ CUtensorMap tma_b2,
+                const __grid_constant__ CUtensorMap tma_c, Sched sched,
                 typename Epi::Params ep, int* err) {
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
   using L = SmemLayout<BN, STAGES, EPI_WARPS>;
@@ -458,13 +480,14 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
       if constexpr (EpiCarry<Epi>::kHas)
-        Epi::tile(ep, mt * BM, nt, ks, quarter, lane, taddr, stage, group, kGroups, carry);
+        Epi::tile(ep, &tma_c, mt * BM, nt, ks, quarter, lane, taddr, stage, group, kGroups, carry);
       else
-        Epi::tile(ep, mt * BM, nt, ks, quarter, lane, taddr, stage, group, kGroups);
+        Epi::tile(ep, &tma_c, mt * BM, nt, ks, quarter, lane, taddr, stage, group, kGroups);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
     }
+    if (lane == 0) bulk_wait_all();  // this warp's TMA stores, if any, are complete
   }
 
   tc_fence_before();
@@ -556,7 +579,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_a2,
-                     const __grid_constant__ CUtensorMap tma_b2, Sched sched,
+                     const __grid_constant__ CUtensorMap tma_b2,
+                     const __grid_constant__ CUtensorMap tma_c, Sched sched,
                      typename Epi::Params ep, int* err) {
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
   static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
@@ -749,13 +773,14 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
       if constexpr (EpiCarry<Epi>::kHas)
-        Epi::tile(ep, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups, carry);
+        Epi::tile(ep, &tma_c, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups, carry);
       else
-        Epi::tile(ep, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups);
+        Epi::tile(ep, &tma_c, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(tempty_bar(acc), 0));
     }
+    if (lane == 0) bulk_wait_all();  // this warp's TMA stores, if any, are complete
   }
 
   tc_fence_before();

@@ -357,9 +357,12 @@ def run_memory_op(args):
     Inputs rotate over enough buffer sets to exceed twice the L2 (126 MB);
     `graph_steps` steps are captured once in a CUDA graph and replayed, so
     host launch overhead stays out of the device time. Algorithmic bytes:
-    rmsnorm 5*N*D*4 (x, y; dy, x, dx) fp32 [2048, 1536]; swiglu 8*N*I*2
-    (g, u, out; dy, g, u, dg, du) bf16 [2048, 8960]; rope 2 passes x (read +
-    write of Q and K + cos/sin reads) bf16 Q [4,12,512,128], K [4,2,512,128].
+    rmsnorm 5*N*D*4 (x, y; dy, x, dx) fp32 [N, 1536]; swiglu 8*N*I*2
+    (g, u, out; dy, g, u, dg, du) bf16 [N, 8960]; rope 2 passes x (read +
+    write of Q and K + cos/sin reads) bf16 Q [B,12,S,128], K [B,2,S,128].
+    B = --batch, S = --seq, N = B*S; the defaults (4 x 512) are the benchmark
+    shapes, larger batches show the same kernels with the per-launch fixed cost
+    amortised.
     """
     from auspex_soup_demo_b200.kernels.rmsnorm import rmsnorm_backward, rmsnorm_forward
     from auspex_soup_demo_b200.kernels.rope import rope_apply
@@ -373,7 +376,7 @@ def run_memory_op(args):
     wl = args.workload
     l2 = 126 * 2 ** 20
     if wl == "rmsnorm":
-        N, D = 2048, 1536
+        N, D = args.batch * args.seq, 1536
         per_set = 4 * N * D * 4
         nsets = max(2, -(-2 * l2 // per_set))
         w = (1 + 0.1 * torch.randn(D, device=dev, generator=g))
@@ -387,9 +390,9 @@ def run_memory_op(args):
         def one(s):
             rmsnorm_forward(s["x"], w, 1e-6, out=s["y"], rstd=s["rstd"])
             rmsnorm_backward(s["dy"], s["x"], w, s["rstd"], True, dx=s["dx"])
-        shape = "x [2048,1536] fp32, dw included"
+        shape = f"x [{N},1536] fp32, dw included"
     elif wl == "swiglu":
-        N, I = 2048, 8960
+        N, I = args.batch * args.seq, 8960
         per_set = 7 * N * I * 2
         nsets = max(2, -(-2 * l2 // per_set))
         sets = [dict(g=torch.randn(N, I, device=dev, generator=g).to(torch.bfloat16),
@@ -404,9 +407,9 @@ def run_memory_op(args):
         def one(s):
             swiglu_forward(s["g"], s["u"], out=s["o"])
             swiglu_backward(s["dy"], s["g"], s["u"], dg=s["dg"], du=s["du"])
-        shape = "gate/up [2048,8960] bf16"
+        shape = f"gate/up [{N},8960] bf16"
     elif wl == "rope":
-        B, S, Hq, Hk, D = 4, 512, 12, 2, 128
+        B, S, Hq, Hk, D = args.batch, args.seq, 12, 2, 128
         qk_bytes = (Hq + Hk) * B * S * D * 2
         per_set = 4 * qk_bytes
         nsets = max(2, -(-2 * l2 // per_set))
@@ -424,7 +427,7 @@ def run_memory_op(args):
         def one(s):
             rope_apply(s["q"], s["k"], cos, sin, False, q_out=s["qo"], k_out=s["ko"])
             rope_apply(s["qo"], s["ko"], cos, sin, True, q_out=s["q"], k_out=s["k"])
-        shape = "Q [4,12,512,128] + K [4,2,512,128] bf16, theta 1e6, fwd + inverse"
+        shape = f"Q [{B},12,{S},128] + K [{B},2,{S},128] bf16, theta 1e6, fwd + inverse"
     else:
         raise SystemExit(f"unknown workload {wl}")
 
@@ -687,8 +690,10 @@ def main():
                          "op's HBM GB/s; qlora: the Qwen2.5-1.5B QLoRA train step's tokens/s; "
                          "ce_vp: the vocab-parallel CE over all ranks")
     ap.add_argument("--tokens", type=int, default=65536, help="ce_vp: tokens per step")
-    ap.add_argument("--batch", type=int, default=4, help="qlora: sequences per GPU")
-    ap.add_argument("--seq", type=int, default=512, help="qlora: tokens per sequence")
+    ap.add_argument("--batch", type=int, default=4,
+                    help="qlora: sequences per GPU; rmsnorm/swiglu/rope: batch of the op's shape")
+    ap.add_argument("--seq", type=int, default=512,
+                    help="qlora: tokens per sequence; rmsnorm/swiglu/rope: sequence length of the op's shape")
     ap.add_argument("--layers", type=int, default=28, help="qlora: decoder layers")
     ap.add_argument("--no-graph", action="store_true", help="qlora: launch eagerly, no CUDA graph")
     ap.add_argument("--no-recompute", action="store_true",

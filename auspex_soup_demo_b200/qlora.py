@@ -295,6 +295,9 @@ class LoRAProjectionGroup:
     On B200 with Qwen2.5-1.5B shapes at 2048 tokens this replaces k_proj /
     v_proj GEMMs with N = 256 (8 of 74 CTA pairs busy) and the separate
     dequantisations, rank-16 GEMMs and autograd gradient sums of each member.
+
+    The members' buffers are views of the group's; build the model on the
+    device it will run on (moving it afterwards copies the views apart).
     """
 
     def __init__(self, members, kind: str):
@@ -934,8 +937,8 @@ class QLoRATrainer:
                     dst_all = buf[:, o0:o0 + n_j, c0:c0 + r_j]
                     src_shape = (n_j, r_j)
                 if all(offs[l] == offs[0] + l * stride for l in range(len(offs))):
-                    src = self.flat_param16.as_strided((L, *src_shape), (stride, *torch.empty(src_shape).stride()),
-                                                       offs[0])
+                    inner = tuple(int(np.prod(src_shape[d + 1:])) for d in range(len(src_shape)))
+                    src = self.flat_param16.as_strided((L, *src_shape), (stride, *inner), offs[0])
                     self._bblk_copies.append((dst_all, src))
                 else:
                     for l, off in enumerate(offs):

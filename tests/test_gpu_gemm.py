@@ -87,6 +87,21 @@ def test_gemm_pair_tile_edges(a_mn, b_mn, m, n, k):
     assert err < 1e-5, err
 
 
+@pytest.mark.parametrize("a_mn,b_mn", [(0, 0), (1, 1)])
+@pytest.mark.parametrize("m,n,k", [(64, 128, 64), (104, 136, 128), (136, 256, 64), (264, 392, 320)])
+def test_gemm_pair_tile_edges_bf16_tma_store(a_mn, b_mn, m, n, k):
+    # bf16 outputs leave through TMA stores clipped to the matrix: every element
+    # inside is written (C starts as NaN) and nothing outside the view is touched
+    a, b, ref = operands(m, n, k, a_mn, b_mn, seed=17)
+    pad = torch.full((m + 8, n + 16), 7.0, dtype=torch.bfloat16, device="cuda")
+    c = pad[:m, :n]
+    c.fill_(float("nan"))
+    run_gemm(a, a_mn, b, b_mn, m, n, k, c=c)
+    err = (c.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 8e-3, err
+    assert bool((pad[m:, :] == 7.0).all()) and bool((pad[:, n:] == 7.0).all())
+
+
 def test_gemm_many_tiles_mn_major():
     m, n, k = 3000, 2048, 448
     a, b, ref = operands(m, n, k, 1, 1, seed=13)
@@ -153,6 +168,17 @@ for (m, n, k, a_mn, b_mn) in [(200, 328, 192, 0, 0), (1000, 1536, 704, 0, 1), (3
     ref = A.float() @ B.float().t()
     err = (c - ref).abs().max().item() / ref.abs().max().item()
     assert err < 1e-5, (m, n, k, a_mn, b_mn, err)
+for (m, n, k) in [(200, 328, 192), (1000, 1536, 704)]:  # bf16 out: TMA-store epilogue
+    A = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+    B = torch.randn(n, k, device="cuda").to(torch.bfloat16)
+    c = torch.full((m, n), float("nan"), device="cuda", dtype=torch.bfloat16)
+    _lib.call("soup_gemm_bf16", A.device, A.data_ptr(), A.stride(0), 0, B.data_ptr(), B.stride(0), 0,
+              c.data_ptr(), c.stride(0), _lib.dtype_code(c.dtype), m, n, k, 1.0, 0, _lib.stream_of(c))
+    torch.cuda.synchronize()
+    assert _lib.device_error(A.device) == 0
+    ref = A.float() @ B.float().t()
+    err = (c.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < 8e-3, ("bf16", m, n, k, err)
 m, n, k, r = 1000, 1536, 704, 16
 A = torch.randn(m, k, device="cuda").to(torch.bfloat16)
 B = torch.randn(k, n, device="cuda").to(torch.bfloat16)

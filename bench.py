@@ -502,6 +502,31 @@ def run_memory_op(args):
     print(json.dumps(line), flush=True)
 
 
+def kernel_table(step, n_steps, top=40):
+    """Per-kernel device time of `n_steps` calls of `step` (CUPTI through
+    torch.profiler; kernels run back to back as in the timed region), printed to
+    stderr as: ms per step, share, launches per step, kernel name."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n_steps):
+            step()
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            agg[e.name][0] += 1
+            agg[e.name][1] += e.device_time_total
+    total = sum(v[1] for v in agg.values())
+    print(f"kernel time per step {total / n_steps / 1000:.3f} ms", file=sys.stderr)
+    for name, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:top]:
+        print(f"{t / n_steps / 1000:8.3f} ms {100 * t / total:5.1f}% {n // n_steps:5d}x  {name[:140]}",
+              file=sys.stderr)
+
+
 def run_qlora(args):
     """Qwen2.5-1.5B-architecture QLoRA train step: tokens/s (whole job).
 
@@ -590,6 +615,8 @@ def run_qlora(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t)
     assert _lib.device_error(dev) == 0
+    if args.profile and rank == 0:
+        kernel_table(one_step, 2)
     n_lora = sum(p.numel() for p in qlora.lora_parameters(model))
     line = {"metric": "QLoRA train tokens/s", "value": round(tok_s, 1), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -728,6 +755,9 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="qlora: launch eagerly, no CUDA graph")
     ap.add_argument("--no-recompute", action="store_true",
                     help="qlora: keep MLP activations instead of recomputing gate/up in backward")
+    ap.add_argument("--profile", action="store_true",
+                    help="qlora: after the timed region, print a per-kernel device-time table of "
+                         "two steps (torch.profiler, CUDA activity) to stderr")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -264,3 +264,45 @@ def test_vocab_parallel_ce_emulated_ranks(world):
 def test_fused_ce_ragged_rows_over_several_pair_tiles():
     # 700 rows: two full 256-row pair tiles and a ragged third
     _check_fused(700, 8192, 256, seed=8)
+
+
+def test_fused_ce_benchmark_configuration_against_torch_fp32():
+    # the benchmark's exact workload (2048 tokens, V 151936, D 1536, its seeded inputs)
+    # against plain PyTorch fp32 on the GPU: logits, log-softmax, dlogits, dH and dW
+    import bench
+
+    dev = torch.device("cuda")
+    hidden_cpu, labels_cpu, weight = bench.make_inputs(0, dev)
+    hidden, labels = hidden_cpu.to(dev), labels_cpu.to(dev)
+    den = float((labels_cpu != -100).sum())
+    losses, ents, hits, sums, dh, dw = fused_linear_cross_entropy(
+        hidden, weight, labels, den, -100, True, compute_dw=True, dw_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert _lib.device_error(dev) == 0
+    h32, w32 = hidden.float(), weight.float()
+    logits = h32 @ w32.t()
+    logp = torch.log_softmax(logits, dim=-1)
+    valid = labels != -100
+    t = labels.clamp_min(0)
+    loss_ref = torch.where(valid, -logp.gather(1, t[:, None])[:, 0], torch.zeros_like(logp[:, 0]))
+    ent_ref = -(logp.exp() * logp).sum(-1)
+    top2 = logits.topk(2, dim=-1)
+    hit_ref = valid & (top2.indices[:, 0] == labels)
+    dl = logp.exp()
+    dl[valid.nonzero()[:, 0], t[valid]] -= 1.0
+    dl[~valid] = 0.0
+    dl /= den
+    dh_ref = dl @ w32
+    dw_ref = dl.t() @ h32
+    del logits, logp, dl
+    torch.testing.assert_close(losses, loss_ref, rtol=1e-4, atol=1e-4)
+    assert abs(float(sums[0]) - float(loss_ref.sum())) <= 1e-4 * abs(float(loss_ref.sum()))
+    torch.testing.assert_close(ents, ent_ref, rtol=2e-3, atol=2e-3)
+    diff = (hits.bool() != hit_ref).nonzero().flatten()
+    if diff.numel():  # only provable near-ties of the fp32 logits may differ
+        gap = (top2.values[diff, 0] - top2.values[diff, 1]).abs()
+        assert bool((gap < 1e-4 * top2.values[diff, 0].abs().clamp_min(1)).all()), (diff, gap)
+    assert diff.numel() <= 2
+    assert int(sums[1]) == int(hits.sum())
+    assert cosine(dh, dh_ref) >= 0.9999
+    assert cosine(dw, dw_ref) >= 0.9999

@@ -1,17 +1,23 @@
 // Fused lm_head cross-entropy on tcgen05, and the plain GEMM entry point.
 //
 // One soup_ce_linear call over `rows` tokens runs:
+//   0. ce_shift (gradient only): per row a shift c = the target logit
+//      (one dot product) + a margin; +inf for ignored rows;
 //   1. logits GEMM  L = H W^T  (M=rows, N=vocab, K=dim; A, B K-major) whose
 //      epilogue, per row and 256-column vocab tile, keeps the online-softmax
 //      state (max, sum exp, sum z*exp, first argmax), captures the target
-//      logit, and stores the logits as bf16 into the workspace;
-//   2. ce_finalize: per row, merges the tile states (ties keep the smaller
-//      index), writes loss / entropy / hit, and rewrites the row's logits in
-//      place as dlogits = (softmax - onehot) / denominator (0 for ignored rows);
+//      logit, and stores E = exp(z - c) as bf16 into the workspace;
+//   2. ce_stats: per row, merges the tile states (ties keep the smaller
+//      index), writes loss / entropy / hit, the row factor
+//      s = exp(c - lse) / denominator and E[t] = (p_t - 1) exp(lse - c), so
+//      that s * E is the row of dlogits = (softmax - onehot) / denominator
+//      (s = 0 for ignored rows); a gated second logits GEMM with c = lse
+//      runs only if a row maximum came out far above its shift;
 //   3. ce_sums: fixed-order sums of the per-row losses and hits;
-//   4. dX GEMM  dH = dL W  (A = dL K-major, B = W MN-major), split along the
-//      vocab into fp32 partials, then a fixed-order reduce to bf16;
-//   5. dW GEMM  dW = dL^T H  (A = dL MN-major, B = H MN-major).
+//   4. dX GEMM  dH = diag(s) E W  (A = E K-major, B = W MN-major), split along
+//      the vocab into fp32 partials, then a fixed-order reduce that applies s;
+//   5. dW GEMM  dW = E^T diag(s) H  (A = E MN-major, B = s * H MN-major).
+// No pass rewrites the [rows, vocab] buffer between the GEMMs.
 // This follows the semantics of chunk_cross_entropy_triton and its kernel in
 // the reference (solution/kernels/chunked_ce.py:32-128, 183-264).
 #include <cuda.h>
@@ -182,12 +188,14 @@ struct EpiStore {
     int M, N;
     const bf16* bias;  // optional [N] added to every row after scaling
     int tma;           // bf16, no accumulate, no k split: store through tma_c
+    const float* row_scale;  // optional [M]: row m scaled by row_scale[m]
   };
   static __device__ __forceinline__ void tile(const Params& p, const CUtensorMap* tmc, int row_base, int nt, int ks,
                                               int quarter, int lane, uint32_t taddr, uint8_t* stage,
                                               int group, int ngroups) {
     const int row0 = row_base + quarter * 32;
-    const float a = p.alpha * (p.scale ? *p.scale : 1.f);
+    float a = p.alpha * (p.scale ? *p.scale : 1.f);
+    if (p.row_scale && row0 + lane < p.M) a *= p.row_scale[row0 + lane];  // lane = row
     const size_t es = p.c_bf16 ? 2 : 4;
     void* C = static_cast<uint8_t*>(p.c) + (size_t)ks * p.split_stride * es;
     const int nch = BN / 32 / ngroups;
@@ -356,6 +364,16 @@ struct EpiSwiGLU {
 
 // Logits epilogue of the CE forward: online-softmax state per (row, tile),
 // target logit capture, bf16 logits store.
+// Shifted exponentials. With `shift` set, the tile stores E = exp(z - c_row)
+// in bf16 instead of the logit z (c = +inf stores 0: ignored rows). The
+// gradient of the row is then dL = s_row * E with one entry corrected for the
+// target, s_row = exp(c_row - lse_row) / denominator, so the dX and dW GEMMs
+// read E directly and no pass rewrites the logits buffer. bf16 has the fp32
+// exponent range: with c within a few tens of the row maximum, E neither
+// overflows nor loses any entry of relative size above e^-50.
+constexpr float kShiftMargin = 32.f;  // c = (target or column-0 logit) + margin
+constexpr float kShiftGap = 40.f;     // a tile maximum above c + gap raises the flag
+
 template <int BN>
 struct EpiCE {
   struct Params {
@@ -367,7 +385,22 @@ struct EpiCE {
     int64_t vocab_offset;  // first vocabulary row of this weight shard (0 unsharded)
     int M, N;
     int tma;  // logits stored through tma_c
+    const float* shift;  // [M] or nullptr (store the logits themselves)
+    int* flag;           // set to 1 when a row's maximum exceeds shift + kShiftGap
+    int onehot;          // shift = lse: store E - 1 at the target column (= p - 1)
   };
+  static __device__ __forceinline__ void store(const Params& p, const CUtensorMap* tmc,
+                                               uint8_t* stage, int lane, int& nstore,
+                                               const float (&v)[32], int col0, int row0) {
+    if (p.tma) {
+      tma_store_block_bf16(tmc, stage, lane, nstore, v, 1.f, col0, row0, p.M);
+    } else {
+      stage_row(stage, lane, v, 1.f);
+      __syncwarp();
+      write_block<true>(stage, lane, p.logits, p.ld_logits, row0, p.M, col0, p.N, true, false);
+      __syncwarp();
+    }
+  }
   static __device__ __forceinline__ void tile(const Params& p, const CUtensorMap* tmc, int row_base, int nt, int ks,
                                               int quarter, int lane, uint32_t taddr, uint8_t* stage,
                                               int group, int ngroups) {
@@ -376,33 +409,27 @@ struct EpiCE {
     const int nch = BN / 32 / ngroups;
     const bool row_ok = row < p.M;
     const int64_t t = row_ok ? p.targets[row] - p.vocab_offset : -1;
+    const bool shifted = p.logits && p.shift;
+    const float c = (shifted && row_ok) ? p.shift[row] : INFINITY;
+    const float cb = c * kLog2e;
     float m = -INFINITY, s = 0.f, w = 0.f;
     int bidx = 0x7fffffff;
     float ztv = 0.f;
-    bool found = false;
+    bool found = false, over = false;
     int nstore = 0;
 #pragma unroll 1
-    for (int c = group * nch; c < (group + 1) * nch; ++c) {
+    for (int cc = group * nch; cc < (group + 1) * nch; ++cc) {
       float v[32];
-      tmem_ld32(taddr + c * 32, v);
-      const int col0 = nt * BN + c * 32;
+      tmem_ld32(taddr + cc * 32, v);
+      const int col0 = nt * BN + cc * 32;
       const int nvalid = p.N - col0;
       if (nvalid <= 0) continue;
-      if (nvalid < 32) {
+      if (nvalid < 32) {  // finite fill: exp gives 0 and 0 * fill stays 0
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (j >= nvalid) v[j] = -INFINITY;
+          if (j >= nvalid) v[j] = -1e30f;
       }
-      if (p.logits) {
-        if (p.tma) {
-          tma_store_block_bf16(tmc, stage, lane, nstore, v, 1.f, col0, row0, p.M);
-        } else {
-          stage_row(stage, lane, v, 1.f);
-          __syncwarp();
-          write_block<true>(stage, lane, p.logits, p.ld_logits, row0, p.M, col0, p.N, true, false);
-          __syncwarp();
-        }
-      }
+      if (p.logits && !shifted) store(p, tmc, stage, lane, nstore, v, col0, row0);
       // chunk maximum with its first index
       float cm = v[0];
       int ci = 0;
@@ -419,8 +446,33 @@ struct EpiCE {
         m = cm;
         bidx = col0 + ci;
       }
+      const bool has_t = t >= col0 && t < col0 + 32 && t < p.N;
+      const int tj = static_cast<int>(t - col0);
+      if (has_t) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j == tj) ztv = v[j];
+        found = true;
+      }
       const float mb = m * kLog2e;
-      if (nvalid >= 32) {
+      if (shifted) {
+        // E_j = exp(z_j - m) * exp(m - c): one extra multiply per element
+        const float f = fast_exp2(mb - cb);
+        over |= cm - c > kShiftGap;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float e = fast_exp2(fmaf(v[j], kLog2e, -mb));  // 0 for padded columns
+          s += e;
+          w = fmaf(v[j], e, w);
+          v[j] = e * f;
+        }
+        if (p.onehot && has_t) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j == tj) v[j] -= 1.f;
+        }
+        store(p, tmc, stage, lane, nstore, v, col0, row0);
+      } else if (nvalid >= 32) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float e = fast_exp2(fmaf(v[j], kLog2e, -mb));
@@ -437,17 +489,11 @@ struct EpiCE {
           }
         }
       }
-      if (t >= col0 && t < col0 + 32 && t < p.N) {
-        const int tj = static_cast<int>(t - col0);
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (j == tj) ztv = v[j];
-        found = true;
-      }
     }
     if (row_ok) {
       p.partials[(int64_t)(nt * ngroups + group) * p.M + row] = make_float4(m, s, w, __int_as_float(bidx));
       if (found) p.zt[row] = ztv;
+      if (over) *p.flag = 1;
     }
   }
 };
@@ -643,34 +689,136 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
 }
 
 // ------------------------------------------------------ CE row kernels -----
-// One row: merge the tile states, metrics, then dlogits in place. Every
-// thread of the block takes part (block-uniform control flow).
-__device__ __forceinline__ void ce_finalize_row(
-    int row, const float4* __restrict__ partials, int n_tiles, const float* __restrict__ zt,
-    const int64_t* __restrict__ targets, bf16* __restrict__ logits, int64_t ld_logits, int rows,
-    int vocab, float inv_den, int64_t ignore_index, float* __restrict__ losses,
-    float* __restrict__ entropies, int32_t* __restrict__ correct, int write_grad,
-    SoftmaxState* red, float* s_lse) {
-  SoftmaxState st = sm_init();
-  for (int j = threadIdx.x; j < n_tiles; j += blockDim.x) {
-    float4 p = partials[(int64_t)j * rows + row];
-    SoftmaxState b{p.x, p.y, p.z, __float_as_int(p.w)};
-    st = sm_merge(st, b);
-  }
-  st = sm_warp_reduce(st);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) red[warp] = st;
-  __syncthreads();
+// Per row, before the logits GEMM: the shift c of the shifted exponentials,
+// the row's target logit (column 0 when the target is outside the
+// vocabulary) plus kShiftMargin, +inf for ignored rows. Any finite value
+// that is not far below the row maximum works; the logit of one column
+// is a lower bound of that maximum. One warp per row; also clears the
+// overflow flag of this call. Rows are 16-byte aligned with dim % 8 == 0.
+__global__ void __launch_bounds__(256) ce_shift_kernel(const bf16* __restrict__ H, int64_t h_ld,
+                                                       const bf16* __restrict__ W, int64_t w_ld,
+                                                       const int64_t* __restrict__ targets,
+                                                       int rows, int vocab, int dim,
+                                                       int64_t ignore_index, float* __restrict__ shift,
+                                                       int* __restrict__ flag) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) *flag = 0;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
   const int64_t t = targets[row];
-  const bool ignored = (t == ignore_index);
-  if (threadIdx.x == 0) {
-    SoftmaxState r = red[0];
-    const int nw = blockDim.x >> 5;
-    for (int i = 1; i < nw; ++i) r = sm_merge(r, red[i]);
+  if (t == ignore_index) {
+    if (lane == 0) shift[row] = INFINITY;
+    return;
+  }
+  const int64_t j = (t >= 0 && t < vocab) ? t : 0;
+  const bf16* h = H + (int64_t)row * h_ld;
+  const bf16* w = W + j * w_ld;
+  float acc = 0.f;
+  for (int k = lane * 8; k < dim; k += 256) {
+    const Vec16<bf16> a = ld16(h + k), b = ld16(w + k);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc = fmaf(__bfloat162float(a.v[i]), __bfloat162float(b.v[i]), acc);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) shift[row] = acc + kShiftMargin;
+}
+
+// After the logits GEMM, per row: merge the tile records (metrics), then the
+// gradient factors of the shifted exponentials:
+//   s = exp(c - lse) / denominator (0 for ignored rows), E[t] = (p_t - 1) exp(lse - c)
+// so that s * E is the row of dlogits. When the GEMM raised the overflow
+// flag every row takes c = lse (s = 1 / denominator) and the gated second
+// logits GEMM rewrites E, the target entries included. With hs set, also
+// hs[row] = s * hidden[row] (the dW GEMM's scaled operand).
+// 8 rows per block of 512 threads: thread (warp w, lane l) merges records
+// j = g, g + 64, ... of row r0 + (l & 7), g = 4 w + (l >> 3), ten loads in
+// flight at a time, so each load instruction of a warp reads four runs of 8
+// consecutive records (128 B) of the [record][row] layout; the 64 partial
+// states of a row are then merged in a fixed order (8 x 8). The block's
+// hidden rows (for hs) are copied to shared memory by cp.async before the
+// records are read, so their latency overlaps the merge without holding
+// registers (the kernel stays at two blocks per SM).
+constexpr int kStatRows = 8;
+constexpr int kStatBatch = 10;
+constexpr int kStatHidMax = 2048;  // dim up to which the hidden rows are staged in shared memory
+__global__ void __launch_bounds__(512, 2) ce_stats_kernel(
+    const float4* __restrict__ partials, int n_tiles, const float* __restrict__ zt,
+    const int64_t* __restrict__ targets, int rows, int vocab, float inv_den, int64_t ignore_index,
+    float* __restrict__ losses, float* __restrict__ entropies, int32_t* __restrict__ correct,
+    bf16* __restrict__ E, int64_t ld_e, float* __restrict__ shift, float* __restrict__ rscale,
+    const int* __restrict__ flag, const bf16* __restrict__ hidden, int64_t h_ld,
+    bf16* __restrict__ hs, int dim) {
+  constexpr int kGroups = 512 / kStatRows;
+  __shared__ SoftmaxState part[kGroups][kStatRows + 1];
+  __shared__ SoftmaxState part2[8][kStatRows + 1];
+  __shared__ float s_scale[kStatRows];
+  __shared__ __align__(16) bf16 hid[kStatRows * kStatHidMax];
+  const int r0 = blockIdx.x * kStatRows;
+  const int lr = threadIdx.x % kStatRows, g = threadIdx.x / kStatRows;
+  const int nvec = dim / 8;
+  const bool hid_smem = hs && dim <= kStatHidMax;
+  // the finalizing threads' row inputs, loaded before the records
+  int64_t pre_t = 0;
+  float pre_z = 0.f, pre_c = 0.f;
+  int pre_flag = 0;
+  if (threadIdx.x < kStatRows && r0 + (int)threadIdx.x < rows) {
+    const int row = r0 + threadIdx.x;
+    pre_t = targets[row];
+    pre_z = zt[row];  // meaningful only when the target is in range
+    if (E) {
+      pre_c = shift[row];
+      pre_flag = *flag;
+    }
+  }
+  if (hid_smem) {
+    for (int i = threadIdx.x; i < kStatRows * nvec; i += blockDim.x) {
+      const int rr = i / nvec;
+      if (r0 + rr >= rows) break;  // i only grows
+      const int k = (i - rr * nvec) * 8;
+      const bf16* src = hidden + (int64_t)(r0 + rr) * h_ld + k;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(hid + rr * dim + k)),
+                   "l"(src)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  {
+    const int row = r0 + lr;
+    SoftmaxState st = sm_init();
+    if (row < rows) {
+      for (int j0 = g; j0 < n_tiles; j0 += kStatBatch * kGroups) {
+        float4 p[kStatBatch];
+#pragma unroll
+        for (int i = 0; i < kStatBatch; ++i) {
+          const int j = j0 + i * kGroups;
+          p[i] = j < n_tiles ? partials[(int64_t)j * rows + row]
+                             : make_float4(-INFINITY, 0.f, 0.f, __int_as_float(0x7fffffff));
+        }
+#pragma unroll
+        for (int i = 0; i < kStatBatch; ++i)
+          st = sm_merge(st, SoftmaxState{p[i].x, p[i].y, p[i].z, __float_as_int(p[i].w)});
+      }
+    }
+    part[g][lr] = st;
+  }
+  __syncthreads();
+  if (threadIdx.x < 8 * kStatRows) {
+    const int sub = threadIdx.x / kStatRows;
+    SoftmaxState st = part[sub * (kGroups / 8)][lr];
+    for (int i = 1; i < kGroups / 8; ++i) st = sm_merge(st, part[sub * (kGroups / 8) + i][lr]);
+    part2[sub][lr] = st;
+  }
+  __syncthreads();
+  if (threadIdx.x < kStatRows && r0 + (int)threadIdx.x < rows) {
+    const int row = r0 + threadIdx.x;
+    SoftmaxState r = part2[0][threadIdx.x];
+    for (int i = 1; i < 8; ++i) r = sm_merge(r, part2[i][threadIdx.x]);
+    const int64_t t = pre_t;
+    const bool ignored = (t == ignore_index);
     const float safe_s = fmaxf(r.s, 1e-12f);
     const float lse = r.m + logf(safe_s);
     const bool in_range = (t >= 0 && t < vocab);
-    const float z_t = in_range ? zt[row] : 0.f;
+    const float z_t = in_range ? pre_z : 0.f;
     float loss = ignored ? 0.f : (lse - z_t);
     float ent = fmaxf(0.f, lse - r.w / safe_s);
     if (!isfinite(loss)) loss = 0.f;
@@ -678,52 +826,58 @@ __device__ __forceinline__ void ce_finalize_row(
     losses[row] = loss;
     entropies[row] = ent;
     correct[row] = (!ignored && in_range && r.idx == static_cast<int>(t)) ? 1 : 0;
-    *s_lse = lse;
+    if (E) {
+      float sc = 0.f;
+      if (!ignored) {
+        if (pre_flag) {
+          shift[row] = lse;
+          sc = inv_den;
+        } else {
+          const float c = pre_c;
+          sc = fast_exp2((c - lse) * kLog2e) * inv_den;
+          if (in_range) {
+            const float q = fast_exp2((z_t - lse) * kLog2e) - 1.f;
+            E[(int64_t)row * ld_e + t] = __float2bfloat16_rn(q * fast_exp2((lse - c) * kLog2e));
+          }
+        }
+      }
+      rscale[row] = sc;
+      s_scale[threadIdx.x] = sc;
+    }
   }
-  if (!write_grad) return;
+  if (!hs) return;  // block-uniform
+  if (hid_smem) asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
-  bf16* lrow = logits + (int64_t)row * ld_logits;
-  const int nvec = vocab / 8;
-  if (ignored) {
-    Vec16<bf16> zero;
-    zero.u = make_uint4(0, 0, 0, 0);
-    for (int i = threadIdx.x; i < nvec; i += blockDim.x) st16(lrow + i * 8, zero);
-    for (int c = nvec * 8 + threadIdx.x; c < vocab; c += blockDim.x) lrow[c] = __float2bfloat16_rn(0.f);
-    return;
-  }
-  const float lb = *s_lse * kLog2e;
-  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
-    Vec16<bf16> z = ld16(lrow + i * 8);
+  for (int i = threadIdx.x; i < kStatRows * nvec; i += blockDim.x) {
+    const int rr = i / nvec;
+    const int row = r0 + rr;
+    if (row >= rows) break;  // i only grows
+    const int k = (i - rr * nvec) * 8;
+    const float sc = s_scale[rr];
+    const Vec16<bf16> a = hid_smem ? *reinterpret_cast<const Vec16<bf16>*>(hid + rr * dim + k)
+                                   : ld16(hidden + (int64_t)row * h_ld + k);
     Vec16<bf16> o;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float p = fast_exp2(fmaf(__bfloat162float(z.v[j]), kLog2e, -lb));
-      if (i * 8 + j == t) p -= 1.f;
-      o.v[j] = __float2bfloat16_rn(p * inv_den);
-    }
-    st16(lrow + i * 8, o);
-  }
-  for (int c = nvec * 8 + threadIdx.x; c < vocab; c += blockDim.x) {
-    float p = fast_exp2(fmaf(__bfloat162float(lrow[c]), kLog2e, -lb));
-    if (c == t) p -= 1.f;
-    lrow[c] = __float2bfloat16_rn(p * inv_den);
+    for (int e = 0; e < 8; ++e) o.v[e] = __float2bfloat16_rn(sc * __bfloat162float(a.v[e]));
+    st16(hs + (int64_t)row * dim + k, o);
   }
 }
 
-// Rows [row0, row_end): block b takes rows row0 + b, row0 + b + gridDim.x, ...
-// `rows` is the partial records' row stride (all rows of the call).
-__global__ void __launch_bounds__(512) ce_finalize_kernel(
-    const float4* __restrict__ partials, int n_tiles, const float* __restrict__ zt,
-    const int64_t* __restrict__ targets, bf16* __restrict__ logits, int64_t ld_logits, int rows,
-    int vocab, float inv_den, int64_t ignore_index, float* __restrict__ losses,
-    float* __restrict__ entropies, int32_t* __restrict__ correct, int write_grad, int row0,
-    int row_end) {
-  __shared__ SoftmaxState red[16];
-  __shared__ float s_lse;
-  for (int row = row0 + blockIdx.x; row < row_end; row += gridDim.x) {
-    ce_finalize_row(row, partials, n_tiles, zt, targets, logits, ld_logits, rows, vocab, inv_den,
-                    ignore_index, losses, entropies, correct, write_grad, red, &s_lse);
-    __syncthreads();  // red / s_lse are rewritten by the next row
+// hs[row] = rscale[row] * hidden[row] (bf16), one block per row.
+__global__ void __launch_bounds__(256) ce_scale_rows_kernel(const bf16* __restrict__ hidden,
+                                                            int64_t h_ld,
+                                                            const float* __restrict__ rscale,
+                                                            int dim, bf16* __restrict__ hs) {
+  const int row = blockIdx.x;
+  const float sc = rscale[row];
+  const bf16* hrow = hidden + (int64_t)row * h_ld;
+  bf16* orow = hs + (int64_t)row * dim;
+  for (int k = threadIdx.x * 8; k < dim; k += blockDim.x * 8) {
+    const Vec16<bf16> a = ld16(hrow + k);
+    Vec16<bf16> o;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o.v[i] = __float2bfloat16_rn(sc * __bfloat162float(a.v[i]));
+    st16(orow + k, o);
   }
 }
 
@@ -755,10 +909,12 @@ __global__ void __launch_bounds__(1024) ce_sums_kernel(const float* __restrict__
   }
 }
 
-// out[m, n] = sum_s ws[s][m][n] (fixed order over s), stored as OutT.
+// out[m, n] = row_scale[m] * sum_s ws[s][m][n] (fixed order over s; no
+// row_scale: 1), stored as OutT. cols % 4 == 0.
 template <typename OutT>
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t slice,
-                                     int rows, int cols, OutT* __restrict__ out, int64_t ldo) {
+                                     int rows, int cols, OutT* __restrict__ out, int64_t ldo,
+                                     const float* __restrict__ row_scale) {
   const int64_t n4 = (int64_t)rows * cols / 4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -772,6 +928,13 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
       acc.w += v.w;
     }
     const int64_t r = e / cols, c = e % cols;
+    if (row_scale) {
+      const float k = row_scale[r];
+      acc.x *= k;
+      acc.y *= k;
+      acc.z *= k;
+      acc.w *= k;
+    }
     OutT* o = out + r * ldo + c;
     o[0] = Cvt<OutT>::from_f(acc.x);
     o[1] = Cvt<OutT>::from_f(acc.y);
@@ -890,7 +1053,9 @@ struct CEWorkspace {
   int n_vtiles;
   int n_parts;  // online-softmax records per row (vocab tiles x epilogue column groups)
   int splits;  // dX vocabulary splits
-  size_t off_logits, off_partials, off_zt, off_splitk, total;
+  size_t off_logits, off_partials, off_zt, off_splitk;
+  size_t off_shift, off_rscale, off_flag, off_hs;  // shifted-exponential gradient state
+  size_t total;
 };
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -939,27 +1104,41 @@ static CEWorkspace ce_layout(int64_t rows, int64_t vocab, int64_t dim) {
   off = align_up(off + (size_t)rows * 4, 256);
   w.off_splitk = off;
   off = align_up(off + (size_t)w.splits * rows * dim * 4, 256);
+  w.off_shift = off;
+  off = align_up(off + (size_t)rows * 4, 256);
+  w.off_rscale = off;
+  off = align_up(off + (size_t)rows * 4, 256);
+  w.off_flag = off;
+  off = align_up(off + 4, 256);
+  w.off_hs = off;
+  off = align_up(off + (size_t)rows * dim * 2, 256);
   w.total = off;
   return w;
 }
 
-// dH[M, D] = dL W: A = dlogits K-major, B = W MN-major. With `splits` > 1 the
-// vocabulary is split into fp32 slices reduced in a fixed order; otherwise the
-// GEMM epilogue writes dH directly. dh_dtype: SOUP_BF16 or SOUP_F32.
+// dH[M, D] = diag(row_scale) dL W: A = dlogits (or shifted exponentials)
+// K-major, B = W MN-major. With `splits` > 1 the vocabulary is split into
+// fp32 slices reduced in a fixed order (the row scale applied there);
+// otherwise the GEMM epilogue writes dH directly. dh_dtype: SOUP_BF16 or SOUP_F32.
 static int dx_gemm(const bf16* L, int64_t ld_logits, const void* weight, int64_t w_ld, int M, int V,
                    int D, int splits, float* splitk, void* dh, int dh_dtype, cudaStream_t stream,
-                   int gemm_stage = -1) {
+                   int gemm_stage = -1, const float* row_scale = nullptr) {
   CUtensorMap ma, mb;
   int rc;
   if ((rc = make_operand_map(&ma, L, false, M, V, ld_logits, BM))) return rc;
   if ((rc = make_operand_map(&mb, weight, true, D, V, w_ld, 64))) return rc;
   Sched sc{m_tiles(M), (D + kBN - 1) / kBN, splits, (V + BK - 1) / BK, 1};
+  // last vocabulary split first: the logits GEMM (which runs over the vocab in
+  // order) leaves the end of dL / E and of W in L2; the last split run is then
+  // the vocab's start, where the dW GEMM begins
+  sc.rev_split = 1;
   const bool bf = dh_dtype == SOUP_BF16;
   if (splits == 1) {
     const int vec = (aligned16(dh) && (D * (bf ? 2 : 4)) % 16 == 0) ? 1 : 0;
     CUtensorMap mc = ma;
     const int tma = (bf && vec && make_store_map(&mc, dh, D, M, D) == SOUP_OK) ? 1 : 0;
-    EpiStore<kBN>::Params ep{dh, D, 0, nullptr, 1.f, bf ? 1 : 0, 0, vec, M, D, nullptr, tma};
+    EpiStore<kBN>::Params ep{dh, D, 0, nullptr, 1.f, bf ? 1 : 0, 0, vec, M, D, nullptr, tma,
+                             row_scale};
     rc = launch_gemm<false, true, EpiStore<kBN>>(ma, mb, mc, sc, ep, stream);
     if (!rc && gemm_stage >= 0) mark_stage(gemm_stage, stream);
     return rc;
@@ -972,10 +1151,10 @@ static int dx_gemm(const bf16* L, int64_t ld_logits, const void* weight, int64_t
   if (blocks > 4 * num_sms()) blocks = 4 * num_sms();
   if (bf)
     splitk_reduce_kernel<bf16><<<blocks, 256, 0, stream>>>(splitk, splits, (int64_t)M * D, M, D,
-                                                          static_cast<bf16*>(dh), D);
+                                                          static_cast<bf16*>(dh), D, row_scale);
   else
     splitk_reduce_kernel<float><<<blocks, 256, 0, stream>>>(splitk, splits, (int64_t)M * D, M, D,
-                                                           static_cast<float*>(dh), D);
+                                                           static_cast<float*>(dh), D, row_scale);
   return launch_status();
 }
 
@@ -1044,29 +1223,52 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   float4* partials = reinterpret_cast<float4*>(ws + w.off_partials);
   float* zt = reinterpret_cast<float*>(ws + w.off_zt);
   float* splitk = reinterpret_cast<float*>(ws + w.off_splitk);
+  float* shift = reinterpret_cast<float*>(ws + w.off_shift);
+  float* rscale = reinterpret_cast<float*>(ws + w.off_rscale);
+  int* flag = reinterpret_cast<int*>(ws + w.off_flag);
+  bf16* hs = reinterpret_cast<bf16*>(ws + w.off_hs);
   const bool need_grad = dhidden || dweight;
   const int M = static_cast<int>(rows), V = static_cast<int>(vocab), D = static_cast<int>(dim);
+  const float inv_den = 1.f / (denominator > 0.f ? denominator : 1.f);
   int rc;
 
-  // 1. logits GEMM + online-softmax epilogue
+  // 0. row shifts of the stored exponentials (gradient only)
+  if (need_grad) {
+    ce_shift_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
+        static_cast<const bf16*>(hidden), h_ld, static_cast<const bf16*>(weight), w_ld, targets, M,
+        V, D, ignore_index, shift, flag);
+    if ((rc = launch_status())) return rc;
+  }
+  // 1. logits GEMM + online-softmax epilogue (+ E = exp(z - shift) stored)
+  CUtensorMap ma, mb, mc;
+  Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
+  EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, 0, M, V, 0,
+                        need_grad ? shift : nullptr, flag, 0};
   {
-    CUtensorMap ma, mb;
     if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
     if ((rc = make_operand_map(&mb, weight, false, vocab, dim, w_ld, b_box_rows()))) return rc;
-    Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
-    CUtensorMap mc = ma;
-    const int tma = (need_grad && make_store_map(&mc, L, V, M, w.ld_logits) == SOUP_OK) ? 1 : 0;
-    EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, 0, M, V, tma};
+    mc = ma;
+    ep.tma = (need_grad && make_store_map(&mc, L, V, M, w.ld_logits) == SOUP_OK) ? 1 : 0;
     if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, mc, sc, ep, stream))) return rc;
     mark_stage(0, stream);
   }
-  const float inv_den = 1.f / (denominator > 0.f ? denominator : 1.f);
-  // 2. metrics + dlogits
+  // 2. metrics, gradient row factors and target entries (+ hs for dW)
   {
-    ce_finalize_kernel<<<M, 512, 0, stream>>>(partials, w.n_parts, zt, targets, L, w.ld_logits, M,
-                                               V, inv_den, ignore_index, losses, entropies,
-                                               correct, need_grad ? 1 : 0, 0, M);
+    ce_stats_kernel<<<(M + kStatRows - 1) / kStatRows, 512, 0, stream>>>(partials, w.n_parts, zt, targets, M, V, inv_den,
+                                            ignore_index, losses, entropies, correct,
+                                            need_grad ? L : nullptr, w.ld_logits, shift, rscale,
+                                            flag, static_cast<const bf16*>(hidden), h_ld,
+                                            dweight ? hs : nullptr, D);
     if ((rc = launch_status())) return rc;
+    if (need_grad) {
+      // overflow fallback: the same GEMM with shift = lse, run only when the
+      // flag is set (otherwise every CTA returns at entry)
+      Sched sc2 = sc;
+      sc2.gate = flag;
+      EpiCE<kBN>::Params ep2 = ep;
+      ep2.onehot = 1;
+      if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, mc, sc2, ep2, stream))) return rc;
+    }
     mark_stage(1, stream);
   }
   if (sums) {
@@ -1074,16 +1276,16 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
     if ((rc = launch_status())) return rc;
     mark_stage(2, stream);
   }
-  // 4. dH = dL W  (split along the vocab)
+  // 4. dH = diag(s) E W  (split along the vocab)
   if (dhidden) {
     if ((rc = dx_gemm(L, w.ld_logits, weight, w_ld, M, V, D, w.splits, splitk, dhidden, SOUP_BF16,
-                      stream, 3)))
+                      stream, 3, rscale)))
       return rc;
     mark_stage(4, stream);
   }
-  // 5. dW = dL^T H
+  // 5. dW = E^T diag(s) H
   if (dweight) {
-    if ((rc = dweight_gemm(L, w.ld_logits, hidden, h_ld, M, V, D, nullptr, dweight, dw_dtype,
+    if ((rc = dweight_gemm(L, w.ld_logits, hs, D, M, V, D, nullptr, dweight, dw_dtype,
                            accumulate_dw, stream)))
       return rc;
     mark_stage(5, stream);
@@ -1113,10 +1315,17 @@ int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const 
     set_last_error("soup_ce_linear_dweight: workspace too small or misaligned");
     return SOUP_ERR_WORKSPACE;
   }
-  const bf16* L = reinterpret_cast<const bf16*>(static_cast<const uint8_t*>(workspace) + w.off_logits);
-  return dweight_gemm(L, w.ld_logits, hidden, h_ld, static_cast<int>(rows), static_cast<int>(vocab),
-                      static_cast<int>(dim), grad_scale, dweight, dw_dtype, accumulate_dw,
-                      as_stream(stream));
+  uint8_t* ws = static_cast<uint8_t*>(const_cast<void*>(workspace));
+  const bf16* L = reinterpret_cast<const bf16*>(ws + w.off_logits);
+  const float* rscale = reinterpret_cast<const float*>(ws + w.off_rscale);
+  bf16* hs = reinterpret_cast<bf16*>(ws + w.off_hs);
+  cudaStream_t st = as_stream(stream);
+  ce_scale_rows_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(
+      static_cast<const bf16*>(hidden), h_ld, rscale, static_cast<int>(dim), hs);
+  int rc = launch_status();
+  if (rc) return rc;
+  return dweight_gemm(L, w.ld_logits, hs, dim, static_cast<int>(rows), static_cast<int>(vocab),
+                      static_cast<int>(dim), grad_scale, dweight, dw_dtype, accumulate_dw, st);
 }
 
 // ------------------------------------------------------ vocab-parallel CE --

@@ -216,6 +216,13 @@ struct Sched {
   int kb_total;  // number of BK blocks along K (both segments)
   int order;
   int kb2;       // trailing blocks of kb_total read from the second segment (0: none)
+  // optional device flag written by an earlier kernel on the stream: when it
+  // reads 0 the whole grid returns at entry (a conditional launch that needs
+  // no host round trip)
+  const int* gate = nullptr;
+  // 1: k splits run last-first (the first wave reads the end of K, e.g. what
+  // the previous GEMM over the same operand left in L2)
+  int rev_split = 0;
   // maps and k offset of block kb
   __device__ __forceinline__ bool second(int kb) const { return kb >= kb_total - kb2; }
   __device__ __forceinline__ int k_elem(int kb) const {
@@ -226,6 +233,7 @@ struct Sched {
     int mn = m_tiles * n_tiles;
     ks = u / mn;
     int r = u - ks * mn;
+    if (rev_split) ks = splits - 1 - ks;
     if (order == 0) {
       mt = r % m_tiles;
       nt = r / m_tiles;
@@ -303,6 +311,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
                 typename Epi::Params ep, int* err) {
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
   using L = SmemLayout<BN, STAGES, EPI_WARPS>;
+  if (sched.gate && *sched.gate == 0) return;  // grid-uniform
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, multiple of 64");
   static_assert(2 * BN <= 512, "two accumulators must fit in 512 TMEM columns");
   constexpr int kTmemCols = (2 * BN <= 128) ? 128 : ((2 * BN <= 256) ? 256 : 512);
@@ -584,6 +593,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
                      typename Epi::Params ep, int* err) {
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
   static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+  if (sched.gate && *sched.gate == 0) return;  // grid-uniform
   constexpr int BNH = BN / 2;  // B rows held by each CTA
   using L = SmemLayout<BNH, STAGES, EPI_WARPS>;
   constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;

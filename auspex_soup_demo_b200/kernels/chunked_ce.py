@@ -12,8 +12,10 @@ the reference runs, per 32/64-token sequence chunk, an fp16 cuBLAS logits GEMM,
 one Triton CE kernel and an fp16 dhidden GEMM (``chunked_ce.py:183-264``),
 re-streaming the 467 MB lm_head twice per chunk. Here all tokens of a call go
 through one ``soup_ce_linear`` launch sequence (tcgen05 logits GEMM with the
-online-softmax epilogue, per-row finalize writing dlogits in place, split-K
-dX GEMM, dW GEMM) in bf16 with fp32 accumulation and fp32 metrics. ``chunk``
+online-softmax epilogue storing row-shifted exponentials exp(z - c), a per-row
+statistics pass, split-K dX GEMM with the per-row gradient factor applied in
+its reduce, dW GEMM) in bf16 with fp32 accumulation and fp32 metrics; no pass
+rewrites the [rows, vocab] buffer between the GEMMs. ``chunk``
 stays in the signature; token rows are processed in blocks sized by
 ``CE_WORKSPACE_BYTES`` instead, which bounds the logits buffer the way
 ``chunk`` bounds it in the reference. With a trainable head the lm_head
@@ -156,7 +158,7 @@ def fused_linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, targe
 
 def _fused_forward_keep_dlogits(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
                                 denominator: float, ignore_index: int):
-    """Forward + dhidden in one pass, leaving the dlogits in a workspace owned by the caller.
+    """Forward + dhidden in one pass, leaving the gradient state in a workspace owned by the caller.
 
     Returns ``(losses, ents, corr, sums, dh, state)`` where ``state`` holds the
     workspace and the bf16 hidden rows needed by :func:`_dweight_from_state`.

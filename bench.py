@@ -345,7 +345,8 @@ def run_b200(args):
     pairs = os.environ.get("SOUP_GEMM_PAIRS", "1") != "0"
     gemm_ms = [st[0], st[3], st[5]]
     achieved = FLOP_PER_GEMM / (statistics.mean(gemm_ms) * 1e-3) / 1e12
-    stage_names = ["logits_gemm", "finalize", "sums", "dx_gemm", "dx_reduce", "dw_gemm"]
+    # stage 0 includes the row-shift kernel, stage 1 the gated fallback GEMM launch
+    stage_names = ["logits_gemm", "row_stats", "sums", "dx_gemm", "dx_reduce", "dw_gemm"]
     traffic = _committed_traffic("gemm_pair_kernel" if pairs else "gemm_kernel")
 
     line = {
@@ -368,7 +369,9 @@ def run_b200(args):
                      + " (logits / dX / dW launches, 2*N*V*D each)",
                      "peak_source": f"{peak_src} bf16_tflops (burst)"},
         "stages_ms": {k: round(v, 4) for k, v in zip(stage_names, st)},
-        "gpu_launches": 6 * args.steps,
+        # per step: row shifts, logits GEMM, row stats, gated fallback GEMM (returns at
+        # entry unless a row overflowed), sums, dX GEMM, dX reduce, dW GEMM
+        "gpu_launches": 8 * args.steps,
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -139,13 +139,17 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
                    int32_t* correct, float* sums, void* dhidden, void* dweight, int dw_dtype,
                    int accumulate_dw, void* workspace, size_t workspace_bytes, void* stream);
 
-/* The lm_head gradient from the dlogits that a preceding soup_ce_linear call
+/* The lm_head gradient from the state that a preceding soup_ce_linear call
  * with a non-NULL dhidden left in `workspace` (same rows/vocab/dim/hidden):
  * dweight (+)= grad_scale[0] * dL^T H, where grad_scale is an optional device
- * fp32 scalar (the upstream gradient of the loss; NULL = 1). Lets an autograd
- * backward apply its upstream gradient inside the GEMM epilogue instead of in a
- * separate pass over the [vocab, dim] gradient. Extends chunked_ce.py:307-311
- * (the reference's head is frozen and has no gradient). */
+ * fp32 scalar (the upstream gradient of the loss; NULL = 1). The workspace
+ * holds dL factored as diag(s) E (E = exp(logit - c_row) in bf16 with the
+ * target entries corrected, s = exp(c_row - lse_row) / denominator per row);
+ * this call scales the hidden rows by s into the workspace and runs one GEMM.
+ * Lets an autograd backward apply its upstream gradient inside the GEMM
+ * epilogue instead of in a separate pass over the [vocab, dim] gradient.
+ * Extends chunked_ce.py:307-311 (the reference's head is frozen and has no
+ * gradient). */
 int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const void* hidden,
                            int64_t h_ld, int64_t rows, int64_t vocab, int64_t dim,
                            const float* grad_scale, void* dweight, int dw_dtype, int accumulate_dw,
@@ -183,7 +187,8 @@ int soup_ce_vp_backward(void* workspace, size_t workspace_bytes, const void* hid
 
 /* Stage timing for measurement: while set (n > 0), each soup_ce_linear call on
  * this host thread records events[i] on its stream after stage i:
- * 0 logits GEMM, 1 finalize, 2 sums, 3 dX GEMM, 4 dX reduce, 5 dW GEMM
+ * 0 row shifts + logits GEMM, 1 row statistics (+ the gated fallback GEMM),
+ * 2 sums, 3 dX GEMM, 4 dX reduce, 5 dW GEMM
  * (a stage that does not run records nothing). n = 0 clears. The events are
  * cudaEvent_t handles owned by the caller. */
 int soup_set_stage_events(void** events, int n);

@@ -2,7 +2,7 @@
 
 * the reference-compatible CE kernel over a logits buffer (in-place grad),
   launched exactly as the reference's test launches its Triton kernel;
-* the fused tcgen05 head CE (logits GEMM + online-softmax epilogue, finalize,
+* the fused tcgen05 head CE (logits GEMM + online-softmax epilogue, row statistics,
   dX and dW GEMMs) through the reference's autograd-Function signature.
 
 Tolerances follow the reference's targets: fp32 loss within 1e-4 relative,
@@ -83,8 +83,8 @@ def _inputs(n, v, d, seed=0, ignore_frac=0.1):
     return hidden, weight, targets
 
 
-def _check_fused(n, v, d, seed, workspace_bytes=None, dw_dtype=torch.float32):
-    hidden, weight, targets = _inputs(n, v, d, seed)
+def _check_fused(n, v, d, seed, workspace_bytes=None, dw_dtype=torch.float32, inputs=None):
+    hidden, weight, targets = inputs if inputs is not None else _inputs(n, v, d, seed)
     den = float((targets != -100).sum())
     logits = hidden.float() @ weight.float().t()
     loss, ent, corr, grad, lse = oracle.ce_rows(logits, targets, den)
@@ -124,6 +124,19 @@ def test_fused_ce_medium():
 def test_fused_ce_full_vocab_and_dim():
     # the benchmark's vocab and hidden size at 512 tokens (oracle runs in seconds)
     assert _check_fused(512, 151936, 1536, seed=3) <= 1
+
+
+def test_fused_ce_targets_far_below_the_maximum():
+    # half of the rows have logits ~100 wide with the target at the row minimum
+    # (loss ~100): above the stored exponentials' shift window, so the overflow
+    # flag is raised and the gated second logits GEMM rewrites them with shift = lse
+    hidden, weight, targets = _inputs(256, 4099, 192, seed=11)
+    hidden[:128] = (hidden[:128].float() * 60.0).to(torch.bfloat16)
+    logits = hidden.float() @ weight.float().t()
+    targets[:128] = logits[:128].argmin(dim=-1)
+    targets[3] = -100
+    assert float((logits[:128].max(-1).values - logits[:128].min(-1).values).min()) > 80.0
+    _check_fused(256, 4099, 192, seed=11, inputs=(hidden, weight, targets))
 
 
 def test_fused_ce_row_blocks_accumulate_dw():

@@ -695,21 +695,28 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
 // that is not far below the row maximum works; the logit of one column
 // is a lower bound of that maximum. One warp per row; also clears the
 // overflow flag of this call. Rows are 16-byte aligned with dim % 8 == 0.
+// With a vocabulary shard (vocab_offset > 0 or a shard of a larger vocab) the
+// target is looked up as targets[row] - vocab_offset; a row whose target is
+// not in the shard uses the shard's first column. has_ignore = 0 (the shard
+// forward does not know the ignore index): ignored rows are treated like
+// rows with a target elsewhere (their gradient factor is 0 later).
 __global__ void __launch_bounds__(256) ce_shift_kernel(const bf16* __restrict__ H, int64_t h_ld,
                                                        const bf16* __restrict__ W, int64_t w_ld,
                                                        const int64_t* __restrict__ targets,
                                                        int rows, int vocab, int dim,
+                                                       int64_t vocab_offset, int has_ignore,
                                                        int64_t ignore_index, float* __restrict__ shift,
                                                        int* __restrict__ flag) {
   if (blockIdx.x == 0 && threadIdx.x == 0) *flag = 0;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const int64_t t = targets[row];
-  if (t == ignore_index) {
+  const int64_t tg = targets[row];
+  if (has_ignore && tg == ignore_index) {
     if (lane == 0) shift[row] = INFINITY;
     return;
   }
+  const int64_t t = tg - vocab_offset;
   const int64_t j = (t >= 0 && t < vocab) ? t : 0;
   const bf16* h = H + (int64_t)row * h_ld;
   const bf16* w = W + j * w_ld;
@@ -1001,41 +1008,51 @@ __global__ void __launch_bounds__(256) ce_combine_kernel(
   lse_out[row] = lse;
 }
 
-// dlogits of one shard in place: (exp(z - lse) - onehot) / denominator.
-__global__ void __launch_bounds__(512) ce_dlogits_kernel(bf16* __restrict__ logits, int64_t ld,
-                                                         const float* __restrict__ lse,
-                                                         const int64_t* __restrict__ targets,
-                                                         int vocab_shard, int64_t vocab_offset,
-                                                         float inv_den, int64_t ignore_index) {
-  const int row = blockIdx.x;
-  bf16* lrow = logits + (int64_t)row * ld;
-  const int64_t tg = targets[row];
-  const int64_t t = tg - vocab_offset;
-  const int nvec = vocab_shard / 8;
-  if (tg == ignore_index) {
-    Vec16<bf16> zero;
-    zero.u = make_uint4(0, 0, 0, 0);
-    for (int i = threadIdx.x; i < nvec; i += blockDim.x) st16(lrow + i * 8, zero);
-    for (int c = nvec * 8 + threadIdx.x; c < vocab_shard; c += blockDim.x)
-      lrow[c] = __float2bfloat16_rn(0.f);
-    return;
+// Gradient factors of one shard's shifted exponentials from the global lse,
+// one warp per row: s = exp(c - lse) / denominator (0 for ignored rows),
+// E[t] = (p_t - 1) exp(lse - c) when the target is in the shard, and with hs
+// set hs[row] = s * hidden[row]. When the shard's logits GEMM raised the
+// overflow flag every row takes c = lse and the gated second GEMM rewrites E.
+__global__ void __launch_bounds__(256) ce_vp_grad_kernel(
+    const float* __restrict__ lse, const float* __restrict__ zt, const int64_t* __restrict__ targets,
+    int rows, int vocab_shard, int64_t vocab_offset, float inv_den, int64_t ignore_index,
+    bf16* __restrict__ E, int64_t ld_e, float* __restrict__ shift, float* __restrict__ rscale,
+    const int* __restrict__ flag, const bf16* __restrict__ hidden, int64_t h_ld,
+    bf16* __restrict__ hs, int dim) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float sc = 0.f;
+  if (lane == 0) {
+    const int64_t tg = targets[row];
+    const float l = lse[row];
+    const bool flagged = *flag != 0;
+    if (flagged) shift[row] = l;  // every row: the fallback GEMM reads it
+    if (tg != ignore_index) {
+      if (flagged) {
+        sc = inv_den;
+      } else {
+        const float c = shift[row];
+        sc = fast_exp2((c - l) * kLog2e) * inv_den;
+        const int64_t t = tg - vocab_offset;
+        if (t >= 0 && t < vocab_shard) {
+          const float q = fast_exp2((zt[row] - l) * kLog2e) - 1.f;
+          E[(int64_t)row * ld_e + t] = __float2bfloat16_rn(q * fast_exp2((l - c) * kLog2e));
+        }
+      }
+    }
+    rscale[row] = sc;
   }
-  const float lb = lse[row] * kLog2e;
-  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
-    Vec16<bf16> z = ld16(lrow + i * 8);
+  if (!hs) return;
+  sc = __shfl_sync(0xffffffffu, sc, 0);
+  const bf16* hrow = hidden + (int64_t)row * h_ld;
+  bf16* orow = hs + (int64_t)row * dim;
+  for (int k = lane * 8; k < dim; k += 256) {
+    const Vec16<bf16> a = ld16(hrow + k);
     Vec16<bf16> o;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float p = fast_exp2(fmaf(__bfloat162float(z.v[j]), kLog2e, -lb));
-      if (i * 8 + j == t) p -= 1.f;
-      o.v[j] = __float2bfloat16_rn(p * inv_den);
-    }
-    st16(lrow + i * 8, o);
-  }
-  for (int c = nvec * 8 + threadIdx.x; c < vocab_shard; c += blockDim.x) {
-    float p = fast_exp2(fmaf(__bfloat162float(lrow[c]), kLog2e, -lb));
-    if (c == t) p -= 1.f;
-    lrow[c] = __float2bfloat16_rn(p * inv_den);
+    for (int e = 0; e < 8; ++e) o.v[e] = __float2bfloat16_rn(sc * __bfloat162float(a.v[e]));
+    st16(orow + k, o);
   }
 }
 
@@ -1236,7 +1253,7 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   if (need_grad) {
     ce_shift_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
         static_cast<const bf16*>(hidden), h_ld, static_cast<const bf16*>(weight), w_ld, targets, M,
-        V, D, ignore_index, shift, flag);
+        V, D, 0, 1, ignore_index, shift, flag);
     if ((rc = launch_status())) return rc;
   }
   // 1. logits GEMM + online-softmax epilogue (+ E = exp(z - shift) stored)
@@ -1358,8 +1375,15 @@ int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shar
   bf16* L = reinterpret_cast<bf16*>(ws + w.off_logits);
   float4* partials = reinterpret_cast<float4*>(ws + w.off_partials);
   float* zt = reinterpret_cast<float*>(ws + w.off_zt);
+  float* shift = reinterpret_cast<float*>(ws + w.off_shift);
+  int* flag = reinterpret_cast<int*>(ws + w.off_flag);
   const int M = static_cast<int>(rows), V = static_cast<int>(vocab_shard), D = static_cast<int>(dim);
   int rc;
+  // row shifts from the shard's own columns (the forward does not know the ignore index)
+  ce_shift_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
+      static_cast<const bf16*>(hidden), h_ld, static_cast<const bf16*>(weight_shard), w_ld, targets,
+      M, V, D, vocab_offset, 0, 0, shift, flag);
+  if ((rc = launch_status())) return rc;
   CUtensorMap ma, mb;
   if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
   if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, b_box_rows())))
@@ -1367,7 +1391,7 @@ int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shar
   Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
   CUtensorMap mc = ma;
   const int tma = make_store_map(&mc, L, V, M, w.ld_logits) == SOUP_OK ? 1 : 0;
-  EpiCE<kBN>::Params ep{targets, partials, zt, L, w.ld_logits, vocab_offset, M, V, tma};
+  EpiCE<kBN>::Params ep{targets, partials, zt, L, w.ld_logits, vocab_offset, M, V, tma, shift, flag, 0};
   if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, mc, sc, ep, stream))) return rc;
   ce_shard_state_kernel<<<(M + 7) / 8, 256, 0, stream>>>(partials, w.n_parts, zt, targets, M, V,
                                                          vocab_offset, states);
@@ -1422,19 +1446,41 @@ int soup_ce_vp_backward(void* workspace, size_t workspace_bytes, const void* hid
   cudaStream_t stream = as_stream(stream_);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   bf16* L = reinterpret_cast<bf16*>(ws + w.off_logits);
+  float4* partials = reinterpret_cast<float4*>(ws + w.off_partials);
+  float* zt = reinterpret_cast<float*>(ws + w.off_zt);
   float* splitk = reinterpret_cast<float*>(ws + w.off_splitk);
+  float* shift = reinterpret_cast<float*>(ws + w.off_shift);
+  float* rscale = reinterpret_cast<float*>(ws + w.off_rscale);
+  int* flag = reinterpret_cast<int*>(ws + w.off_flag);
+  bf16* hs = reinterpret_cast<bf16*>(ws + w.off_hs);
   const int M = static_cast<int>(rows), V = static_cast<int>(vocab_shard), D = static_cast<int>(dim);
   const float den = denominator > 0.f ? denominator : 1.f;
-  ce_dlogits_kernel<<<M, 512, 0, stream>>>(L, w.ld_logits, lse, targets, V, vocab_offset, 1.f / den,
-                                           ignore_index);
-  int rc = launch_status();
-  if (rc) return rc;
+  int rc;
+  // gradient factors from the global lse (+ s * H for dW)
+  ce_vp_grad_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
+      lse, zt, targets, M, V, vocab_offset, 1.f / den, ignore_index, L, w.ld_logits, shift, rscale,
+      flag, static_cast<const bf16*>(hidden), h_ld, dweight_shard ? hs : nullptr, D);
+  if ((rc = launch_status())) return rc;
+  // overflow fallback: the shard's logits GEMM again with shift = lse, only when flagged
+  {
+    CUtensorMap ma, mb;
+    if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
+    if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, b_box_rows())))
+      return rc;
+    Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
+    sc.gate = flag;
+    CUtensorMap mc = ma;
+    const int tma = make_store_map(&mc, L, V, M, w.ld_logits) == SOUP_OK ? 1 : 0;
+    EpiCE<kBN>::Params ep{targets, partials, zt, L, w.ld_logits, vocab_offset, M, V, tma,
+                          shift, flag, 1};
+    if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, mc, sc, ep, stream))) return rc;
+  }
   if (dhidden_partial &&
       (rc = dx_gemm(L, w.ld_logits, weight_shard, w_ld, M, V, D, w.splits, splitk, dhidden_partial,
-                    dh_dtype, stream)))
+                    dh_dtype, stream, -1, rscale)))
     return rc;
   if (dweight_shard)
-    return dweight_gemm(L, w.ld_logits, hidden, h_ld, M, V, D, nullptr, dweight_shard, dw_dtype,
+    return dweight_gemm(L, w.ld_logits, hs, D, M, V, D, nullptr, dweight_shard, dw_dtype,
                         accumulate_dw, stream);
   return SOUP_OK;
 }

@@ -10,8 +10,10 @@ hidden state. Per step:
 2. one NCCL all-gather of the records (rows x 20 bytes per rank);
 3. ``soup_ce_vp_combine``: merge the ranks' records in rank order -> loss,
    entropy, hit, global lse (identical on every rank);
-4. ``soup_ce_vp_backward``: the shard's dlogits from the global lse, the
-   rank's partial dhidden and its dW shard (local);
+4. ``soup_ce_vp_backward``: the shard's per-row gradient factors from the
+   global lse (the forward stored exp(z - c) per row, so no pass rewrites
+   the shard's [rows, V_r] buffer), the rank's partial dhidden and its dW
+   shard (local);
 5. one NCCL all-reduce (sum) of the partial dhidden.
 
 Row semantics match the single-GPU path (reference ``chunked_ce.py:46-128``).

@@ -160,14 +160,17 @@ int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const 
  * [vocab_offset, vocab_offset + vocab_shard) of W runs:
  *   1. soup_ce_vp_forward: logits GEMM over its shard with the online-softmax
  *      epilogue; states[rows][5] = {max, sum exp, sum z*exp, global argmax
- *      (int32 bits), target logit or 0}; the shard's logits stay in workspace;
+ *      (int32 bits), target logit or 0}; the shard's row-shifted exponentials
+ *      exp(z - c_row) stay in workspace (c_row: the target logit when the
+ *      target is in the shard, else the shard's first column, + a margin);
  *   2. (caller) all-gather the states of all ranks into states_all[nranks][rows][5];
  *   3. soup_ce_vp_combine: merges the ranks' states per row in rank order
  *      (argmax ties keep the smaller index): losses, entropies, correct, the
  *      global lse [rows] and optional sums[2];
- *   4. soup_ce_vp_backward: dlogits of the shard in place from the global
- *      lse, this rank's partial dhidden = dL_shard W_shard (F32 or BF16) and
- *      its dW_shard = dL_shard^T H (local, no exchange);
+ *   4. soup_ce_vp_backward: the per-row gradient factors from the global lse
+ *      (the shard's buffer is not rewritten), this rank's partial dhidden =
+ *      dL_shard W_shard (F32 or BF16) and its dW_shard = dL_shard^T H (local,
+ *      no exchange);
  *   5. (caller) sum the partial dhidden over ranks (all-reduce).
  * Same row semantics as chunked_ce.py:46-128. */
 size_t soup_ce_vp_workspace_bytes(int64_t rows, int64_t vocab_shard, int64_t dim);

@@ -236,15 +236,22 @@ def test_autograd_function_callable_head_path():
     assert cosine(h.grad, ref[4]) >= 0.9999
 
 
-@pytest.mark.parametrize("world", [1, 3, 8])
-def test_vocab_parallel_ce_emulated_ranks(world):
+@pytest.mark.parametrize("world, far", [(1, False), (3, False), (8, False), (3, True)])
+def test_vocab_parallel_ce_emulated_ranks(world, far):
     """Shards processed one after another on one GPU, records combined as the
-    all-gather would, partial dhidden summed as the all-reduce would."""
+    all-gather would, partial dhidden summed as the all-reduce would. far: half
+    of the rows have logits ~100+ wide with the target at the row minimum, so
+    the shards' stored exponentials overflow their shift window and the gated
+    fallback GEMM of the backward rewrites them."""
     from auspex_soup_demo_b200.kernels.vocab_parallel import (shard_range, vp_backward_shard,
                                                               vp_combine, vp_forward_shard)
 
     n, v, d = 384, 20011, 256  # vocab not divisible by the rank count or the tile width
     hidden, weight, targets = _inputs(n, v, d, seed=11)
+    if far:
+        hidden[:192] = (hidden[:192].float() * 60.0).to(torch.bfloat16)
+        targets[:192] = (hidden[:192].float() @ weight.float().t()).argmin(dim=-1)
+        targets[3] = -100
     targets[5] = v - 1          # last vocabulary row (last shard)
     targets[6] = 0              # first row (first shard)
     den = float((targets != -100).sum())

@@ -214,6 +214,34 @@ def test_autograd_function_trainable_head_accumulates_weight_grad():
     assert abs(ratio2 - 4.0) < 0.03, ratio2
 
 
+def test_autograd_function_trainable_head_after_overflow_fallback():
+    # rows whose target is ~100 nats below the row maximum: the forward takes the
+    # gated fallback GEMM, and the backward's dW (soup_ce_linear_dweight, scaling the
+    # hidden rows by the stored per-row factors) must still match the oracle
+    B, S, D, V = 1, 130, 128, 3000
+    g = torch.Generator().manual_seed(12)
+    hidden = torch.randn(B, S, D, generator=g)
+    hidden[0, :64] *= 90.0
+    hidden = hidden.to(torch.bfloat16)
+    W = (0.05 * torch.randn(V, D, generator=g)).to(torch.bfloat16)
+    target = torch.randint(0, V, (B, S), generator=g)
+    logits = hidden[0].float() @ W.float().t()
+    target[0, :64] = logits[:64].argmin(dim=-1)
+    assert float((logits[:64].max(-1).values - logits[:64].min(-1).values).min()) > 80.0
+    den = float(S)
+    ref = oracle.chunked_ce(hidden, W, target, 64, den, compute_dw=True)
+    head = torch.nn.Linear(D, V, bias=False, dtype=torch.bfloat16, device="cuda")
+    with torch.no_grad():
+        head.weight.copy_(W.cuda())
+    Fn = make_triton_chunked_loss_function()
+    h = hidden.cuda().requires_grad_(True)
+    loss, *_ = Fn.apply(h, head, target.cuda(), 64, den, -100, True)
+    loss.backward()
+    assert abs(float(loss.detach()) - float(ref[0])) <= 1e-4 * abs(float(ref[0]))
+    assert cosine(h.grad, ref[4]) >= 0.9999
+    assert cosine(head.weight.grad, ref[5]) >= 0.999  # bf16-stored weight grad
+
+
 def test_autograd_function_callable_head_path():
     """A head without a findable weight: its logits + the CE kernel + autograd (reference :200-210)."""
     B, S, D, V = 2, 40, 64, 1000

@@ -631,16 +631,21 @@ static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const 
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cuda_status(cudaErrorInvalidDevice);
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // programmatic dependent launch: the prologue (barriers, TMEM allocation)
+  // overlaps the previous kernel's tail; the kernel waits (griddepcontrol.wait)
+  // before any global memory access
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(gemm_threads(kEpiWarps));
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (max_clusters[dev] == 0) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);

@@ -311,7 +311,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
                 typename Epi::Params ep, int* err) {
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
   using L = SmemLayout<BN, STAGES, EPI_WARPS>;
-  if (sched.gate && *sched.gate == 0) return;  // grid-uniform
+  if (sched.gate) {  // grid-uniform; the flag comes from an earlier kernel
+    pdl_wait();
+    if (*sched.gate == 0) return;
+  }
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, multiple of 64");
   static_assert(2 * BN <= 512, "two accumulators must fit in 512 TMEM columns");
   constexpr int kTmemCols = (2 * BN <= 128) ? 128 : ((2 * BN <= 256) ? 256 : 512);
@@ -365,6 +368,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int n_units = sched.units();
+  pdl_wait();  // no thread touches global memory before this (see gemm_pair_kernel)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -499,6 +503,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     if (lane == 0) bulk_wait_all();  // this warp's TMA stores, if any, are complete
   }
 
+  pdl_trigger();  // see gemm_pair_kernel
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -593,7 +598,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
                      typename Epi::Params ep, int* err) {
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "4 or 8 epilogue warps");
   static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
-  if (sched.gate && *sched.gate == 0) return;  // grid-uniform
+  if (sched.gate) {  // grid-uniform; the flag comes from an earlier kernel
+    pdl_wait();
+    if (*sched.gate == 0) return;
+  }
   constexpr int BNH = BN / 2;  // B rows held by each CTA
   using L = SmemLayout<BNH, STAGES, EPI_WARPS>;
   constexpr int kTmemCols = (2 * BN <= 256) ? 256 : 512;
@@ -652,6 +660,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int n_units = sched.units();
+  // Launched with programmatic dependent launch: the prologue above (barriers,
+  // TMEM, descriptor prefetch) may overlap the previous kernel; no thread
+  // touches global memory before this wait.
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -793,6 +805,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     if (lane == 0) bulk_wait_all();  // this warp's TMA stores, if any, are complete
   }
 
+  // the next kernel of the stream (if launched with programmatic dependent
+  // launch) may start its own prologue during this teardown; it still waits
+  // for this grid's completion before it reads what this grid wrote
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();

@@ -1180,7 +1180,8 @@ static int dx_gemm(const bf16* L, int64_t ld_logits, const void* weight, int64_t
   return launch_status();
 }
 
-// dW[V, D] (+)= scale * dL^T H: A = dlogits read MN-major, B = hidden MN-major.
+// dW[V, D] (+)= scale * dL^T H: A = dlogits (or shifted exponentials, with H
+// already scaled by the row factors) read MN-major, B = hidden MN-major.
 static int dweight_gemm(const bf16* L, int64_t ld_logits, const void* hidden, int64_t h_ld, int M,
                         int V, int D, const float* scale, void* dweight, int dw_dtype,
                         int accumulate, cudaStream_t stream) {

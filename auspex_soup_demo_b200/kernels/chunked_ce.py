@@ -156,7 +156,7 @@ def fused_linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, targe
     return losses, ents, corr, total, dh, dw
 
 
-def _fused_forward_keep_dlogits(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
+def _fused_forward_keep_grad_state(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
                                 denominator: float, ignore_index: int):
     """Forward + dhidden in one pass, leaving the gradient state in a workspace owned by the caller.
 
@@ -292,7 +292,7 @@ def make_triton_chunked_loss_function():
                 if want_dw and _rows_per_block(h2.shape[0], weight.shape[0], D,
                                                CE_WORKSPACE_BYTES) == h2.shape[0]:
                     # dW is deferred to backward, where grad_loss scales it in the epilogue
-                    losses, ents, corr, sums, dh, state = _fused_forward_keep_dlogits(
+                    losses, ents, corr, sums, dh, state = _fused_forward_keep_grad_state(
                         h2, weight, target.reshape(-1), den, ignore_index)
                     dw = None
                 else:

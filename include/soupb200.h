@@ -121,8 +121,10 @@ int soup_ce_rows(void* logits, int64_t row_stride, const int64_t* targets, float
 /* ---- Fused lm_head cross-entropy (tcgen05 GEMMs) -------------------------
  * Replaces chunk_cross_entropy_triton (chunked_ce.py:183-264) driven by
  * TritonChunkedHeadLoss.forward (chunked_ce.py:271-304): the logits GEMM with
- * an online-softmax epilogue, the per-row metrics, dlogits, the input
- * gradient and (new, no reference counterpart) the lm_head gradient.
+ * an online-softmax epilogue, the per-row metrics, the logits' gradient (kept
+ * factored: per-row factors times the stored exponentials exp(z - c_row), no
+ * [rows, vocab] pass between the GEMMs), the input gradient and (new, no
+ * reference counterpart) the lm_head gradient.
  * hidden [rows, dim] bf16 (row stride h_ld), weight [vocab, dim] bf16
  * (row stride w_ld), targets [rows] int64.
  * Outputs: losses/entropies [rows] fp32, correct [rows] int32,

@@ -2,7 +2,8 @@
 //
 // One soup_ce_linear call over `rows` tokens runs:
 //   0. ce_shift (gradient only): per row a shift c = the target logit
-//      (one dot product) + a margin; +inf for ignored rows;
+//      (one dot product; column 0's for ignored rows and targets outside the
+//      vocabulary) + a margin;
 //   1. logits GEMM  L = H W^T  (M=rows, N=vocab, K=dim; A, B K-major) whose
 //      epilogue, per row and 256-column vocab tile, keeps the online-softmax
 //      state (max, sum exp, sum z*exp, first argmax), captures the target
@@ -11,7 +12,7 @@
 //      index), writes loss / entropy / hit, the row factor
 //      s = exp(c - lse) / denominator and E[t] = (p_t - 1) exp(lse - c), so
 //      that s * E is the row of dlogits = (softmax - onehot) / denominator
-//      (s = 0 for ignored rows); a gated second logits GEMM with c = lse
+//      (s = 0 for ignored rows, whose E stays finite); a gated second logits GEMM with c = lse
 //      runs only if a row maximum came out far above its shift;
 //   3. ce_sums: fixed-order sums of the per-row losses and hits;
 //   4. dX GEMM  dH = diag(s) E W  (A = E K-major, B = W MN-major), split along
@@ -365,7 +366,7 @@ struct EpiSwiGLU {
 // Logits epilogue of the CE forward: online-softmax state per (row, tile),
 // target logit capture, bf16 logits store.
 // Shifted exponentials. With `shift` set, the tile stores E = exp(z - c_row)
-// in bf16 instead of the logit z (c = +inf stores 0: ignored rows). The
+// in bf16 instead of the logit z. The
 // gradient of the row is then dL = s_row * E with one entry corrected for the
 // target, s_row = exp(c_row - lse_row) / denominator, so the dX and dW GEMMs
 // read E directly and no pass rewrites the logits buffer. bf16 has the fp32
@@ -388,6 +389,8 @@ struct EpiCE {
     const float* shift;  // [M] or nullptr (store the logits themselves)
     int* flag;           // set to 1 when a row's maximum exceeds shift + kShiftGap
     int onehot;          // shift = lse: store E - 1 at the target column (= p - 1)
+    int has_ignore;      // rows whose target is ignore_index store E = 0 (statistics kept)
+    int64_t ignore_index;
   };
   static __device__ __forceinline__ void store(const Params& p, const CUtensorMap* tmc,
                                                uint8_t* stage, int lane, int& nstore,
@@ -401,22 +404,34 @@ struct EpiCE {
       __syncwarp();
     }
   }
-  static __device__ __forceinline__ void tile(const Params& p, const CUtensorMap* tmc, int row_base, int nt, int ks,
-                                              int quarter, int lane, uint32_t taddr, uint8_t* stage,
-                                              int group, int ngroups) {
-    const int row0 = row_base + quarter * 32;
+  // Shifted mode: the sums run against a fixed reference, the row's shift c:
+  // S = sum exp(z - c), W = sum z exp(z - c), whose terms are the stored E
+  // themselves, on packed fp32 pairs; the record is rescaled to the tile
+  // maximum once at the end. A chunk maximum more than kRebase above the
+  // reference (possible only on a row that also raises the overflow flag,
+  // kRebase > kShiftGap) moves the reference up so the sums stay finite; the
+  // values then stored for that row are rewritten by the fallback GEMM.
+  static constexpr float kRebase = 60.f;
+  static __device__ __forceinline__ void tile_shifted(const Params& p, const CUtensorMap* tmc,
+                                                      int row0, int nt, int lane, uint32_t taddr,
+                                                      uint8_t* stage, int group, int ngroups) {
     const int row = row0 + lane;
     const int nch = BN / 32 / ngroups;
     const bool row_ok = row < p.M;
     const int64_t t = row_ok ? p.targets[row] - p.vocab_offset : -1;
-    const bool shifted = p.logits && p.shift;
-    const float c = (shifted && row_ok) ? p.shift[row] : INFINITY;
-    const float cb = c * kLog2e;
-    float m = -INFINITY, s = 0.f, w = 0.f;
+    // rows past M: any finite reference (nothing of theirs is stored or recorded)
+    const float c = row_ok ? p.shift[row] : 0.f;
+    // an ignored row's gradient is 0: store zeros, which also keeps the dX / dW
+    // operands sparse (zero operands draw less tensor-core power)
+    const bool zero_row = p.has_ignore && row_ok && p.targets[row] == p.ignore_index;
+    float ref = c;
+    float m = -INFINITY;
     int bidx = 0x7fffffff;
     float ztv = 0.f;
     bool found = false, over = false;
     int nstore = 0;
+    uint64_t S2 = f2_pack(0.f, 0.f), W2 = f2_pack(0.f, 0.f);
+    const uint64_t L2 = f2_pack(kLog2e, kLog2e);
 #pragma unroll 1
     for (int cc = group * nch; cc < (group + 1) * nch; ++cc) {
       float v[32];
@@ -429,7 +444,107 @@ struct EpiCE {
         for (int j = 0; j < 32; ++j)
           if (j >= nvalid) v[j] = -1e30f;
       }
-      if (p.logits && !shifted) store(p, tmc, stage, lane, nstore, v, col0, row0);
+      float cm = v[0];
+#pragma unroll
+      for (int j = 1; j < 32; ++j) cm = fmaxf(cm, v[j]);
+      if (cm > m) {  // new maximum: its first index in the chunk
+        int ci = 0;
+#pragma unroll
+        for (int j = 31; j >= 0; --j)
+          if (v[j] == cm) ci = j;
+        m = cm;
+        bidx = col0 + ci;
+      }
+      const bool has_t = t >= col0 && t < col0 + 32 && t < p.N;
+      const int tj = static_cast<int>(t - col0);
+      if (has_t) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j == tj) ztv = v[j];
+        found = true;
+      }
+      over |= cm - c > kShiftGap;
+      if (cm - ref > kRebase) {
+        const float f = fast_exp2((ref - cm) * kLog2e);
+        const uint64_t f2 = f2_pack(f, f);
+        S2 = f2_mul(S2, f2);
+        W2 = f2_mul(W2, f2);
+        ref = cm;
+      }
+      const float rb = ref * kLog2e;
+      const uint64_t NR = f2_pack(-rb, -rb);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint64_t z = f2_pack(v[2 * i], v[2 * i + 1]);
+        float a0, a1;
+        f2_unpack(f2_fma(z, L2, NR), a0, a1);
+        const float e0 = fast_exp2(a0), e1 = fast_exp2(a1);  // 0 for padded columns
+        const uint64_t e = f2_pack(e0, e1);
+        S2 = f2_add(S2, e);
+        W2 = f2_fma(z, e, W2);
+        v[2 * i] = e0;
+        v[2 * i + 1] = e1;
+      }
+      if (p.onehot && has_t) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j == tj) v[j] -= 1.f;
+      }
+      if (zero_row) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      }
+      store(p, tmc, stage, lane, nstore, v, col0, row0);
+    }
+    if (row_ok) {
+      float s0, s1, w0, w1;
+      f2_unpack(S2, s0, s1);
+      f2_unpack(W2, w0, w1);
+      // relative to the tile maximum; a tile more than 80 below the reference
+      // holds probabilities below e^-48 of the row (the reference is at most
+      // 32 above the logit of one of the row's columns) and counts as empty
+      float sr = 0.f, wr = 0.f;
+      if (m != -INFINITY && ref - m <= 80.f) {
+        const float g = fast_exp2((ref - m) * kLog2e);
+        sr = (s0 + s1) * g;
+        wr = (w0 + w1) * g;
+      }
+      p.partials[(int64_t)(nt * ngroups + group) * p.M + row] = make_float4(m, sr, wr, __int_as_float(bidx));
+      if (found) p.zt[row] = ztv;
+      if (over) *p.flag = 1;
+    }
+  }
+  static __device__ __forceinline__ void tile(const Params& p, const CUtensorMap* tmc, int row_base, int nt, int ks,
+                                              int quarter, int lane, uint32_t taddr, uint8_t* stage,
+                                              int group, int ngroups) {
+    const int row0 = row_base + quarter * 32;
+    if (p.logits && p.shift) {
+      tile_shifted(p, tmc, row0, nt, lane, taddr, stage, group, ngroups);
+      return;
+    }
+    // raw mode: the logits themselves (or nothing) stored, running-maximum sums
+    const int row = row0 + lane;
+    const int nch = BN / 32 / ngroups;
+    const bool row_ok = row < p.M;
+    const int64_t t = row_ok ? p.targets[row] - p.vocab_offset : -1;
+    float m = -INFINITY, s = 0.f, w = 0.f;
+    int bidx = 0x7fffffff;
+    float ztv = 0.f;
+    bool found = false;
+    int nstore = 0;
+#pragma unroll 1
+    for (int cc = group * nch; cc < (group + 1) * nch; ++cc) {
+      float v[32];
+      tmem_ld32(taddr + cc * 32, v);
+      const int col0 = nt * BN + cc * 32;
+      const int nvalid = p.N - col0;
+      if (nvalid <= 0) continue;
+      if (nvalid < 32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j >= nvalid) v[j] = -1e30f;
+      }
+      if (p.logits) store(p, tmc, stage, lane, nstore, v, col0, row0);
       // chunk maximum with its first index
       float cm = v[0];
       int ci = 0;
@@ -446,33 +561,15 @@ struct EpiCE {
         m = cm;
         bidx = col0 + ci;
       }
-      const bool has_t = t >= col0 && t < col0 + 32 && t < p.N;
-      const int tj = static_cast<int>(t - col0);
-      if (has_t) {
+      if (t >= col0 && t < col0 + 32 && t < p.N) {
+        const int tj = static_cast<int>(t - col0);
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (j == tj) ztv = v[j];
         found = true;
       }
       const float mb = m * kLog2e;
-      if (shifted) {
-        // E_j = exp(z_j - m) * exp(m - c): one extra multiply per element
-        const float f = fast_exp2(mb - cb);
-        over |= cm - c > kShiftGap;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float e = fast_exp2(fmaf(v[j], kLog2e, -mb));  // 0 for padded columns
-          s += e;
-          w = fmaf(v[j], e, w);
-          v[j] = e * f;
-        }
-        if (p.onehot && has_t) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j == tj) v[j] -= 1.f;
-        }
-        store(p, tmc, stage, lane, nstore, v, col0, row0);
-      } else if (nvalid >= 32) {
+      if (nvalid >= 32) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float e = fast_exp2(fmaf(v[j], kLog2e, -mb));
@@ -493,7 +590,6 @@ struct EpiCE {
     if (row_ok) {
       p.partials[(int64_t)(nt * ngroups + group) * p.M + row] = make_float4(m, s, w, __int_as_float(bidx));
       if (found) p.zt[row] = ztv;
-      if (over) *p.flag = 1;
     }
   }
 };
@@ -695,32 +791,24 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
 
 // ------------------------------------------------------ CE row kernels -----
 // Per row, before the logits GEMM: the shift c of the shifted exponentials,
-// the row's target logit (column 0 when the target is outside the
-// vocabulary) plus kShiftMargin, +inf for ignored rows. Any finite value
-// that is not far below the row maximum works; the logit of one column
-// is a lower bound of that maximum. One warp per row; also clears the
-// overflow flag of this call. Rows are 16-byte aligned with dim % 8 == 0.
-// With a vocabulary shard (vocab_offset > 0 or a shard of a larger vocab) the
-// target is looked up as targets[row] - vocab_offset; a row whose target is
-// not in the shard uses the shard's first column. has_ignore = 0 (the shard
-// forward does not know the ignore index): ignored rows are treated like
-// rows with a target elsewhere (their gradient factor is 0 later).
+// the logit of the row's target (targets[row] - vocab_offset on a vocabulary
+// shard) plus kShiftMargin, or of column 0 when the target is outside the
+// vocabulary (shard) or the row is ignored: ignored rows still record their
+// entropy, and their gradient factor is 0 later. Any finite value not far
+// below the row maximum works; the logit of one column is a lower bound of
+// that maximum. One warp per row; also clears the overflow flag of this call.
+// Rows are 16-byte aligned with dim % 8 == 0.
 __global__ void __launch_bounds__(256) ce_shift_kernel(const bf16* __restrict__ H, int64_t h_ld,
                                                        const bf16* __restrict__ W, int64_t w_ld,
                                                        const int64_t* __restrict__ targets,
                                                        int rows, int vocab, int dim,
-                                                       int64_t vocab_offset, int has_ignore,
-                                                       int64_t ignore_index, float* __restrict__ shift,
+                                                       int64_t vocab_offset, float* __restrict__ shift,
                                                        int* __restrict__ flag) {
   if (blockIdx.x == 0 && threadIdx.x == 0) *flag = 0;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const int64_t tg = targets[row];
-  if (has_ignore && tg == ignore_index) {
-    if (lane == 0) shift[row] = INFINITY;
-    return;
-  }
   const int64_t t = tg - vocab_offset;
   const int64_t j = (t >= 0 && t < vocab) ? t : 0;
   const bf16* h = H + (int64_t)row * h_ld;
@@ -840,9 +928,9 @@ __global__ void __launch_bounds__(512, 2) ce_stats_kernel(
     correct[row] = (!ignored && in_range && r.idx == static_cast<int>(t)) ? 1 : 0;
     if (E) {
       float sc = 0.f;
+      if (pre_flag) shift[row] = lse;  // every row: the fallback GEMM reads it
       if (!ignored) {
         if (pre_flag) {
-          shift[row] = lse;
           sc = inv_den;
         } else {
           const float c = pre_c;
@@ -1259,14 +1347,14 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   if (need_grad) {
     ce_shift_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
         static_cast<const bf16*>(hidden), h_ld, static_cast<const bf16*>(weight), w_ld, targets, M,
-        V, D, 0, 1, ignore_index, shift, flag);
+        V, D, 0, shift, flag);
     if ((rc = launch_status())) return rc;
   }
   // 1. logits GEMM + online-softmax epilogue (+ E = exp(z - shift) stored)
   CUtensorMap ma, mb, mc;
   Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
   EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, 0, M, V, 0,
-                        need_grad ? shift : nullptr, flag, 0};
+                        need_grad ? shift : nullptr, flag, 0, 1, ignore_index};
   {
     if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
     if ((rc = make_operand_map(&mb, weight, false, vocab, dim, w_ld, b_box_rows()))) return rc;
@@ -1385,10 +1473,10 @@ int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shar
   int* flag = reinterpret_cast<int*>(ws + w.off_flag);
   const int M = static_cast<int>(rows), V = static_cast<int>(vocab_shard), D = static_cast<int>(dim);
   int rc;
-  // row shifts from the shard's own columns (the forward does not know the ignore index)
+  // row shifts from the shard's own columns
   ce_shift_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
       static_cast<const bf16*>(hidden), h_ld, static_cast<const bf16*>(weight_shard), w_ld, targets,
-      M, V, D, vocab_offset, 0, 0, shift, flag);
+      M, V, D, vocab_offset, shift, flag);
   if ((rc = launch_status())) return rc;
   CUtensorMap ma, mb;
   if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;

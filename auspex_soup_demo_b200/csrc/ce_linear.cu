@@ -1404,7 +1404,7 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   return SOUP_OK;
 }
 
-int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const void* hidden,
+int soup_ce_linear_dweight(void* workspace, size_t workspace_bytes, const void* hidden,
                            int64_t h_ld, int64_t rows, int64_t vocab, int64_t dim,
                            const float* grad_scale, void* dweight, int dw_dtype, int accumulate_dw,
                            void* stream) {
@@ -1426,7 +1426,7 @@ int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const 
     set_last_error("soup_ce_linear_dweight: workspace too small or misaligned");
     return SOUP_ERR_WORKSPACE;
   }
-  uint8_t* ws = static_cast<uint8_t*>(const_cast<void*>(workspace));
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
   const bf16* L = reinterpret_cast<const bf16*>(ws + w.off_logits);
   const float* rscale = reinterpret_cast<const float*>(ws + w.off_rscale);
   bf16* hs = reinterpret_cast<bf16*>(ws + w.off_hs);

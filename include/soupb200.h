@@ -152,7 +152,7 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
  * epilogue instead of in a separate pass over the [vocab, dim] gradient.
  * Extends chunked_ce.py:307-311 (the reference's head is frozen and has no
  * gradient). */
-int soup_ce_linear_dweight(const void* workspace, size_t workspace_bytes, const void* hidden,
+int soup_ce_linear_dweight(void* workspace, size_t workspace_bytes, const void* hidden,
                            int64_t h_ld, int64_t rows, int64_t vocab, int64_t dim,
                            const float* grad_scale, void* dweight, int dw_dtype, int accumulate_dw,
                            void* stream);

@@ -93,3 +93,44 @@ def test_dtype_codes():
     assert _lib.dtype_code(torch.bfloat16) == _lib.BF16
     with pytest.raises(TypeError):
         _lib.dtype_code(torch.int32)
+
+
+def test_ce_gradient_state_entry_points_validate_before_the_gpu():
+    """The lm_head-gradient call and the vocab-parallel stages reject bad arguments
+    (null pointers, bad dtype codes, a workspace smaller than their layout) before
+    any launch."""
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(16)  # 16-byte aligned, never dereferenced
+    n, v, d = 4, 64, 8
+    # soup_ce_linear_dweight(workspace, bytes, hidden, h_ld, rows, vocab, dim, grad_scale,
+    #                        dweight, dw_dtype, accumulate, stream)
+    st = lib.soup_ce_linear_dweight(None, 1 << 20, fake, d, n, v, d, None, fake, _lib.F32, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    st = lib.soup_ce_linear_dweight(fake, 1 << 20, fake, d, n, v, d, None, fake, 7, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    st = lib.soup_ce_linear_dweight(fake, 1 << 20, fake, d, n, v, 12, None, fake, _lib.F32, 0, None)
+    assert st in (_lib.SOUP_ERR_INVALID, _lib.SOUP_ERR_UNSUPPORTED)  # dim % 8 != 0, h_ld < dim
+    need = lib.soup_ce_linear_workspace_bytes(n, v, d)
+    st = lib.soup_ce_linear_dweight(fake, need - 1, fake, d, n, v, d, None, fake, _lib.F32, 0, None)
+    assert st == _lib.SOUP_ERR_WORKSPACE
+    # soup_ce_vp_forward(hidden, h_ld, weight_shard, w_ld, targets, rows, vocab_shard,
+    #                    vocab_offset, dim, states, workspace, bytes, stream)
+    st = lib.soup_ce_vp_forward(None, d, fake, d, fake, n, v, 0, d, fake, fake, 1 << 20, None)
+    assert st == _lib.SOUP_ERR_INVALID
+    st = lib.soup_ce_vp_forward(fake, d, fake, d, fake, n, v, -1, d, fake, fake, 1 << 20, None)
+    assert st == _lib.SOUP_ERR_INVALID  # negative vocab offset
+    need_vp = lib.soup_ce_vp_workspace_bytes(n, v, d)
+    st = lib.soup_ce_vp_forward(fake, d, fake, d, fake, n, v, 0, d, fake, fake, need_vp - 1, None)
+    assert st == _lib.SOUP_ERR_WORKSPACE
+    # soup_ce_vp_backward(workspace, bytes, hidden, h_ld, weight_shard, w_ld, targets, rows,
+    #                     vocab_shard, vocab_offset, dim, lse, denominator, ignore_index,
+    #                     dhidden_partial, dh_dtype, dweight_shard, dw_dtype, accumulate, stream)
+    st = lib.soup_ce_vp_backward(fake, need_vp, fake, d, fake, d, fake, n, v, 0, d, None, 1.0, -100,
+                                 fake, _lib.F32, None, _lib.BF16, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID  # no lse
+    st = lib.soup_ce_vp_backward(fake, need_vp, fake, d, fake, d, fake, n, v, 0, d, fake, 1.0, -100,
+                                 fake, 7, None, _lib.BF16, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID  # bad dhidden dtype
+    st = lib.soup_ce_vp_backward(fake, need_vp - 1, fake, d, fake, d, fake, n, v, 0, d, fake, 1.0,
+                                 -100, fake, _lib.F32, None, _lib.BF16, 0, None)
+    assert st == _lib.SOUP_ERR_WORKSPACE

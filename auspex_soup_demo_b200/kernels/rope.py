@@ -44,6 +44,17 @@ def _cos_view(cos: torch.Tensor, sin: torch.Tensor, x: torch.Tensor):
     return cos, sin, sb, ss
 
 
+def rope_tables(seq_len: int, head_dim: int, theta: float, dtype=torch.bfloat16, device=None):
+    """cos/sin [S, D] for positions 0..S-1 as transformers' Qwen2 rotary embedding
+    builds them: fp32 inverse frequencies and angles, ``cat(freqs, freqs)``, cast
+    to the activation dtype."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64, device=device).float()
+                           / head_dim))
+    freqs = torch.arange(seq_len, device=device).float()[:, None] * inv[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos().to(dtype), emb.sin().to(dtype)
+
+
 def _check_x(x: torch.Tensor):
     if x.dim() != 4:
         raise ValueError(f"RoPE input must be [B, H, S, D], got {tuple(x.shape)}")

@@ -14,7 +14,9 @@ hidden state. Per step:
    global lse (the forward stored exp(z - c) per row, so no pass rewrites
    the shard's [rows, V_r] buffer), the rank's partial dhidden and its dW
    shard (local);
-5. one NCCL all-reduce (sum) of the partial dhidden.
+5. one NCCL reduce-scatter (sum) of the bf16 partial dhidden over token
+   blocks, so each rank receives the rows it owns (or, on request, an fp32
+   all-reduce that leaves every row on every rank).
 
 Row semantics match the single-GPU path (reference ``chunked_ce.py:46-128``).
 """
@@ -111,28 +113,115 @@ def vp_backward_shard(state: ShardState, lse: torch.Tensor, denominator: float,
     return dh, dw
 
 
+def token_block(rows: int, rank: int, world: int):
+    """(start, count) of the token rows whose dhidden rank keeps after the
+    reduce-scatter: blocks of ceil(rows / world) rows in rank order, the last
+    one(s) shorter when rows is not a multiple of world."""
+    per = -(-rows // world)
+    start = min(rank * per, rows)
+    return start, min(per, rows - start)
+
+
+def _host_staged(group) -> bool:
+    """True when the group's backend moves host tensors only (gloo): the
+    collectives are then staged through host copies of the device buffers."""
+    import torch.distributed as dist
+
+    return dist.get_backend(group) == "gloo"
+
+
+def _all_gather_records(states: torch.Tensor, world: int, group) -> torch.Tensor:
+    import torch.distributed as dist
+
+    if _host_staged(group):
+        parts = [torch.empty_like(states, device="cpu") for _ in range(world)]
+        dist.all_gather(parts, states.cpu(), group=group)
+        return torch.stack(parts).to(states.device)
+    out = torch.empty(world, *states.shape, dtype=states.dtype, device=states.device)
+    dist.all_gather_into_tensor(out, states, group=group)
+    return out
+
+
+def _reduce_scatter_rows(dh: torch.Tensor, rank: int, world: int, group) -> torch.Tensor:
+    """Sum of every rank's dh [rows, D], of which this rank receives its token block."""
+    import torch.distributed as dist
+
+    rows = dh.shape[0]
+    start, count = token_block(rows, rank, world)
+    if _host_staged(group):
+        h = dh.cpu()
+        dist.all_reduce(h, op=dist.ReduceOp.SUM, group=group)
+        return h[start:start + count].to(dh.device)
+    per = -(-rows // world)
+    src = dh
+    if per * world != rows:  # zero rows pad the last block to the common size
+        src = torch.zeros(per * world, dh.shape[1], dtype=dh.dtype, device=dh.device)
+        src[:rows].copy_(dh)
+    out = torch.empty(per, dh.shape[1], dtype=dh.dtype, device=dh.device)
+    dist.reduce_scatter_tensor(out, src, op=dist.ReduceOp.SUM, group=group)
+    return out[:count]
+
+
 def vocab_parallel_cross_entropy(hidden: torch.Tensor, weight_shard: torch.Tensor, vocab_offset: int,
                                  vocab_total: int, targets: torch.Tensor, denominator: float = 1.0,
                                  ignore_index: int = IGNORE_INDEX, group=None, with_grad: bool = True,
-                                 compute_dw: bool = True, workspace: Optional[torch.Tensor] = None):
-    """All stages on this rank with NCCL collectives over `group`.
+                                 compute_dw: bool = True, workspace: Optional[torch.Tensor] = None,
+                                 dh_reduce: str = "scatter", timers: Optional[dict] = None):
+    """All stages on this rank with collectives over `group` (NCCL; a gloo group
+    stages them through host memory).
 
-    Returns ``(losses, entropies, correct, sums, dhidden fp32 | None, dW shard | None)``;
-    dhidden is summed over ranks (identical everywhere), dW covers this rank's rows.
+    Returns ``(losses, entropies, correct, sums, dhidden | None, dW shard | None)``;
+    dW covers this rank's vocabulary rows. dhidden:
+
+    * ``dh_reduce="scatter"`` (default): the bf16 partials are reduce-scattered
+      over token blocks; this rank gets rows ``token_block(rows, rank, world)``
+      of the summed dhidden (bf16), a quarter of the bytes of an fp32
+      all-reduce;
+    * ``dh_reduce="all"``: fp32 partials all-reduced, every rank gets all rows.
+
+    ``timers``: when a dict is given, (start, end) CUDA events of each stage
+    (forward, all_gather, combine, backward, dh_reduce) are stored in it.
     """
     import torch.distributed as dist
 
+    if dh_reduce not in ("scatter", "all"):
+        raise ValueError(f"dh_reduce must be 'scatter' or 'all', not {dh_reduce!r}")
     world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    stream = torch.cuda.current_stream(hidden.device)
+
+    def mark(name, start=True):
+        if timers is None:
+            return
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        timers[name] = (ev, None) if start else (timers[name][0], ev)
+
+    mark("forward")
     states, st = vp_forward_shard(hidden, weight_shard, targets, vocab_offset, workspace)
-    if world > 1:
-        states_all = torch.empty(world, *states.shape, dtype=states.dtype, device=states.device)
-        dist.all_gather_into_tensor(states_all, states, group=group)
-    else:
-        states_all = states.unsqueeze(0)
+    mark("forward", False)
+    mark("all_gather")
+    states_all = _all_gather_records(states, world, group) if world > 1 else states.unsqueeze(0)
+    mark("all_gather", False)
+    mark("combine")
     losses, ents, corr, lse, sums = vp_combine(states_all, st.targets, vocab_total, ignore_index)
+    mark("combine", False)
     dh = dw = None
     if with_grad:
-        dh, dw = vp_backward_shard(st, lse, denominator, ignore_index, compute_dw=compute_dw)
-        if world > 1:
-            dist.all_reduce(dh, op=dist.ReduceOp.SUM, group=group)
+        mark("backward")
+        dh_dtype = torch.bfloat16 if dh_reduce == "scatter" else torch.float32
+        dh, dw = vp_backward_shard(st, lse, denominator, ignore_index, dh_dtype=dh_dtype,
+                                   compute_dw=compute_dw)
+        mark("backward", False)
+        mark("dh_reduce")
+        if dh_reduce == "scatter":
+            dh = _reduce_scatter_rows(dh, rank, world, group) if world > 1 else dh
+        elif world > 1:
+            if _host_staged(group):
+                h = dh.cpu()
+                dist.all_reduce(h, op=dist.ReduceOp.SUM, group=group)
+                dh = h.to(dh.device)
+            else:
+                dist.all_reduce(dh, op=dist.ReduceOp.SUM, group=group)
+        mark("dh_reduce", False)
     return losses, ents, corr, sums, dh, dw

@@ -1,30 +1,43 @@
-"""Benchmark of the fused lm_head cross-entropy (forward + backward) on B200.
+"""Benchmark of the B200 QLoRA path: train-step tokens/s (headline), fused CE, memory-bound ops.
 
-Workload (default): hidden [2048, 1536] bf16 ~N(0,1), lm_head W [151936, 1536]
-bf16 ~N(0, 0.02), labels uniform in [0, 151936) with 10 % set to -100, chunk 32;
-outputs mean loss, entropy, top-1 hits, dhidden and dW. One step = one pass of
-the fused path over the 2048 tokens. Algorithmic work: 3 GEMMs x 2*N*V*D =
-2.868 TFLOP per step (logits, dX, dW). Metric: TFLOP/s, higher is better.
+Default line (``python bench.py --gpus N --steps K --warmup W``): the
+Qwen2.5-1.5B-architecture QLoRA train step, data parallel over the N ranks
+(one process per GPU, torchrun). Per GPU: batch 4 x 2048 tokens of uniform
+random ids (weak scaling: the per-GPU batch is the same at every N), 28
+decoder layers with NF4 (blocksize 64) base weights, LoRA r16 / alpha 32 on
+q/k/v/o/gate/up/down, the fused RMSNorm / RoPE / SwiGLU / head-CE ops, AdamW
+2e-4, and with N > 1 one NCCL all-reduce of the flat 73.9 MB LoRA gradient
+per step. The whole step (forward, backward, all-reduce, AdamW) is one CUDA
+graph replay.
 
-* ``value``: device-resident inputs, the tensor-level fused call, CUDA events
-  around exactly K steps (barrier + synchronize on both sides, max over ranks).
-* ``e2e``: the reference-facing autograd Function
-  (``make_triton_chunked_loss_function``) with the hidden states and labels
-  copied host->device (pinned) each step and loss + hit count read back.
-* ``roofline``: the tcgen05 GEMM kernel (three launches per step, 2*N*V*D
-  FLOP each) timed by CUDA events the library records between its stages.
-* ``cpu_baseline``: the same computation in PyTorch eager on the host cores
-  (the oracle restatement), on one 128-token chunk, all threads.
+* ``value``: tokens/s of all ranks, device-resident ids, CUDA events around
+  exactly K replays (barrier + synchronize on both sides, max over ranks).
+* ``e2e``: the same step with the ids and labels copied from pinned host
+  memory and the loss read back every step, inside the timed region.
+* ``roofline``: the step's dominant kernel, the gate/up GEMM with the SwiGLU
+  epilogue (2 launches per layer), timed live by CUDA events on its stream at
+  the step's shape; ``step_mfu``: algorithmic FLOPs per token (formula in
+  ``oracle.qlora_step.train_flop_per_token``) x tokens/s per GPU over the
+  measured sustained bf16 peak.
+* ``allreduce``: the gradient all-reduce alone (N > 1), CUDA events.
+* nested results of the same run: ``ce`` (fused head CE fwd+bwd TFLOP/s on
+  2048 tokens per rank, with its e2e, roofline, stages and a sustained run),
+  ``mem_ops`` (RMSNorm / SwiGLU / RoPE fwd+bwd HBM GB/s at the benchmark
+  shapes), ``ce_vp`` (vocab-parallel CE on 65536 tokens, strong scaling over
+  the N ranks, with its collective / compute split) and, at N = 1,
+  ``qlora_s512`` (the 1-GPU configuration: batch 4 x 512).
+* ``cpu_baseline`` (rank 0, N = 1): the reference's eager formulation of the
+  step on the host cores (``oracle.qlora_step``) on a bounded sample,
+  normalised by algorithmic FLOPs per token to the benchmark configuration.
 
-``--impl reference`` times only that CPU path (the reference's PyTorch eager
-formulation of the op) and prints its own line. With N > 1 GPUs (torchrun),
-every rank runs the same per-GPU workload on its own tokens (weak scaling,
-no collective on the data path).
+``--impl reference`` times only that CPU step and prints its own line.
+``--workload ce|rmsnorm|swiglu|rope|qlora|ce_vp`` prints one section alone.
 """
 
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -39,11 +52,19 @@ if ROOT not in sys.path:
 
 import torch  # noqa: E402
 
+# fused head CE workload
 N_TOK, DIM, VOCAB, CHUNK = 2048, 1536, 151936, 32
 FLOP_PER_GEMM = 2.0 * N_TOK * DIM * VOCAB
 FLOP_PER_STEP = 3 * FLOP_PER_GEMM
-METRIC = "fused-CE TFLOP/s (fwd+bwd, logits+dX+dW GEMMs)"
-WORKLOAD = "chunked lm_head cross-entropy fwd+bwd, hidden [2048,1536] bf16, W [151936,1536] bf16"
+CE_METRIC = "fused-CE TFLOP/s (fwd+bwd, logits+dX+dW GEMMs)"
+CE_WORKLOAD = "chunked lm_head cross-entropy fwd+bwd, hidden [2048,1536] bf16, W [151936,1536] bf16"
+
+# QLoRA step workload
+METRIC = "QLoRA train tokens/s"
+QLORA_BATCH, QLORA_SEQ, QLORA_LAYERS = 4, 2048, 28
+INTER = 8960
+# bounded CPU sample of the step: all 28 layers, one sequence of 256 tokens
+CPU_LAYERS, CPU_BATCH, CPU_SEQ = 28, 1, 256
 
 
 def _peaks():
@@ -63,6 +84,15 @@ def _sustained_peak():
             return float(json.load(f)["bf16_tflops_sustained"]), "measured"
     except Exception:
         return 1400.0, "fallback"
+
+
+def _committed_traffic(key):
+    """Mean DRAM bytes per launch of a kernel from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(f"{key}_bytes_per_launch")
+    except Exception:
+        return None
 
 
 class ClockSampler:
@@ -117,7 +147,334 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
-# ----------------------------------------------------------------- inputs ---
+class Ranks:
+    """One process per GPU (torchrun env), NCCL process group with a bounded timeout."""
+
+    def __init__(self, timeout_s: int = 300):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s), device_id=self.dev)
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = torch.tensor([v], device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t)
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def _free():
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
+def ctypes_void_p_array(values):
+    import ctypes
+
+    return (ctypes.c_void_p * len(values))(*values)
+
+
+def count_own_kernels(step, n_steps=1):
+    """Launches per step of this library's kernels (namespace soup::), from a CUPTI trace."""
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n_steps):
+            step()
+        torch.cuda.synchronize()
+    import re
+
+    mine = re.compile(r"\b(soup|tc)::")  # the library's namespaces (soup::, soup::tc::)
+    own = other = 0
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            if mine.search(e.name):
+                own += 1
+            elif "Memcpy" not in e.name and "Memset" not in e.name:
+                other += 1
+    return own // n_steps, other // n_steps
+
+
+def kernel_table(step, n_steps, top=40):
+    """Per-kernel device time of `n_steps` calls of `step` (CUPTI through
+    torch.profiler; kernels run back to back as in the timed region), printed to
+    stderr as: ms per step, share, launches per step, kernel name."""
+    import collections
+
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n_steps):
+            step()
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            agg[e.name][0] += 1
+            agg[e.name][1] += e.device_time_total
+    total = sum(v[1] for v in agg.values())
+    print(f"kernel time per step {total / n_steps / 1000:.3f} ms", file=sys.stderr)
+    for name, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:top]:
+        print(f"{t / n_steps / 1000:8.3f} ms {100 * t / total:5.1f}% {n // n_steps:5d}x  {name[:140]}",
+              file=sys.stderr)
+
+
+# ============================================================ CPU baseline ===
+def cpu_step_sample(steps: int, warmup: int, seconds: float = 0.0):
+    """Time the reference's eager step on the host (oracle.qlora_step) and
+    normalise by algorithmic FLOPs per token to the benchmark configuration.
+
+    Returns (tokens/s at the benchmark configuration, seconds per sample step,
+    steps timed, threads)."""
+    from oracle import qlora_step as ref
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = ref.build_model(CPU_LAYERS, seed=0)
+    runner = ref.EagerQLoRAStep(model)
+    g = torch.Generator().manual_seed(1234)
+    ids = torch.randint(0, VOCAB, (CPU_BATCH, CPU_SEQ), generator=g)
+    labels = ref.causal_labels(ids)
+    for _ in range(warmup):
+        runner.step(ids, labels)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        runner.step(ids, labels)
+        n += 1
+        el = time.perf_counter() - t0
+        if n >= steps and el >= seconds:
+            break
+    per = el / n
+    sample_flop = CPU_BATCH * CPU_SEQ * ref.train_flop_per_token(CPU_SEQ, CPU_LAYERS)
+    full_fpt = ref.train_flop_per_token(QLORA_SEQ, QLORA_LAYERS)
+    tok_s = sample_flop / per / full_fpt
+    del runner, model
+    gc.collect()
+    return tok_s, per, n, threads
+
+
+def _cpu_sample_text(per, n):
+    from oracle import qlora_step as ref
+
+    return (f"{n} steps of the eager PyTorch QLoRA step on the host (transformers Qwen2, "
+            f"{CPU_LAYERS} layers, bf16 dense frozen base, LoRA r16 on 7 projections, chunked "
+            f"fp32 head CE, AdamW) on batch {CPU_BATCH} x {CPU_SEQ} tokens, {per:.3f} s/step = "
+            f"{CPU_BATCH * CPU_SEQ * ref.train_flop_per_token(CPU_SEQ, CPU_LAYERS) / per / 1e12:.3f} "
+            f"TFLOP/s; tokens/s normalised by FLOPs per token to batch {QLORA_BATCH} x "
+            f"{QLORA_SEQ} ({ref.train_flop_per_token(QLORA_SEQ) / 1e9:.3f} GFLOP/token); "
+            "same_config false")
+
+
+def run_reference(args):
+    """--impl reference: the reference's eager step on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    tok_s, per, n, threads = cpu_step_sample(args.steps, args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tok_s, 3), "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids)",
+        "config": {"workload": "Qwen2.5-1.5B-architecture QLoRA step, eager PyTorch on the host",
+                   "sample": f"batch {CPU_BATCH} x {CPU_SEQ} tokens per step, {CPU_LAYERS} layers",
+                   "normalised_to": f"batch {QLORA_BATCH} x {QLORA_SEQ} per step",
+                   "same_config": False, "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": round(tok_s, 3), "unit": "tokens/s", "cores": threads,
+                         "kind": "port", "sample": _cpu_sample_text(per, n)},
+        "e2e": {"value": round(tok_s, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ============================================================= QLoRA step ===
+def measure_qlora(args, R: Ranks, batch: int, seq: int, with_extras: bool = True):
+    """Train-step tokens/s of the QLoRA step on this rank group (see module doc)."""
+    from auspex_soup_demo_b200 import _lib, apply, qlora
+    from oracle import qlora_step as ref
+
+    apply()
+    if args.no_recompute:
+        from auspex_soup_demo_b200.kernels import swiglu as _swiglu
+        _swiglu.RECOMPUTE = False
+    dev = R.dev
+    model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=args.layers), device=dev,
+                                    seed=0)
+    trainer = qlora.QLoRATrainer(model, lr=2e-4, ddp=R.world > 1)
+    g = torch.Generator().manual_seed(1234 + R.rank)
+    ids_cpu = torch.randint(0, VOCAB, (batch, seq), generator=g)
+    labels_cpu = qlora.causal_labels(ids_cpu)
+    ids, labels = ids_cpu.to(dev), labels_cpu.to(dev)
+    den = float((labels_cpu != -100).sum())
+    # every rank's batch has the same number of labelled tokens (no padding), so
+    # averaging the per-rank gradients gives the gradient of the global mean loss
+    use_graph = not args.no_graph
+    if use_graph:
+        trainer.capture(ids, labels, den, warmup=max(args.warmup, 3))
+
+    def one_step():
+        return trainer.replay() if use_graph else trainer.step(ids, labels, den)
+
+    for _ in range(max(args.warmup, 3)):
+        one_step()
+    torch.cuda.synchronize()
+    assert _lib.device_error(dev) == 0
+    stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(R.local) as clocks:
+        R.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            loss, _ = one_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        R.barrier()
+    ms = R.max(e0.elapsed_time(e1) / args.steps)
+    tok_s = R.world * batch * seq / (ms * 1e-3)
+
+    # e2e: ids and labels from pinned host memory each step, loss read back
+    ids_pin = ids_cpu.pin_memory()
+    lab_pin = labels_cpu.pin_memory()
+    out_pin = torch.empty(1, dtype=torch.float32).pin_memory()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    R.barrier()
+    torch.cuda.synchronize()
+    e2.record(stream)
+    for _ in range(args.steps):
+        ids.copy_(ids_pin, non_blocking=True)
+        labels.copy_(lab_pin, non_blocking=True)
+        loss, _ = one_step()
+        out_pin.copy_(loss.view(1), non_blocking=True)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    R.barrier()
+    e2e_ms = R.max(e2.elapsed_time(e3) / args.steps)
+    assert _lib.device_error(dev) == 0
+    res = {"tokens_per_s": tok_s, "ms": ms, "e2e_ms": e2e_ms, "loss": float(out_pin[0]),
+           "clocks": clocks.summary(), "graph": use_graph,
+           "lora_params": sum(p.numel() for p in qlora.lora_parameters(model))}
+
+    if with_extras:
+        # kernels of this library per step (every rank replays: the graph holds the all-reduce)
+        own, other = count_own_kernels(one_step)
+        res["own_kernels_per_step"] = own
+        res["other_kernels_per_step"] = other
+        # the gradient all-reduce alone
+        if R.world > 1:
+            ar = []
+            for _ in range(6):
+                a0 = torch.cuda.Event(enable_timing=True)
+                a1 = torch.cuda.Event(enable_timing=True)
+                R.barrier()
+                a0.record(stream)
+                trainer._allreduce_grads()
+                a1.record(stream)
+                torch.cuda.synchronize()
+                ar.append(a0.elapsed_time(a1))
+            ar_ms = R.max(statistics.median(ar[1:]))
+            nbytes = trainer.flat_grad.numel() * 4
+            res["allreduce"] = {"ms": round(ar_ms, 4), "bytes": nbytes,
+                                "busbw_gbs": round(2 * (R.world - 1) / R.world * nbytes / (ar_ms * 1e-3) / 1e9, 1),
+                                "share_of_step": round(ar_ms / ms, 4),
+                                "op": "NCCL all_reduce(AVG) of the flat fp32 LoRA gradient, eager, "
+                                      "CUDA events, median of 5, max over ranks"}
+        # dominant kernel: the gate/up GEMM with the SwiGLU epilogue, at the step's shape
+        grp = model.model.layers[0].mlp.gate_proj.lora_group
+        if grp is not None and grp.interleaved:
+            res["dominant"] = time_gate_up_gemm(grp, batch * seq, dev)
+        if args.profile and R.rank == 0:
+            kernel_table(one_step, 2)
+        sus_peak, sus_src = _sustained_peak()
+        fpt = ref.train_flop_per_token(seq, args.layers)
+        res["step_mfu"] = {"flop_per_token": fpt,
+                           "achieved_tflops_per_gpu": round(fpt * tok_s / R.world / 1e12, 1),
+                           "frac": round(fpt * tok_s / R.world / 1e12 / sus_peak, 4),
+                           "peak": sus_peak,
+                           "peak_source": f"{sus_src} bf16_tflops_sustained (the step runs for "
+                                          "seconds under the power cap)",
+                           "formula": "oracle.qlora_step.train_flop_per_token: 4 x base and head "
+                                      "params (fwd + dX), 3 x causal attention fwd, 6 r (in+out) "
+                                      "per LoRA projection; recompute, NF4 and AdamW not counted"}
+    trainer.release_graph()
+    del trainer, model
+    _free()
+    return res
+
+
+def time_gate_up_gemm(group, m: int, dev, reps: int = 20):
+    """CUDA-event duration of the gate/up GEMM + SwiGLU epilogue launch (forward and
+    recompute-backward modes) at m tokens: the QLoRA step's largest kernel."""
+    from auspex_soup_demo_b200 import qlora
+
+    k = group.in_features
+    g = torch.Generator(device=dev).manual_seed(5)
+    x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+    w = group.base_weight(torch.bfloat16)
+    As16, Bblk = group.factors(torch.bfloat16)
+    xa = x @ As16.t()
+    inter = group.outs[0]
+    h = torch.empty(m, inter, device=dev, dtype=torch.bfloat16)
+    dh = torch.randn(m, inter, device=dev, generator=g).to(torch.bfloat16)
+    dy = torch.empty(m, group.n_total, device=dev, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    for mode, name in ((0, "fwd"), (1, "bwd")):
+        def launch():
+            if mode == 0:
+                qlora.swiglu_gemm(x, w, xa, Bblk, None, 0, h)
+            else:
+                qlora.swiglu_gemm(x, w, xa, Bblk, None, 1, dh, dy)
+        for _ in range(3):
+            launch()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            launch()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        out[name] = e0.elapsed_time(e1) / reps
+    n = group.n_total
+    r = Bblk.shape[1]
+    flop = 2.0 * m * n * (k + r)
+    peak, _, src = _peaks()
+    mean_ms = (out["fwd"] + out["bwd"]) / 2
+    achieved = flop / (mean_ms * 1e-3) / 1e12
+    return {"kernel": "soup::tc::gemm_pair_kernel<EpiSwiGLU> (gate/up + rank-32 LoRA k-block, "
+                      "SwiGLU epilogue; forward and recompute-backward modes)",
+            "shape": f"M {m} x N {n} (gate/up interleaved) x K {k} + rank {r}",
+            "flop_per_launch": flop, "ms_fwd": round(out["fwd"], 4), "ms_bwd": round(out["bwd"], 4),
+            "achieved": round(achieved, 1), "peak": peak, "frac": round(achieved / peak, 4),
+            "peak_source": f"{src} bf16_tflops (burst: the launch is timed alone, {reps} back to back)",
+            "traffic": _committed_traffic(f"gemm_pair_kernel_swiglu_m{m}")}
+
+
+# ============================================================== fused CE ====
 def make_inputs(seed: int, device):
     g = torch.Generator().manual_seed(seed)
     hidden = torch.randn(N_TOK, DIM, generator=g).to(torch.bfloat16)
@@ -128,7 +485,6 @@ def make_inputs(seed: int, device):
     return hidden, labels, weight
 
 
-# ----------------------------------------------------------- CPU baseline ---
 def cpu_eager_chunk(hidden_chunk, weight_cpu, labels_chunk, den):
     """One chunk of the reference's eager formulation: h@W^T, fp32 CE, autograd for dh and dW."""
     h = hidden_chunk.clone().requires_grad_(True)
@@ -141,10 +497,10 @@ def cpu_eager_chunk(hidden_chunk, weight_cpu, labels_chunk, den):
         _ = -(logp.exp() * logp).sum(-1)
         _ = (logits.argmax(-1) == labels_chunk).sum()
     loss.backward()
-    return float(loss)
+    return float(loss.detach())
 
 
-def cpu_baseline(seconds: float = 8.0, rows: int = 4 * CHUNK):
+def ce_cpu_baseline(seconds: float = 8.0, rows: int = 4 * CHUNK):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(7)
@@ -167,65 +523,15 @@ def cpu_baseline(seconds: float = 8.0, rows: int = 4 * CHUNK):
                       f"PyTorch eager bf16 GEMMs + fp32 CE + autograd dh/dW, {per * 1e3:.1f} ms/chunk"}
 
 
-# ------------------------------------------------------------------- runs ---
-def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    rows = 4 * CHUNK
-    g = torch.Generator().manual_seed(7)
-    weight = (0.02 * torch.randn(VOCAB, DIM, generator=g)).to(torch.bfloat16)
-    hidden = torch.randn(rows, DIM, generator=g).to(torch.bfloat16)
-    labels = torch.randint(0, VOCAB, (rows,), generator=g)
-    labels[torch.rand(rows, generator=g) < 0.1] = -100
-    den = float((labels != -100).sum())
-    for _ in range(args.warmup):
-        cpu_eager_chunk(hidden, weight, labels, den)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        cpu_eager_chunk(hidden, weight, labels, den)
-    el = time.perf_counter() - t0
-    per = el / args.steps
-    flop = 3 * 2.0 * rows * DIM * VOCAB
-    val = flop / per / 1e12
-    line = {
-        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "TFLOP/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": f"{rows}-token chunk per step",
-                   "l2": "n/a (CPU)"},
-        "cpu_baseline": {"value": round(val, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": f"one {rows}-token chunk per step, PyTorch eager on the host"},
-        "e2e": {"value": round(val, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-
-
-def run_b200(args):
-    import torch.distributed as dist
-
+def measure_ce(args, R: Ranks):
+    """Fused head CE fwd+bwd on 2048 tokens per rank (weak scaling, no collective)."""
     from auspex_soup_demo_b200 import _lib
     from auspex_soup_demo_b200.kernels import make_triton_chunked_loss_function
     from auspex_soup_demo_b200.kernels.chunked_ce import fused_linear_cross_entropy
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    hidden_cpu, labels_cpu, weight = make_inputs(rank, dev)
+    dev = R.dev
+    world = R.world
+    hidden_cpu, labels_cpu, weight = make_inputs(R.rank, dev)
     hidden = hidden_cpu.to(dev)
     labels = labels_cpu.to(dev)
     den = float((labels_cpu != -100).sum())
@@ -247,8 +553,8 @@ def run_b200(args):
     torch.cuda.synchronize()
     assert _lib.device_error(dev) == 0
 
-    # ---- per-stage timing (one extra pass per step, outside the timed loop) ----
-    handles = (ctypes_void_p_array([e.cuda_event for e in stage_ev]))
+    # per-stage timing (one extra pass per step, outside the timed loop)
+    handles = ctypes_void_p_array([e.cuda_event for e in stage_ev])
     _lib.lib().soup_set_stage_events(handles, 6)
     stage_ms = [[] for _ in range(6)]
     for _ in range(max(3, min(args.steps, 10))):
@@ -262,27 +568,22 @@ def run_b200(args):
     _lib.lib().soup_set_stage_events(None, 0)
     st = [statistics.median(v) for v in stage_ms]
 
-    # ---- timed region: device-resident inputs ----
+    # timed region: device-resident inputs
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        barrier()
+    with ClockSampler(R.local) as clocks:
+        R.barrier()
         torch.cuda.synchronize()
         ev0.record(stream)
         for _ in range(args.steps):
-            out = step()
+            step()
         ev1.record(stream)
         torch.cuda.synchronize()
-        barrier()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    ms_all = ms
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_all = float(t)
+        R.barrier()
+    ms_all = R.max(ev0.elapsed_time(ev1) / args.steps)
     value = world * FLOP_PER_STEP / (ms_all * 1e-3) / 1e12
 
-    # ---- e2e through the reference-facing autograd Function, host buffers ----
+    # e2e through the reference-facing autograd Function, host buffers
     head = torch.nn.Linear(DIM, VOCAB, bias=False, dtype=torch.bfloat16, device=dev)
     with torch.no_grad():
         head.weight.copy_(weight)
@@ -335,43 +636,34 @@ def run_b200(args):
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    barrier()
+    R.barrier()
     torch.cuda.synchronize()
     e0.record(stream)
     e2e_run(args.steps, e0)
     e1.record(stream)
     torch.cuda.synchronize()
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t)
+    R.barrier()
+    e2e_ms = R.max(e0.elapsed_time(e1) / args.steps)
     e2e_val = world * FLOP_PER_STEP / (e2e_ms * 1e-3) / 1e12
     assert _lib.device_error(dev) == 0
 
-    # ---- sustained: the device-resident step back to back for ~1 s. The K-step
-    # region above lasts K x ~2.2 ms, mostly at boost clocks before the power
-    # controller reacts; this run settles under the 1 kW cap and its clock record
-    # shows it (sw_power_cap). Every rank runs it (same collectives).
+    # sustained: the device-resident step back to back for ~1 s; the K-step region
+    # runs mostly at boost clocks before the power controller reacts, this one
+    # settles under the 1 kW cap (sw_power_cap in its clock record)
     sustained = None
     if args.sustained_steps > 0:
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
-        with ClockSampler(local) as sclocks:
-            barrier()
+        with ClockSampler(R.local) as sclocks:
+            R.barrier()
             torch.cuda.synchronize()
             s0.record(stream)
             for _ in range(args.sustained_steps):
                 step()
             s1.record(stream)
             torch.cuda.synchronize()
-            barrier()
-        sus_ms = s0.elapsed_time(s1) / args.sustained_steps
-        if world > 1:
-            t = torch.tensor([sus_ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            sus_ms = float(t)
+            R.barrier()
+        sus_ms = R.max(s0.elapsed_time(s1) / args.sustained_steps)
         sus_val = world * FLOP_PER_STEP / (sus_ms * 1e-3) / 1e12
         sus_peak, sus_src = _sustained_peak()
         sustained = {"steps": args.sustained_steps, "value": round(sus_val, 2),
@@ -382,20 +674,17 @@ def run_b200(args):
                      "peak_source": f"{sus_src} bf16_tflops_sustained (cuBLAS, seconds-long loop)"}
         assert _lib.device_error(dev) == 0
 
-    peak_tf, peak_hbm, peak_src = _peaks()
+    peak_tf, _, peak_src = _peaks()
     pairs = os.environ.get("SOUP_GEMM_PAIRS", "1") != "0"
     gemm_ms = [st[0], st[3], st[5]]
     achieved = FLOP_PER_GEMM / (statistics.mean(gemm_ms) * 1e-3) / 1e12
     # stage 0 includes the row-shift kernel, stage 1 the gated fallback GEMM launch
     stage_names = ["logits_gemm", "row_stats", "sums", "dx_gemm", "dx_reduce", "dw_gemm"]
     traffic = _committed_traffic("gemm_pair_kernel" if pairs else "gemm_kernel")
-
-    line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_all, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": WORKLOAD, "tokens_per_gpu": N_TOK, "chunk": CHUNK,
+    out = {
+        "metric": CE_METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "ms_per_step": round(ms_all, 4), "scaling": "weak",
+        "config": {"workload": CE_WORKLOAD, "tokens_per_gpu": N_TOK, "chunk": CHUNK,
                    "ignore_frac": 0.1, "parallelism": f"dp{world} (tokens sharded, no collective)",
                    "l2": "inputs larger than L2 (W 467 MB, logits buffer 622 MB)"},
         "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s",
@@ -412,21 +701,17 @@ def run_b200(args):
         "stages_ms": {k: round(v, 4) for k, v in zip(stage_names, st)},
         # per step: row shifts, logits GEMM, row stats, gated fallback GEMM (returns at
         # entry unless a row overflowed), sums, dX GEMM, dX reduce, dW GEMM
-        "gpu_launches": 8 * args.steps,
+        "gpu_launches_per_step": 8,
         "clocks": clocks.summary(),
         "sustained": sustained,
     }
-    if rank == 0 and world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    del head, weight, hidden, h_buf
+    _free()
+    return out
 
 
 # ----------------------------------------------- memory-bound op workloads ---
-def run_memory_op(args):
+def measure_mem_op(wl: str, batch: int, seq: int, steps: int, warmup: int, dev):
     """HBM GB/s of one memory-bound fused op (fwd + bwd) at its benchmark shape.
 
     Inputs rotate over enough buffer sets to exceed twice the L2 (126 MB);
@@ -435,23 +720,16 @@ def run_memory_op(args):
     rmsnorm 5*N*D*4 (x, y; dy, x, dx) fp32 [N, 1536]; swiglu 8*N*I*2
     (g, u, out; dy, g, u, dg, du) bf16 [N, 8960]; rope 2 passes x (read +
     write of Q and K + cos/sin reads) bf16 Q [B,12,S,128], K [B,2,S,128].
-    B = --batch, S = --seq, N = B*S; the defaults (4 x 512) are the benchmark
-    shapes, larger batches show the same kernels with the per-launch fixed cost
-    amortised.
+    N = batch * seq; 4 x 512 are the benchmark shapes.
     """
     from auspex_soup_demo_b200.kernels.rmsnorm import rmsnorm_backward, rmsnorm_forward
-    from auspex_soup_demo_b200.kernels.rope import rope_apply
+    from auspex_soup_demo_b200.kernels.rope import rope_apply, rope_tables
     from auspex_soup_demo_b200.kernels.swiglu import swiglu_backward, swiglu_forward
 
-    import oracle
-
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(0)
-    wl = args.workload
     l2 = 126 * 2 ** 20
     if wl == "rmsnorm":
-        N, D = args.batch * args.seq, 1536
+        N, D = batch * seq, 1536
         per_set = 4 * N * D * 4
         nsets = max(2, -(-2 * l2 // per_set))
         w = (1 + 0.1 * torch.randn(D, device=dev, generator=g))
@@ -460,14 +738,14 @@ def run_memory_op(args):
                      y=torch.empty(N, D, device=dev), dx=torch.empty(N, D, device=dev),
                      rstd=torch.empty(N, device=dev)) for _ in range(nsets)]
         algo = 5 * N * D * 4 + 3 * D * 4 + 2 * N * 4
-        launches = 3
 
         def one(s):
             rmsnorm_forward(s["x"], w, 1e-6, out=s["y"], rstd=s["rstd"])
             rmsnorm_backward(s["dy"], s["x"], w, s["rstd"], True, dx=s["dx"])
         shape = f"x [{N},1536] fp32, dw included"
+        dtype = "f32"
     elif wl == "swiglu":
-        N, I = args.batch * args.seq, 8960
+        N, I = batch * seq, INTER
         per_set = 7 * N * I * 2
         nsets = max(2, -(-2 * l2 // per_set))
         sets = [dict(g=torch.randn(N, I, device=dev, generator=g).to(torch.bfloat16),
@@ -477,34 +755,35 @@ def run_memory_op(args):
                      dg=torch.empty(N, I, device=dev, dtype=torch.bfloat16),
                      du=torch.empty(N, I, device=dev, dtype=torch.bfloat16)) for _ in range(nsets)]
         algo = 8 * N * I * 2
-        launches = 2
 
         def one(s):
             swiglu_forward(s["g"], s["u"], out=s["o"])
             swiglu_backward(s["dy"], s["g"], s["u"], dg=s["dg"], du=s["du"])
         shape = f"gate/up [{N},8960] bf16"
+        dtype = "bf16"
     elif wl == "rope":
-        B, S, Hq, Hk, D = args.batch, args.seq, 12, 2, 128
+        B, S, Hq, Hk, D = batch, seq, 12, 2, 128
         qk_bytes = (Hq + Hk) * B * S * D * 2
         per_set = 4 * qk_bytes
         nsets = max(2, -(-2 * l2 // per_set))
-        cos, sin = oracle.rope_cos_sin(S, D, 1e6, torch.bfloat16)
-        cos = cos[None, None].to(dev)
-        sin = sin[None, None].to(dev)
+        cos, sin = rope_tables(S, D, 1e6, torch.bfloat16, dev)
+        cos = cos[None, None]
+        sin = sin[None, None]
         sets = [dict(q=torch.randn(B, Hq, S, D, device=dev, generator=g).to(torch.bfloat16),
                      k=torch.randn(B, Hk, S, D, device=dev, generator=g).to(torch.bfloat16),
                      qo=torch.empty(B, Hq, S, D, device=dev, dtype=torch.bfloat16),
                      ko=torch.empty(B, Hk, S, D, device=dev, dtype=torch.bfloat16))
                 for _ in range(nsets)]
         algo = 2 * (2 * qk_bytes + 2 * S * (D // 2) * 2)
-        launches = 2
 
         def one(s):
             rope_apply(s["q"], s["k"], cos, sin, False, q_out=s["qo"], k_out=s["ko"])
             rope_apply(s["qo"], s["ko"], cos, sin, True, q_out=s["q"], k_out=s["k"])
         shape = f"Q [{B},12,{S},128] + K [{B},2,{S},128] bf16, theta 1e6, fwd + inverse"
+        dtype = "bf16"
     else:
         raise SystemExit(f"unknown workload {wl}")
+    launches_per_step = {"rmsnorm": 3, "swiglu": 2, "rope": 2}[wl]
 
     graph_steps = max(nsets, 16)
     side = torch.cuda.Stream(dev)
@@ -518,12 +797,12 @@ def run_memory_op(args):
     with torch.cuda.graph(graph):
         for i in range(graph_steps):
             one(sets[i % nsets])
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(max(warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    reps = max(1, args.steps)
+    reps = max(1, steps)
     with ClockSampler(dev.index) as clocks:
         e0.record()
         for _ in range(reps):
@@ -533,250 +812,192 @@ def run_memory_op(args):
     ms = e0.elapsed_time(e1) / (reps * graph_steps)
     gbs = algo / (ms * 1e-3) / 1e9
     _, peak_hbm, src = _peaks()
-    line = {"metric": f"{wl} fwd+bwd HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
-            "n_gpus": 1, "steps": reps * graph_steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 5), "higher_is_better": True, "dtype": "bf16" if wl != "rmsnorm" else "f32",
-            "data": "synthetic",
-            "config": {"workload": f"{wl}: {shape}", "buffer_sets": nsets,
-                       "l2": f"rotating {nsets} input sets, {nsets * per_set / 2**20:.0f} MiB > 2x L2",
-                       "timing": f"CUDA graph of {graph_steps} steps, replayed {reps}x"},
-            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak_hbm, "unit": "GB/s",
-                         "frac": round(gbs / peak_hbm, 4), "traffic": None,
-                         "algorithmic_bytes_per_step": algo, "peak_source": f"{src} hbm_gbs"},
-            "gpu_launches": launches * reps * graph_steps, "clocks": clocks.summary()}
-    print(json.dumps(line), flush=True)
+    res = {"metric": f"{wl} fwd+bwd HBM GB/s", "value": round(gbs, 1), "unit": "GB/s",
+           "steps": reps * graph_steps, "ms_per_step": round(ms, 5), "dtype": dtype,
+           "config": {"workload": f"{wl}: {shape}", "buffer_sets": nsets,
+                      "l2": f"rotating {nsets} input sets, {nsets * per_set / 2**20:.0f} MiB > 2x L2",
+                      "timing": f"CUDA graph of {graph_steps} steps, replayed {reps}x"},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak_hbm, "unit": "GB/s",
+                        "frac": round(gbs / peak_hbm, 4),
+                        "traffic": _committed_traffic(f"{wl}_b{batch}_s{seq}"),
+                        "algorithmic_bytes_per_step": algo, "peak_source": f"{src} hbm_gbs"},
+           "launches_per_step": launches_per_step, "clocks": clocks.summary()}
+    del graph, sets
+    _free()
+    return res
 
 
-def kernel_table(step, n_steps, top=40):
-    """Per-kernel device time of `n_steps` calls of `step` (CUPTI through
-    torch.profiler; kernels run back to back as in the timed region), printed to
-    stderr as: ms per step, share, launches per step, kernel name."""
-    import collections
+# ===================================================== vocab-parallel CE ====
+def measure_ce_vp(args, R: Ranks):
+    """Vocab-parallel fused CE: T tokens, W [151936, 1536] bf16 sharded over the ranks.
 
-    from torch.profiler import ProfilerActivity, profile
-
-    torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        for _ in range(n_steps):
-            step()
-        torch.cuda.synchronize()
-    agg = collections.defaultdict(lambda: [0, 0.0])
-    for e in prof.events():
-        if e.device_type == torch.autograd.DeviceType.CUDA:
-            agg[e.name][0] += 1
-            agg[e.name][1] += e.device_time_total
-    total = sum(v[1] for v in agg.values())
-    print(f"kernel time per step {total / n_steps / 1000:.3f} ms", file=sys.stderr)
-    for name, (n, t) in sorted(agg.items(), key=lambda kv: -kv[1][1])[:top]:
-        print(f"{t / n_steps / 1000:8.3f} ms {100 * t / total:5.1f}% {n // n_steps:5d}x  {name[:140]}",
-              file=sys.stderr)
-
-
-def run_qlora(args):
-    """Qwen2.5-1.5B-architecture QLoRA train step: tokens/s (whole job).
-
-    Random-init model (28 layers, NF4 blocksize 64, LoRA r16/a32 on
-    q/k/v/o/gate/up/down), uniform random token ids, AdamW 2e-4, the fused
-    patches installed. One step = forward + backward + optimiser step on
-    `batch` x `seq` tokens per GPU. N > 1: DDP over NCCL, LoRA grads only.
+    Strong scaling: the whole problem (6*T*D*V FLOP per step) is fixed; each rank
+    computes its vocabulary shard for all tokens. Collectives per step: one
+    all-gather of the per-token softmax records and one reduce-scatter of the
+    bf16 partial dhidden (each rank keeps its token block).
     """
-    import torch.distributed as dist
-
-    from auspex_soup_demo_b200 import _lib, apply, qlora
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    apply()
-    if args.no_recompute:
-        from auspex_soup_demo_b200.kernels import swiglu as _swiglu
-        _swiglu.RECOMPUTE = False
-    B, S = args.batch, args.seq
-    model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=args.layers), device=dev,
-                                    seed=0)
-    trainer = qlora.QLoRATrainer(model, lr=2e-4, ddp=world > 1)
-    g = torch.Generator().manual_seed(1234 + rank)
-    ids_cpu = torch.randint(0, 151936, (B, S), generator=g)
-    labels_cpu = qlora.causal_labels(ids_cpu)
-    ids, labels = ids_cpu.to(dev), labels_cpu.to(dev)
-    den = float((labels_cpu != -100).sum())
-    # every rank's batch has the same number of labelled tokens (no padding), so
-    # averaging the per-rank gradients gives the gradient of the global mean loss
-    use_graph = not args.no_graph
-    if use_graph:
-        trainer.capture(ids, labels, den, warmup=max(args.warmup, 3))
-
-    def one_step():
-        return trainer.replay() if use_graph else trainer.step(ids, labels, den)
-
-    for _ in range(max(args.warmup, 3)):
-        one_step()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    stream = torch.cuda.current_stream(dev)
-    with ClockSampler(local) as clocks:
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for _ in range(args.steps):
-            loss, _ = one_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t)
-    tok_s = world * B * S / (ms * 1e-3)
-    # e2e: token ids from pinned host memory each step, loss read back
-    ids_pin = ids_cpu.pin_memory()
-    lab_pin = labels_cpu.pin_memory()
-    out_pin = torch.empty(1, dtype=torch.float32).pin_memory()
-    e2 = torch.cuda.Event(enable_timing=True)
-    e3 = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e2.record(stream)
-    for _ in range(args.steps):
-        ids.copy_(ids_pin, non_blocking=True)
-        labels.copy_(lab_pin, non_blocking=True)
-        loss, _ = one_step()
-        out_pin.copy_(loss.view(1), non_blocking=True)
-    e3.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e2.elapsed_time(e3) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t)
-    assert _lib.device_error(dev) == 0
-    if args.profile and rank == 0:
-        kernel_table(one_step, 2)
-    n_lora = sum(p.numel() for p in qlora.lora_parameters(model))
-    line = {"metric": "QLoRA train tokens/s", "value": round(tok_s, 1), "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids)",
-            "config": {"workload": "Qwen2.5-1.5B-architecture QLoRA step",
-                       "layers": args.layers, "batch_per_gpu": B, "seq_len": S,
-                       "lora": "r16 a32 q/k/v/o/gate/up/down", "lora_params": n_lora,
-                       "base": "NF4 blocksize 64, dequantised per use", "optimizer": "AdamW 2e-4",
-                       "mlp_recompute": not args.no_recompute,
-                       "parallelism": f"dp{world}" + (" (one NCCL allreduce of the flat LoRA grads)"
-                                                      if world > 1 else ""),
-                       "l2": "weights and activations far larger than L2"},
-            "e2e": {"value": round(world * B * S / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": 2 * B * S * 8, "d2h_bytes_per_step": 4,
-                    "ms_per_step": round(e2e_ms, 3)},
-            "final_loss": float(loss), "cuda_graph": use_graph, "clocks": clocks.summary()}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    trainer.release_graph()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def run_ce_vp(args):
-    """Vocab-parallel fused CE: 65536 tokens, W [151936, 1536] bf16 sharded over N GPUs.
-
-    Strong scaling: the whole problem (6*T*D*V = 91.77 TFLOP per step) is fixed;
-    each rank computes its vocabulary shard for all tokens. Collectives per
-    step: all-gather of per-token softmax records, all-reduce of dhidden (fp32).
-    """
-    import torch.distributed as dist
-
     from auspex_soup_demo_b200 import _lib
-    from auspex_soup_demo_b200.kernels.vocab_parallel import shard_range, vocab_parallel_cross_entropy
+    from auspex_soup_demo_b200.kernels.vocab_parallel import (shard_range,
+                                                              vocab_parallel_cross_entropy)
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    dev = R.dev
     T = args.tokens
     g = torch.Generator(device=dev).manual_seed(7)  # same hidden/targets on every rank
     hidden = torch.randn(T, DIM, device=dev, generator=g).to(torch.bfloat16)
     targets = torch.randint(0, VOCAB, (T,), device=dev, generator=g)
     targets[torch.rand(T, device=dev, generator=g) < 0.1] = -100
     den = float((targets != -100).sum())
-    off, size = shard_range(VOCAB, rank, world)
-    gw = torch.Generator(device=dev).manual_seed(1000 + rank)
+    off, size = shard_range(VOCAB, R.rank, R.world)
+    gw = torch.Generator(device=dev).manual_seed(1000 + R.rank)
     w_shard = (0.02 * torch.randn(size, DIM, device=dev, generator=gw)).to(torch.bfloat16)
     ws = torch.empty(_lib.lib().soup_ce_vp_workspace_bytes(T, size, DIM), dtype=torch.uint8,
                      device=dev)
+    stream = torch.cuda.current_stream(dev)
+    timers = {}
 
-    def step():
+    def step(timed=False):
         return vocab_parallel_cross_entropy(hidden, w_shard, off, VOCAB, targets, den,
-                                            workspace=ws)
+                                            workspace=ws, timers=timers if timed else None)
 
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    stream = torch.cuda.current_stream(dev)
-    with ClockSampler(local) as clocks:
-        if world > 1:
-            dist.barrier()
+    with ClockSampler(R.local) as clocks:
+        R.barrier()
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
             out = step()
         e1.record(stream)
         torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t)
+        R.barrier()
+    ms = R.max(e0.elapsed_time(e1) / args.steps)
+    # stage split (extra steps with events between the stages)
+    split = {}
+    for _ in range(3):
+        timers.clear()
+        R.barrier()
+        step(timed=True)
+        torch.cuda.synchronize()
+        for k, (a, b) in timers.items():
+            split.setdefault(k, []).append(a.elapsed_time(b))
+    split = {k: round(R.max(statistics.median(v)), 4) for k, v in sorted(split.items())}
     flop = 6.0 * T * DIM * VOCAB
     assert _lib.device_error(dev) == 0
-    line = {"metric": "vocab-parallel fused-CE TFLOP/s (fwd+bwd)", "value": round(flop / (ms * 1e-3) / 1e12, 2),
-            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"vocab-parallel CE, {T} tokens, W [151936,1536] bf16 "
-                                   f"sharded {world} ways ({size} rows on rank 0)",
-                       "collectives": "all_gather of per-token records + all_reduce(sum) of fp32 dhidden",
-                       "l2": "inputs larger than L2"},
-            "loss": float(out[3][0]) / den, "clocks": clocks.summary()}
-    if rank == 0:
+    res = {"metric": "vocab-parallel fused-CE TFLOP/s (fwd+bwd)",
+           "value": round(flop / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": R.world,
+           "ms_per_step": round(ms, 3), "scaling": "strong",
+           "config": {"workload": f"vocab-parallel CE, {T} tokens, W [151936,1536] bf16 "
+                                  f"sharded {R.world} ways ({size} rows on rank 0)",
+                      "collectives": "all_gather of per-token records + reduce_scatter of the bf16 "
+                                     "partial dhidden (token blocks)",
+                      "l2": "inputs larger than L2"},
+           "stages_ms": split, "loss": float(out[3][0]) / den, "clocks": clocks.summary()}
+    del ws, w_shard, hidden
+    _free()
+    return res
+
+
+# ================================================================== runs ====
+def run_step(args):
+    """The default line: QLoRA step tokens/s with the other measurements nested."""
+    R = Ranks()
+    seq = args.seq or QLORA_SEQ
+    q = measure_qlora(args, R, args.batch, seq, with_extras=True)
+    extras = {}
+    if not args.no_extras:
+        if R.world == 1:
+            s512 = measure_qlora(args, R, 4, 512, with_extras=False)
+            extras["qlora_s512"] = {"metric": METRIC, "value": round(s512["tokens_per_s"], 1),
+                                    "unit": "tokens/s", "ms_per_step": round(s512["ms"], 3),
+                                    "e2e_tokens_per_s": round(4 * 512 / (s512["e2e_ms"] * 1e-3), 1),
+                                    "config": "batch 4 x 512 on 1 GPU (CUDA graph)",
+                                    "clocks": s512["clocks"]}
+        extras["ce"] = measure_ce(args, R)
+        extras["mem_ops"] = {wl: measure_mem_op(wl, 4, 512, args.steps, args.warmup, R.dev)
+                             for wl in ("rmsnorm", "swiglu", "rope")}
+        extras["ce_vp"] = measure_ce_vp(args, R)
+    B = args.batch
+    own = q.get("own_kernels_per_step", 0)
+    line = {
+        "metric": METRIC, "value": round(q["tokens_per_s"], 1), "unit": "tokens/s",
+        "n_gpus": R.world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(q["ms"], 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids)",
+        "config": {"workload": "Qwen2.5-1.5B-architecture QLoRA train step",
+                   "model": "Qwen2.5-1.5B architecture, random init", "layers": args.layers,
+                   "batch_per_gpu": B, "seq_len": seq, "global_batch": B * R.world,
+                   "lora": "r16 a32 q/k/v/o/gate/up/down", "lora_params": q["lora_params"],
+                   "base": "NF4 blocksize 64, dequantised per use", "optimizer": "AdamW 2e-4",
+                   "mlp_recompute": not args.no_recompute,
+                   "parallelism": f"dp{R.world}" + (" (one NCCL all-reduce of the flat fp32 LoRA "
+                                                    "gradient per step)" if R.world > 1 else ""),
+                   "l2": "weights and activations far larger than L2"},
+        "e2e": {"value": round(R.world * B * seq / (q["e2e_ms"] * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": 2 * B * seq * 8, "d2h_bytes_per_step": 4,
+                "ms_per_step": round(q["e2e_ms"], 3),
+                "api": "QLoRATrainer (CUDA graph replay) with ids + labels copied from pinned host "
+                       "memory and the loss read back every step"},
+        "gpu_launches": own * args.steps,
+        "gpu_launches_note": f"{own} launches of this library's kernels per step "
+                             f"({q.get('other_kernels_per_step', 0)} other kernels: cuBLAS, cuDNN "
+                             "attention, PyTorch elementwise, NCCL), counted from a CUPTI trace of "
+                             "one step",
+        "clocks": q["clocks"],
+        "final_loss": q["loss"], "cuda_graph": q["graph"],
+    }
+    dom = q.get("dominant")
+    if dom:
+        line["roofline"] = {"bound": "tensor", "achieved": dom["achieved"], "peak": dom["peak"],
+                            "unit": "TFLOP/s", "frac": dom["frac"], "traffic": dom["traffic"],
+                            "kernel": dom["kernel"], "shape": dom["shape"],
+                            "ms_per_launch": {"fwd": dom["ms_fwd"], "bwd": dom["ms_bwd"]},
+                            "flop_per_launch": dom["flop_per_launch"],
+                            "peak_source": dom["peak_source"]}
+    line["step_mfu"] = q.get("step_mfu")
+    if "allreduce" in q:
+        line["allreduce"] = q["allreduce"]
+    line.update(extras)
+    if R.rank == 0 and R.world == 1 and not args.no_cpu:
+        tok_s, per, n, threads = cpu_step_sample(2, 1, seconds=12.0)
+        line["cpu_baseline"] = {"value": round(tok_s, 3), "unit": "tokens/s", "cores": threads,
+                                "kind": "port", "sample": _cpu_sample_text(per, n)}
+        if "ce" in line:
+            line["ce"]["cpu_baseline"] = ce_cpu_baseline()
+    if R.rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    R.close()
 
 
-def _committed_traffic(kernel):
-    """Mean DRAM bytes per GEMM launch of `kernel` from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "traffic.json")
-    try:
-        with open(path) as f:
-            return json.load(f).get(f"{kernel}_bytes_per_launch")
-    except Exception:
-        return None
-
-
-def ctypes_void_p_array(values):
-    import ctypes
-
-    return (ctypes.c_void_p * len(values))(*values)
+def run_section(args):
+    """One section alone (--workload ...), printed as its own line."""
+    R = Ranks()
+    base = {"n_gpus": R.world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "vs_baseline": None, "data": "synthetic"}
+    if args.workload == "ce":
+        res = measure_ce(args, R)
+        if R.rank == 0 and R.world == 1 and not args.no_cpu:
+            res["cpu_baseline"] = ce_cpu_baseline()
+        res["dtype"] = "bf16"
+    elif args.workload == "qlora":
+        q = measure_qlora(args, R, args.batch, args.seq or QLORA_SEQ, with_extras=True)
+        res = {"metric": METRIC, "value": round(q["tokens_per_s"], 1), "unit": "tokens/s",
+               "ms_per_step": round(q["ms"], 3), "dtype": "bf16", "scaling": "weak",
+               "config": {"workload": "Qwen2.5-1.5B-architecture QLoRA train step",
+                          "layers": args.layers, "batch_per_gpu": args.batch,
+                          "seq_len": args.seq or QLORA_SEQ},
+               **{k: v for k, v in q.items() if k not in ("tokens_per_s", "ms")}}
+    elif args.workload == "ce_vp":
+        res = measure_ce_vp(args, R)
+        res["dtype"] = "bf16"
+    else:
+        res = measure_mem_op(args.workload, args.batch, args.seq or 512, args.steps, args.warmup,
+                             R.dev)
+    if R.rank == 0:
+        print(json.dumps({**base, **res}), flush=True)
+    R.close()
 
 
 def main():
@@ -784,38 +1005,37 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline legs")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="default line: skip the nested ce / mem_ops / ce_vp / qlora_s512 results")
+    ap.add_argument("--workload", default="step",
+                    choices=["step", "qlora", "ce", "rmsnorm", "swiglu", "rope", "ce_vp"],
+                    help="step (default): the QLoRA train step with the other results nested; "
+                         "qlora: the step alone; ce: the fused head CE; rmsnorm/swiglu/rope: one "
+                         "memory-bound op's HBM GB/s; ce_vp: the vocab-parallel CE over all ranks")
     ap.add_argument("--sustained-steps", type=int, default=500,
                     help="ce: extra back-to-back steps timed under the power cap (0: skip)")
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", default="ce",
-                    choices=["ce", "rmsnorm", "swiglu", "rope", "qlora", "ce_vp"],
-                    help="ce (default): the fused head CE; rmsnorm/swiglu/rope: one memory-bound "
-                         "op's HBM GB/s; qlora: the Qwen2.5-1.5B QLoRA train step's tokens/s; "
-                         "ce_vp: the vocab-parallel CE over all ranks")
     ap.add_argument("--tokens", type=int, default=65536, help="ce_vp: tokens per step")
-    ap.add_argument("--batch", type=int, default=4,
-                    help="qlora: sequences per GPU; rmsnorm/swiglu/rope: batch of the op's shape")
-    ap.add_argument("--seq", type=int, default=512,
-                    help="qlora: tokens per sequence; rmsnorm/swiglu/rope: sequence length of the op's shape")
-    ap.add_argument("--layers", type=int, default=28, help="qlora: decoder layers")
-    ap.add_argument("--no-graph", action="store_true", help="qlora: launch eagerly, no CUDA graph")
+    ap.add_argument("--batch", type=int, default=QLORA_BATCH,
+                    help="step/qlora: sequences per GPU; rmsnorm/swiglu/rope: batch of the op's shape")
+    ap.add_argument("--seq", type=int, default=None,
+                    help="step/qlora: tokens per sequence (2048); rmsnorm/swiglu/rope: sequence "
+                         "length of the op's shape (512)")
+    ap.add_argument("--layers", type=int, default=QLORA_LAYERS, help="step/qlora: decoder layers")
+    ap.add_argument("--no-graph", action="store_true", help="step/qlora: launch eagerly, no CUDA graph")
     ap.add_argument("--no-recompute", action="store_true",
-                    help="qlora: keep MLP activations instead of recomputing gate/up in backward")
+                    help="step/qlora: keep MLP activations instead of recomputing gate/up in backward")
     ap.add_argument("--profile", action="store_true",
-                    help="qlora: after the timed region, print a per-kernel device-time table of "
-                         "two steps (torch.profiler, CUDA activity) to stderr")
+                    help="step/qlora: after the timed region, print a per-kernel device-time table "
+                         "of two steps (torch.profiler, CUDA activity) to stderr")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "qlora":
-        run_qlora(args)
-    elif args.workload == "ce_vp":
-        run_ce_vp(args)
-    elif args.workload != "ce":
-        run_memory_op(args)
+    elif args.workload == "step":
+        run_step(args)
     else:
-        run_b200(args)
+        run_section(args)
 
 
 if __name__ == "__main__":

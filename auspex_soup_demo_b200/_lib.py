@@ -51,6 +51,9 @@ _SIGNATURES = {
     "soup_version": (c_int, []),
     "soup_last_error": (ctypes.c_char_p, []),
     "soup_device_error": (c_int, [c_vp, ctypes.POINTER(c_int)]),
+    "soup_set_wait_limit_ns": (c_int, [ctypes.c_uint64]),
+    "soup_gemm_wait_expiry_check": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, ctypes.c_uint64,
+                                            c_vp]),
     "soup_rmsnorm_fwd": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_f, c_int,
                                  c_int, c_vp]),
     "soup_rmsnorm_bwd_workspace_bytes": (c_sz, [c_i64, c_i64]),
@@ -66,18 +69,19 @@ _SIGNATURES = {
     "soup_ce_rows": (c_int, [c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f, c_i64, c_int,
                              c_int, c_vp]),
     "soup_ce_linear_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64]),
-    "soup_ce_linear": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_f, c_i64,
-                               c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_vp, c_sz,
-                               c_vp]),
-    "soup_ce_linear_dweight": (c_int, [c_vp, c_sz, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,
-                                       c_int, c_int, c_vp]),
+    "soup_ce_linear": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_i64, c_vp, c_i64, c_i64,
+                               c_i64, c_f, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_vp, c_int,
+                               c_int, c_vp, c_sz, c_vp]),
+    "soup_ce_linear_dweight": (c_int, [c_vp, c_sz, c_vp, c_i64, c_int, c_i64, c_i64, c_i64, c_vp,
+                                       c_vp, c_int, c_int, c_vp]),
     "soup_ce_vp_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64]),
-    "soup_ce_vp_forward": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp,
-                                   c_vp, c_sz, c_vp]),
+    "soup_ce_vp_forward": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_i64, c_i64, c_i64, c_i64,
+                                   c_vp, c_vp, c_sz, c_vp]),
     "soup_ce_vp_combine": (c_int, [c_vp, c_int, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp,
                                    c_vp, c_vp]),
-    "soup_ce_vp_backward": (c_int, [c_vp, c_sz, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64,
-                                    c_i64, c_vp, c_f, c_i64, c_vp, c_int, c_vp, c_int, c_int, c_vp]),
+    "soup_ce_vp_backward": (c_int, [c_vp, c_sz, c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_i64, c_vp,
+                                    c_i64, c_i64, c_i64, c_i64, c_vp, c_f, c_i64, c_vp, c_int, c_vp,
+                                    c_int, c_int, c_vp]),
     "soup_set_stage_events": (c_int, [ctypes.POINTER(c_vp), c_int]),
     "soup_nf4_quantize": (c_int, [c_vp, c_i64, c_int, c_int, ctypes.POINTER(c_f), c_vp, c_vp, c_vp]),
     "soup_nf4_dequant": (c_int, [c_vp, c_vp, c_i64, c_int, ctypes.POINTER(c_f), c_vp, c_int, c_vp]),

@@ -608,10 +608,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D bf16 map over a row-major matrix [outer, inner] with row stride ld
-// (elements), box {64, box_outer}, 128-byte swizzle, zero fill out of bounds.
+// 2-D map of a 16-bit type (bf16 by default, or fp16) over a row-major matrix
+// [outer, inner] with row stride ld (elements), box {64, box_outer}, 128-byte
+// swizzle, zero fill out of bounds.
 static int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
-                    uint32_t box_outer) {
+                    uint32_t box_outer,
+                    CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   auto fn = encode_fn();
   if (!fn) {
     set_last_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -621,7 +623,7 @@ static int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t 
   cuuint64_t strides[1] = {ld * 2};
   cuuint32_t box[2] = {64, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+  CUresult r = fn(map, dt, 2, const_cast<void*>(ptr), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -662,9 +664,11 @@ static int make_store_map(CUtensorMap* map, const void* ptr, uint64_t inner, uin
 // Operand map: K-major operand stored [rows, K]: box {64 (K), rows_box};
 // MN-major operand stored [K, rows]: box {64 (MN), 64 (K)}.
 static int make_operand_map(CUtensorMap* map, const void* ptr, bool mn_major, int64_t rows, int64_t k,
-                            int64_t ld, int rows_box) {
-  if (mn_major) return make_map(map, ptr, rows, k, ld, 64);
-  return make_map(map, ptr, k, rows, ld, rows_box);
+                            int64_t ld, int rows_box, bool f16 = false) {
+  const CUtensorMapDataType dt =
+      f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (mn_major) return make_map(map, ptr, rows, k, ld, 64, dt);
+  return make_map(map, ptr, k, rows, ld, rows_box, dt);
 }
 
 static bool tma_ok(const void* p, int64_t ld) {
@@ -703,11 +707,14 @@ static int launch_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb, cons
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    if (e != cudaSuccess) return cuda_status(e);
-    attr_set[dev] = true;
+  if (dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lock(cache_mutex());
+    if (!attr_set[dev]) {
+      cudaError_t e =
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+      if (e != cudaSuccess) return cuda_status(e);
+      attr_set[dev] = true;
+    }
   }
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
   const int grid = units < num_sms() ? units : num_sms();
@@ -742,22 +749,28 @@ static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const 
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (max_clusters[dev] == 0) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    if (e != cudaSuccess) return cuda_status(e);
-    int n = 0;
-    cfg.gridDim = dim3(2 * (num_sms() / 2));
-    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-    if (e != cudaSuccess) return cuda_status(e);
-    if (n <= 0) {
-      set_last_error("pair GEMM: no cluster of two CTAs fits on this device");
-      return SOUP_ERR_UNSUPPORTED;
+  const int sms = num_sms();
+  int max_cl = 0;
+  {
+    std::lock_guard<std::mutex> lock(cache_mutex());
+    if (max_clusters[dev] == 0) {
+      cudaError_t e =
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+      if (e != cudaSuccess) return cuda_status(e);
+      int n = 0;
+      cfg.gridDim = dim3(2 * (sms / 2));
+      e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) return cuda_status(e);
+      if (n <= 0) {
+        set_last_error("pair GEMM: no cluster of two CTAs fits on this device");
+        return SOUP_ERR_UNSUPPORTED;
+      }
+      max_clusters[dev] = n;
     }
-    max_clusters[dev] = n;
+    max_cl = max_clusters[dev];
   }
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
-  const int clusters = units < max_clusters[dev] ? units : max_clusters[dev];
+  const int clusters = units < max_cl ? units : max_cl;
   cfg.gridDim = dim3(2 * clusters);
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mb, ma2, mb2, mc, sched, ep, err));
 }
@@ -776,6 +789,7 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
     set_last_error("device error word unavailable");
     return SOUP_ERR_CUDA;
   }
+  if (sched.wait_ns == 0) sched.wait_ns = wait_limit_ns();
   if (use_pairs())
     return launch_gemm_pair<A_MN, B_MN, Epi>(ma, mb, ma2, mb2, mc, sched, ep, stream, err);
   return launch_gemm_single<A_MN, B_MN, Epi>(ma, mb, ma2, mb2, mc, sched, ep, stream, err);
@@ -797,9 +811,11 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
 // entropy, and their gradient factor is 0 later. Any finite value not far
 // below the row maximum works; the logit of one column is a lower bound of
 // that maximum. One warp per row; also clears the overflow flag of this call.
-// Rows are 16-byte aligned with dim % 8 == 0.
-__global__ void __launch_bounds__(256) ce_shift_kernel(const bf16* __restrict__ H, int64_t h_ld,
-                                                       const bf16* __restrict__ W, int64_t w_ld,
+// Rows are 16-byte aligned with dim % 8 == 0. T: the operands' type (bf16 or
+// fp16, as the logits GEMM reads them).
+template <typename T>
+__global__ void __launch_bounds__(256) ce_shift_kernel(const T* __restrict__ H, int64_t h_ld,
+                                                       const T* __restrict__ W, int64_t w_ld,
                                                        const int64_t* __restrict__ targets,
                                                        int rows, int vocab, int dim,
                                                        int64_t vocab_offset, float* __restrict__ shift,
@@ -811,13 +827,13 @@ __global__ void __launch_bounds__(256) ce_shift_kernel(const bf16* __restrict__ 
   const int64_t tg = targets[row];
   const int64_t t = tg - vocab_offset;
   const int64_t j = (t >= 0 && t < vocab) ? t : 0;
-  const bf16* h = H + (int64_t)row * h_ld;
-  const bf16* w = W + j * w_ld;
+  const T* h = H + (int64_t)row * h_ld;
+  const T* w = W + j * w_ld;
   float acc = 0.f;
   for (int k = lane * 8; k < dim; k += 256) {
-    const Vec16<bf16> a = ld16(h + k), b = ld16(w + k);
+    const Vec16<T> a = ld16(h + k), b = ld16(w + k);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc = fmaf(__bfloat162float(a.v[i]), __bfloat162float(b.v[i]), acc);
+    for (int i = 0; i < 8; ++i) acc = fmaf(Cvt<T>::to_f(a.v[i]), Cvt<T>::to_f(b.v[i]), acc);
   }
   acc = warp_sum(acc);
   if (lane == 0) shift[row] = acc + kShiftMargin;
@@ -841,18 +857,19 @@ __global__ void __launch_bounds__(256) ce_shift_kernel(const bf16* __restrict__ 
 constexpr int kStatRows = 8;
 constexpr int kStatBatch = 10;
 constexpr int kStatHidMax = 2048;  // dim up to which the hidden rows are staged in shared memory
+template <typename T>  // the hidden rows' type (bf16 or fp16); hs is bf16
 __global__ void __launch_bounds__(512, 2) ce_stats_kernel(
     const float4* __restrict__ partials, int n_tiles, const float* __restrict__ zt,
     const int64_t* __restrict__ targets, int rows, int vocab, float inv_den, int64_t ignore_index,
     float* __restrict__ losses, float* __restrict__ entropies, int32_t* __restrict__ correct,
     bf16* __restrict__ E, int64_t ld_e, float* __restrict__ shift, float* __restrict__ rscale,
-    const int* __restrict__ flag, const bf16* __restrict__ hidden, int64_t h_ld,
+    const int* __restrict__ flag, const T* __restrict__ hidden, int64_t h_ld,
     bf16* __restrict__ hs, int dim) {
   constexpr int kGroups = 512 / kStatRows;
   __shared__ SoftmaxState part[kGroups][kStatRows + 1];
   __shared__ SoftmaxState part2[8][kStatRows + 1];
   __shared__ float s_scale[kStatRows];
-  __shared__ __align__(16) bf16 hid[kStatRows * kStatHidMax];
+  __shared__ __align__(16) T hid[kStatRows * kStatHidMax];
   const int r0 = blockIdx.x * kStatRows;
   const int lr = threadIdx.x % kStatRows, g = threadIdx.x / kStatRows;
   const int nvec = dim / 8;
@@ -875,7 +892,7 @@ __global__ void __launch_bounds__(512, 2) ce_stats_kernel(
       const int rr = i / nvec;
       if (r0 + rr >= rows) break;  // i only grows
       const int k = (i - rr * nvec) * 8;
-      const bf16* src = hidden + (int64_t)(r0 + rr) * h_ld + k;
+      const T* src = hidden + (int64_t)(r0 + rr) * h_ld + k;
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(hid + rr * dim + k)),
                    "l"(src)
                    : "memory");
@@ -954,29 +971,30 @@ __global__ void __launch_bounds__(512, 2) ce_stats_kernel(
     if (row >= rows) break;  // i only grows
     const int k = (i - rr * nvec) * 8;
     const float sc = s_scale[rr];
-    const Vec16<bf16> a = hid_smem ? *reinterpret_cast<const Vec16<bf16>*>(hid + rr * dim + k)
-                                   : ld16(hidden + (int64_t)row * h_ld + k);
+    const Vec16<T> a = hid_smem ? *reinterpret_cast<const Vec16<T>*>(hid + rr * dim + k)
+                                : ld16(hidden + (int64_t)row * h_ld + k);
     Vec16<bf16> o;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o.v[e] = __float2bfloat16_rn(sc * __bfloat162float(a.v[e]));
+    for (int e = 0; e < 8; ++e) o.v[e] = __float2bfloat16_rn(sc * Cvt<T>::to_f(a.v[e]));
     st16(hs + (int64_t)row * dim + k, o);
   }
 }
 
-// hs[row] = rscale[row] * hidden[row] (bf16), one block per row.
-__global__ void __launch_bounds__(256) ce_scale_rows_kernel(const bf16* __restrict__ hidden,
+// hs[row] = rscale[row] * hidden[row] (bf16; hidden bf16 or fp16), one block per row.
+template <typename T>
+__global__ void __launch_bounds__(256) ce_scale_rows_kernel(const T* __restrict__ hidden,
                                                             int64_t h_ld,
                                                             const float* __restrict__ rscale,
                                                             int dim, bf16* __restrict__ hs) {
   const int row = blockIdx.x;
   const float sc = rscale[row];
-  const bf16* hrow = hidden + (int64_t)row * h_ld;
+  const T* hrow = hidden + (int64_t)row * h_ld;
   bf16* orow = hs + (int64_t)row * dim;
   for (int k = threadIdx.x * 8; k < dim; k += blockDim.x * 8) {
-    const Vec16<bf16> a = ld16(hrow + k);
+    const Vec16<T> a = ld16(hrow + k);
     Vec16<bf16> o;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o.v[i] = __float2bfloat16_rn(sc * __bfloat162float(a.v[i]));
+    for (int i = 0; i < 8; ++i) o.v[i] = __float2bfloat16_rn(sc * Cvt<T>::to_f(a.v[i]));
     st16(orow + k, o);
   }
 }
@@ -1106,11 +1124,13 @@ __global__ void __launch_bounds__(256) ce_combine_kernel(
 // E[t] = (p_t - 1) exp(lse - c) when the target is in the shard, and with hs
 // set hs[row] = s * hidden[row]. When the shard's logits GEMM raised the
 // overflow flag every row takes c = lse and the gated second GEMM rewrites E.
+// T: the hidden rows' type (bf16 or fp16); hs is bf16.
+template <typename T>
 __global__ void __launch_bounds__(256) ce_vp_grad_kernel(
     const float* __restrict__ lse, const float* __restrict__ zt, const int64_t* __restrict__ targets,
     int rows, int vocab_shard, int64_t vocab_offset, float inv_den, int64_t ignore_index,
     bf16* __restrict__ E, int64_t ld_e, float* __restrict__ shift, float* __restrict__ rscale,
-    const int* __restrict__ flag, const bf16* __restrict__ hidden, int64_t h_ld,
+    const int* __restrict__ flag, const T* __restrict__ hidden, int64_t h_ld,
     bf16* __restrict__ hs, int dim) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -1138,13 +1158,13 @@ __global__ void __launch_bounds__(256) ce_vp_grad_kernel(
   }
   if (!hs) return;
   sc = __shfl_sync(0xffffffffu, sc, 0);
-  const bf16* hrow = hidden + (int64_t)row * h_ld;
+  const T* hrow = hidden + (int64_t)row * h_ld;
   bf16* orow = hs + (int64_t)row * dim;
   for (int k = lane * 8; k < dim; k += 256) {
-    const Vec16<bf16> a = ld16(hrow + k);
+    const Vec16<T> a = ld16(hrow + k);
     Vec16<bf16> o;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) o.v[e] = __float2bfloat16_rn(sc * __bfloat162float(a.v[e]));
+    for (int e = 0; e < 8; ++e) o.v[e] = __float2bfloat16_rn(sc * Cvt<T>::to_f(a.v[e]));
     st16(orow + k, o);
   }
 }
@@ -1288,6 +1308,35 @@ static int dweight_gemm(const bf16* L, int64_t ld_logits, const void* hidden, in
   return launch_gemm<true, true, EpiStore<kBN>>(ma, mb, mc, sc, ep, stream);
 }
 
+// Launch helpers shared by the entry points below (operand type T of the
+// hidden rows and the weight: bf16 or fp16).
+template <typename T>
+static int launch_shift(const void* hidden, int64_t h_ld, const void* weight, int64_t w_ld,
+                        const int64_t* targets, int M, int V, int D, int64_t vocab_offset,
+                        float* shift, int* flag, cudaStream_t stream) {
+  ce_shift_kernel<T><<<(M + 7) / 8, 256, 0, stream>>>(
+      static_cast<const T*>(hidden), h_ld, static_cast<const T*>(weight), w_ld, targets, M, V, D,
+      vocab_offset, shift, flag);
+  return launch_status();
+}
+
+static int check_in_dtype(const char* fn, int in_dtype, const void* weight_bwd, bool need_dx) {
+  if (in_dtype != SOUP_BF16 && in_dtype != SOUP_F16) {
+    char msg[160];
+    snprintf(msg, sizeof(msg), "%s: in_dtype must be BF16 or F16", fn);
+    set_last_error(msg);
+    return SOUP_ERR_INVALID;
+  }
+  if (in_dtype == SOUP_F16 && need_dx && !weight_bwd) {
+    char msg[200];
+    snprintf(msg, sizeof(msg),
+             "%s: fp16 operands need weight_bwd, a bf16 copy of the weight for the dX GEMM", fn);
+    set_last_error(msg);
+    return SOUP_ERR_INVALID;
+  }
+  return SOUP_OK;
+}
+
 }  // namespace tc
 }  // namespace soup
 
@@ -1301,25 +1350,34 @@ size_t soup_ce_linear_workspace_bytes(int64_t rows, int64_t vocab, int64_t dim) 
   return ce_layout(rows, vocab, dim).total;
 }
 
-int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t w_ld,
-                   const int64_t* targets, int64_t rows, int64_t vocab, int64_t dim,
-                   float denominator, int64_t ignore_index, float* losses, float* entropies,
-                   int32_t* correct, float* sums, void* dhidden, void* dweight, int dw_dtype,
-                   int accumulate_dw, void* workspace, size_t workspace_bytes, void* stream_) {
+int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t w_ld, int in_dtype,
+                   const void* weight_bwd, int64_t wb_ld, const int64_t* targets, int64_t rows,
+                   int64_t vocab, int64_t dim, float denominator, int64_t ignore_index,
+                   float* losses, float* entropies, int32_t* correct, float* sums, void* dhidden,
+                   int dh_dtype, void* dweight, int dw_dtype, int accumulate_dw, void* workspace,
+                   size_t workspace_bytes, void* stream_) {
   if (!hidden || !weight || !targets || !losses || !entropies || !correct || !workspace) {
     set_last_error("soup_ce_linear: null pointer argument");
     return SOUP_ERR_INVALID;
   }
   if (rows <= 0 || vocab <= 0 || dim <= 0 || rows > (1 << 30) || vocab > (1 << 30) ||
-      h_ld < dim || w_ld < dim) {
+      h_ld < dim || w_ld < dim || (weight_bwd && wb_ld < dim)) {
     set_last_error("soup_ce_linear: bad sizes");
     return SOUP_ERR_INVALID;
   }
-  if (dweight && dw_dtype != SOUP_F32 && dw_dtype != SOUP_BF16) {
-    set_last_error("soup_ce_linear: dweight dtype must be F32 or BF16");
+  if ((dweight && dw_dtype != SOUP_F32 && dw_dtype != SOUP_BF16) ||
+      (dhidden && dh_dtype != SOUP_F32 && dh_dtype != SOUP_BF16)) {
+    set_last_error("soup_ce_linear: dhidden / dweight dtypes must be F32 or BF16");
     return SOUP_ERR_INVALID;
   }
-  if (!tma_ok(hidden, h_ld) || !tma_ok(weight, w_ld) || (dim % 8) != 0) {
+  int rc = check_in_dtype("soup_ce_linear", in_dtype, weight_bwd, dhidden != nullptr);
+  if (rc) return rc;
+  const bool f16 = in_dtype == SOUP_F16;
+  // the dX GEMM multiplies the bf16 exponentials by a bf16 weight
+  const void* wb = f16 ? weight_bwd : weight;
+  const int64_t wbl = f16 ? wb_ld : w_ld;
+  if (!tma_ok(hidden, h_ld) || !tma_ok(weight, w_ld) || (dhidden && !tma_ok(wb, wbl)) ||
+      (dim % 8) != 0) {
     set_last_error("soup_ce_linear: hidden/weight need 16-byte aligned rows and dim % 8 == 0");
     return SOUP_ERR_UNSUPPORTED;
   }
@@ -1341,23 +1399,24 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   const bool need_grad = dhidden || dweight;
   const int M = static_cast<int>(rows), V = static_cast<int>(vocab), D = static_cast<int>(dim);
   const float inv_den = 1.f / (denominator > 0.f ? denominator : 1.f);
-  int rc;
 
   // 0. row shifts of the stored exponentials (gradient only)
   if (need_grad) {
-    ce_shift_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
-        static_cast<const bf16*>(hidden), h_ld, static_cast<const bf16*>(weight), w_ld, targets, M,
-        V, D, 0, shift, flag);
-    if ((rc = launch_status())) return rc;
+    rc = f16 ? launch_shift<__half>(hidden, h_ld, weight, w_ld, targets, M, V, D, 0, shift, flag,
+                                    stream)
+             : launch_shift<bf16>(hidden, h_ld, weight, w_ld, targets, M, V, D, 0, shift, flag,
+                                  stream);
+    if (rc) return rc;
   }
   // 1. logits GEMM + online-softmax epilogue (+ E = exp(z - shift) stored)
   CUtensorMap ma, mb, mc;
   Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
+  sc.ab_f16 = f16 ? 1 : 0;
   EpiCE<kBN>::Params ep{targets, partials, zt, need_grad ? L : nullptr, w.ld_logits, 0, M, V, 0,
                         need_grad ? shift : nullptr, flag, 0, 1, ignore_index};
   {
-    if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
-    if ((rc = make_operand_map(&mb, weight, false, vocab, dim, w_ld, b_box_rows()))) return rc;
+    if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM, f16))) return rc;
+    if ((rc = make_operand_map(&mb, weight, false, vocab, dim, w_ld, b_box_rows(), f16))) return rc;
     mc = ma;
     ep.tma = (need_grad && make_store_map(&mc, L, V, M, w.ld_logits) == SOUP_OK) ? 1 : 0;
     if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, mc, sc, ep, stream))) return rc;
@@ -1365,11 +1424,17 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   }
   // 2. metrics, gradient row factors and target entries (+ hs for dW)
   {
-    ce_stats_kernel<<<(M + kStatRows - 1) / kStatRows, 512, 0, stream>>>(partials, w.n_parts, zt, targets, M, V, inv_den,
-                                            ignore_index, losses, entropies, correct,
-                                            need_grad ? L : nullptr, w.ld_logits, shift, rscale,
-                                            flag, static_cast<const bf16*>(hidden), h_ld,
-                                            dweight ? hs : nullptr, D);
+    const unsigned blocks = (M + kStatRows - 1) / kStatRows;
+    if (f16)
+      ce_stats_kernel<__half><<<blocks, 512, 0, stream>>>(
+          partials, w.n_parts, zt, targets, M, V, inv_den, ignore_index, losses, entropies, correct,
+          need_grad ? L : nullptr, w.ld_logits, shift, rscale, flag,
+          static_cast<const __half*>(hidden), h_ld, dweight ? hs : nullptr, D);
+    else
+      ce_stats_kernel<bf16><<<blocks, 512, 0, stream>>>(
+          partials, w.n_parts, zt, targets, M, V, inv_den, ignore_index, losses, entropies, correct,
+          need_grad ? L : nullptr, w.ld_logits, shift, rscale, flag,
+          static_cast<const bf16*>(hidden), h_ld, dweight ? hs : nullptr, D);
     if ((rc = launch_status())) return rc;
     if (need_grad) {
       // overflow fallback: the same GEMM with shift = lse, run only when the
@@ -1389,7 +1454,7 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
   }
   // 4. dH = diag(s) E W  (split along the vocab)
   if (dhidden) {
-    if ((rc = dx_gemm(L, w.ld_logits, weight, w_ld, M, V, D, w.splits, splitk, dhidden, SOUP_BF16,
+    if ((rc = dx_gemm(L, w.ld_logits, wb, wbl, M, V, D, w.splits, splitk, dhidden, dh_dtype,
                       stream, 3, rscale)))
       return rc;
     mark_stage(4, stream);
@@ -1405,7 +1470,7 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
 }
 
 int soup_ce_linear_dweight(void* workspace, size_t workspace_bytes, const void* hidden,
-                           int64_t h_ld, int64_t rows, int64_t vocab, int64_t dim,
+                           int64_t h_ld, int in_dtype, int64_t rows, int64_t vocab, int64_t dim,
                            const float* grad_scale, void* dweight, int dw_dtype, int accumulate_dw,
                            void* stream) {
   if (!workspace || !hidden || !dweight || rows <= 0 || vocab <= 0 || dim <= 0 ||
@@ -1417,6 +1482,8 @@ int soup_ce_linear_dweight(void* workspace, size_t workspace_bytes, const void* 
     set_last_error("soup_ce_linear_dweight: dweight dtype must be F32 or BF16");
     return SOUP_ERR_INVALID;
   }
+  int rc = check_in_dtype("soup_ce_linear_dweight", in_dtype, nullptr, false);
+  if (rc) return rc;
   if (!tma_ok(hidden, h_ld) || (dim % 8) != 0) {
     set_last_error("soup_ce_linear_dweight: hidden needs 16-byte aligned rows and dim % 8 == 0");
     return SOUP_ERR_UNSUPPORTED;
@@ -1431,9 +1498,13 @@ int soup_ce_linear_dweight(void* workspace, size_t workspace_bytes, const void* 
   const float* rscale = reinterpret_cast<const float*>(ws + w.off_rscale);
   bf16* hs = reinterpret_cast<bf16*>(ws + w.off_hs);
   cudaStream_t st = as_stream(stream);
-  ce_scale_rows_kernel<<<static_cast<unsigned>(rows), 256, 0, st>>>(
-      static_cast<const bf16*>(hidden), h_ld, rscale, static_cast<int>(dim), hs);
-  int rc = launch_status();
+  if (in_dtype == SOUP_F16)
+    ce_scale_rows_kernel<__half><<<static_cast<unsigned>(rows), 256, 0, st>>>(
+        static_cast<const __half*>(hidden), h_ld, rscale, static_cast<int>(dim), hs);
+  else
+    ce_scale_rows_kernel<bf16><<<static_cast<unsigned>(rows), 256, 0, st>>>(
+        static_cast<const bf16*>(hidden), h_ld, rscale, static_cast<int>(dim), hs);
+  rc = launch_status();
   if (rc) return rc;
   return dweight_gemm(L, w.ld_logits, hs, dim, static_cast<int>(rows), static_cast<int>(vocab),
                       static_cast<int>(dim), grad_scale, dweight, dw_dtype, accumulate_dw, st);
@@ -1446,7 +1517,7 @@ size_t soup_ce_vp_workspace_bytes(int64_t rows, int64_t vocab_shard, int64_t dim
 }
 
 int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shard, int64_t w_ld,
-                       const int64_t* targets, int64_t rows, int64_t vocab_shard,
+                       int in_dtype, const int64_t* targets, int64_t rows, int64_t vocab_shard,
                        int64_t vocab_offset, int64_t dim, float* states, void* workspace,
                        size_t workspace_bytes, void* stream_) {
   if (!hidden || !weight_shard || !targets || !states || !workspace || rows <= 0 ||
@@ -1455,6 +1526,8 @@ int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shar
     set_last_error("soup_ce_vp_forward: bad arguments");
     return SOUP_ERR_INVALID;
   }
+  if (int rc0 = check_in_dtype("soup_ce_vp_forward", in_dtype, nullptr, false)) return rc0;
+  const bool f16 = in_dtype == SOUP_F16;
   if (!tma_ok(hidden, h_ld) || !tma_ok(weight_shard, w_ld) || (dim % 8) != 0) {
     set_last_error("soup_ce_vp_forward: hidden/weight need 16-byte aligned rows and dim % 8 == 0");
     return SOUP_ERR_UNSUPPORTED;
@@ -1474,15 +1547,17 @@ int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shar
   const int M = static_cast<int>(rows), V = static_cast<int>(vocab_shard), D = static_cast<int>(dim);
   int rc;
   // row shifts from the shard's own columns
-  ce_shift_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
-      static_cast<const bf16*>(hidden), h_ld, static_cast<const bf16*>(weight_shard), w_ld, targets,
-      M, V, D, vocab_offset, shift, flag);
-  if ((rc = launch_status())) return rc;
+  rc = f16 ? launch_shift<__half>(hidden, h_ld, weight_shard, w_ld, targets, M, V, D, vocab_offset,
+                                  shift, flag, stream)
+           : launch_shift<bf16>(hidden, h_ld, weight_shard, w_ld, targets, M, V, D, vocab_offset,
+                                shift, flag, stream);
+  if (rc) return rc;
   CUtensorMap ma, mb;
-  if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
-  if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, b_box_rows())))
+  if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM, f16))) return rc;
+  if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, b_box_rows(), f16)))
     return rc;
   Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
+  sc.ab_f16 = f16 ? 1 : 0;
   CUtensorMap mc = ma;
   const int tma = make_store_map(&mc, L, V, M, w.ld_logits) == SOUP_OK ? 1 : 0;
   EpiCE<kBN>::Params ep{targets, partials, zt, L, w.ld_logits, vocab_offset, M, V, tma, shift, flag, 0};
@@ -1512,23 +1587,31 @@ int soup_ce_vp_combine(const float* states_all, int nranks, const int64_t* targe
 }
 
 int soup_ce_vp_backward(void* workspace, size_t workspace_bytes, const void* hidden, int64_t h_ld,
-                        const void* weight_shard, int64_t w_ld, const int64_t* targets,
+                        const void* weight_shard, int64_t w_ld, int in_dtype,
+                        const void* weight_shard_bwd, int64_t wb_ld, const int64_t* targets,
                         int64_t rows, int64_t vocab_shard, int64_t vocab_offset, int64_t dim,
                         const float* lse, float denominator, int64_t ignore_index,
                         void* dhidden_partial, int dh_dtype, void* dweight_shard, int dw_dtype,
                         int accumulate_dw, void* stream_) {
   if (!workspace || !hidden || !weight_shard || !targets || !lse || rows <= 0 ||
       vocab_shard <= 0 || dim <= 0 || rows > (1 << 30) || vocab_shard > (1 << 30) ||
-      h_ld < dim || w_ld < dim) {
+      h_ld < dim || w_ld < dim || (weight_shard_bwd && wb_ld < dim)) {
     set_last_error("soup_ce_vp_backward: bad arguments");
     return SOUP_ERR_INVALID;
   }
+  if (int rc0 = check_in_dtype("soup_ce_vp_backward", in_dtype, weight_shard_bwd,
+                               dhidden_partial != nullptr))
+    return rc0;
+  const bool f16 = in_dtype == SOUP_F16;
+  const void* wb = f16 ? weight_shard_bwd : weight_shard;
+  const int64_t wbl = f16 ? wb_ld : w_ld;
   if ((dhidden_partial && dh_dtype != SOUP_F32 && dh_dtype != SOUP_BF16) ||
       (dweight_shard && dw_dtype != SOUP_F32 && dw_dtype != SOUP_BF16)) {
     set_last_error("soup_ce_vp_backward: gradient dtypes must be F32 or BF16");
     return SOUP_ERR_INVALID;
   }
-  if (!tma_ok(hidden, h_ld) || !tma_ok(weight_shard, w_ld) || (dim % 8) != 0) {
+  if (!tma_ok(hidden, h_ld) || !tma_ok(weight_shard, w_ld) ||
+      (dhidden_partial && !tma_ok(wb, wbl)) || (dim % 8) != 0) {
     set_last_error("soup_ce_vp_backward: hidden/weight need 16-byte aligned rows and dim % 8 == 0");
     return SOUP_ERR_UNSUPPORTED;
   }
@@ -1551,17 +1634,23 @@ int soup_ce_vp_backward(void* workspace, size_t workspace_bytes, const void* hid
   const float den = denominator > 0.f ? denominator : 1.f;
   int rc;
   // gradient factors from the global lse (+ s * H for dW)
-  ce_vp_grad_kernel<<<(M + 7) / 8, 256, 0, stream>>>(
-      lse, zt, targets, M, V, vocab_offset, 1.f / den, ignore_index, L, w.ld_logits, shift, rscale,
-      flag, static_cast<const bf16*>(hidden), h_ld, dweight_shard ? hs : nullptr, D);
+  if (f16)
+    ce_vp_grad_kernel<__half><<<(M + 7) / 8, 256, 0, stream>>>(
+        lse, zt, targets, M, V, vocab_offset, 1.f / den, ignore_index, L, w.ld_logits, shift,
+        rscale, flag, static_cast<const __half*>(hidden), h_ld, dweight_shard ? hs : nullptr, D);
+  else
+    ce_vp_grad_kernel<bf16><<<(M + 7) / 8, 256, 0, stream>>>(
+        lse, zt, targets, M, V, vocab_offset, 1.f / den, ignore_index, L, w.ld_logits, shift,
+        rscale, flag, static_cast<const bf16*>(hidden), h_ld, dweight_shard ? hs : nullptr, D);
   if ((rc = launch_status())) return rc;
   // overflow fallback: the shard's logits GEMM again with shift = lse, only when flagged
   {
     CUtensorMap ma, mb;
-    if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM))) return rc;
-    if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, b_box_rows())))
+    if ((rc = make_operand_map(&ma, hidden, false, rows, dim, h_ld, BM, f16))) return rc;
+    if ((rc = make_operand_map(&mb, weight_shard, false, vocab_shard, dim, w_ld, b_box_rows(), f16)))
       return rc;
     Sched sc{m_tiles(M), w.n_vtiles, 1, (D + BK - 1) / BK, 0};
+    sc.ab_f16 = f16 ? 1 : 0;
     sc.gate = flag;
     CUtensorMap mc = ma;
     const int tma = make_store_map(&mc, L, V, M, w.ld_logits) == SOUP_OK ? 1 : 0;
@@ -1570,7 +1659,7 @@ int soup_ce_vp_backward(void* workspace, size_t workspace_bytes, const void* hid
     if ((rc = launch_gemm<false, false, EpiCE<kBN>>(ma, mb, mc, sc, ep, stream))) return rc;
   }
   if (dhidden_partial &&
-      (rc = dx_gemm(L, w.ld_logits, weight_shard, w_ld, M, V, D, w.splits, splitk, dhidden_partial,
+      (rc = dx_gemm(L, w.ld_logits, wb, wbl, M, V, D, w.splits, splitk, dhidden_partial,
                     dh_dtype, stream, -1, rscale)))
     return rc;
   if (dweight_shard)
@@ -1647,6 +1736,29 @@ int soup_gemm_bf16_lora(const void* a, int64_t lda, int a_mn_major, const void* 
   if (!a_mn_major && b_mn_major) return launch_gemm<false, true, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
   if (a_mn_major && !b_mn_major) return launch_gemm<true, false, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
   return launch_gemm<true, true, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
+}
+
+int soup_gemm_wait_expiry_check(const void* a, const void* b, void* c, int64_t m, int64_t n,
+                                int64_t k, uint64_t wait_ns, void* stream_) {
+  if (!a || !b || !c || m <= 0 || n <= 0 || k < 2 * BK || m > (1 << 20) || n > (1 << 20) ||
+      k > (1 << 20) || wait_ns < 1000000ull || wait_ns > kWaitNs) {
+    set_last_error("soup_gemm_wait_expiry_check: bad arguments (k >= 128, 1 ms <= wait <= 2 s)");
+    return SOUP_ERR_INVALID;
+  }
+  if (!tma_ok(a, k) || !tma_ok(b, k) || !aligned16(c) || (n * 2) % 16 != 0) {
+    set_last_error("soup_gemm_wait_expiry_check: operands need 16-byte aligned rows");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_operand_map(&ma, a, false, m, k, k, BM))) return rc;
+  if ((rc = make_operand_map(&mb, b, false, n, k, k, b_box_rows()))) return rc;
+  EpiStore<kBN>::Params ep{c, n, 0, nullptr, 1.f, 1, 0, 1, (int)m, (int)n};
+  const int mt = m_tiles(m), nt = (int)((n + kBN - 1) / kBN);
+  Sched sc{mt, nt, 1, (int)((k + BK - 1) / BK), nt > mt ? 0 : 1, 0};
+  sc.wait_ns = wait_ns;
+  sc.withhold = 1;  // the second k-block of every worker's first tile
+  return launch_gemm<false, false, EpiStore<kBN>>(ma, mb, ma, mb, ma, sc, ep, as_stream(stream_));
 }
 
 int soup_gemm_bf16_lora_swiglu(const void* a, int64_t lda, const void* b, int64_t ldb,

@@ -398,6 +398,7 @@ int ctas_per_sm(K kernel, int threads, size_t smem) {
   static int used = 0;
   int dev = 0;
   cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(cache_mutex());
   for (int i = 0; i < used; ++i)
     if (cache[i].k == (const void*)kernel && cache[i].threads == threads && cache[i].smem == smem &&
         cache[i].dev == dev)
@@ -615,8 +616,11 @@ constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB
 __device__ __align__(256) float g_rms_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
 // Device address of the array, looked up once per device with that device
-// current. In host code the array's name is only a host-side stand-in, so the
-// kernels must receive this address instead.
+// current (under the library's cache lock, so concurrent first calls from
+// several host threads are safe). In host code the array's name is only a
+// host-side stand-in, so the kernels must receive this address instead. The
+// cached address is not refreshed after cudaDeviceReset: a process that resets
+// a device must not call this entry point on it again.
 float* noalloc_scratch(int* status) {
   static float* addr[64] = {nullptr};
   int dev = 0;
@@ -630,6 +634,7 @@ float* noalloc_scratch(int* status) {
     *status = SOUP_ERR_UNSUPPORTED;
     return nullptr;
   }
+  std::lock_guard<std::mutex> lock(cache_mutex());
   if (!addr[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_rms_noalloc_scratch);

@@ -1,21 +1,34 @@
-// Library-wide state: last error text, SM count, the device error word.
+// Library-wide state: last error text, SM count, the device error word, the
+// wait limit of the GEMM kernels, and the lock of the per-device caches.
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "soup_common.cuh"
 
 namespace soup {
 
+std::mutex& cache_mutex() {
+  static std::mutex mu;
+  return mu;
+}
+
 // Written by bounded waits that expire inside the GEMM kernels (0 = none).
 // Kernels receive its address as an argument (see device_err_ptr).
 __device__ int g_device_err = 0;
+// soup_device_error's read-and-clear writes the old value here.
+__device__ int g_device_err_read = 0;
 
+// Per-device addresses, filled once per device with that device current. They
+// are not refreshed after cudaDeviceReset (the library assumes the contexts it
+// has seen stay alive for the process).
 int* device_err_ptr() {
   static int* cached[64] = {nullptr};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(cache_mutex());
   if (!cached[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_err) != cudaSuccess) return nullptr;
@@ -23,6 +36,16 @@ int* device_err_ptr() {
   }
   return cached[dev];
 }
+
+static std::atomic<unsigned long long> g_wait_limit_ns{0};
+
+uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }
+
+namespace {
+// One thread takes the error word and clears it in the same atomic step, so a
+// code written meanwhile by a kernel on another stream is not lost.
+__global__ void take_device_error_kernel() { g_device_err_read = atomicExch(&g_device_err, 0); }
+}  // namespace
 
 static thread_local char g_last_error[512] = "";
 
@@ -42,6 +65,7 @@ int num_sms() {
   static int cached[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(cache_mutex());
   if (cached[dev] == 0) {
     int n = 0;
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
@@ -61,20 +85,27 @@ const char* soup_last_error(void) { return soup::g_last_error; }
 
 int soup_device_error(void* stream, int* out_code) {
   if (!out_code) return SOUP_ERR_INVALID;
-  int v = 0;
   cudaStream_t s = soup::as_stream(stream);
-  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, soup::g_device_err, sizeof(int), 0,
-                                            cudaMemcpyDeviceToHost, s);
+  // host callers are serialised too: the read-back slot is shared per device
+  std::lock_guard<std::mutex> lock(soup::cache_mutex());
+  soup::take_device_error_kernel<<<1, 1, 0, s>>>();
+  cudaError_t e = cudaGetLastError();
+  int v = 0;
+  if (e == cudaSuccess)
+    e = cudaMemcpyFromSymbolAsync(&v, soup::g_device_err_read, sizeof(int), 0,
+                                  cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) return soup::cuda_status(e);
   *out_code = v;
-  if (v != 0) {
-    int zero = 0;
-    e = cudaMemcpyToSymbolAsync(soup::g_device_err, &zero, sizeof(int), 0,
-                                cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) return soup::cuda_status(e);
+  return SOUP_OK;
+}
+
+int soup_set_wait_limit_ns(uint64_t ns) {
+  if (ns != 0 && ns < 1000000ull) {
+    soup::set_last_error("soup_set_wait_limit_ns: the limit must be 0 (default, 2 s) or >= 1 ms");
+    return SOUP_ERR_INVALID;
   }
+  soup::g_wait_limit_ns.store(ns, std::memory_order_relaxed);
   return SOUP_OK;
 }
 

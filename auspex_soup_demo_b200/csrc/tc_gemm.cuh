@@ -156,7 +156,8 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
                    bar)
                : "memory");
 }
-// D(tmem) (+)= A(smem desc) * B(smem desc), kind::f16 (bf16 in, fp32 acc).
+// D(tmem) (+)= A(smem desc) * B(smem desc), kind::f16 (bf16 or fp16 in, as the
+// instruction descriptor says; fp32 accumulate).
 __device__ __forceinline__ void tc_mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                             uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -200,7 +201,8 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo,
   return d;
 }
 
-// Instruction descriptor: fp32 accumulate, bf16 A and B, M=bm, N=bn.
+// Instruction descriptor: fp32 accumulate, bf16 A and B, M=bm, N=bn (bits 7-9
+// and 10-12 are the A / B formats: 1 bf16, 0 fp16; see Sched::idesc).
 __host__ __device__ constexpr uint32_t idesc_bf16(int bn, bool a_mn, bool b_mn, int bm = BM) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
          ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
@@ -223,6 +225,19 @@ struct Sched {
   // 1: k splits run last-first (the first wave reads the end of K, e.g. what
   // the previous GEMM over the same operand left in L2)
   int rev_split = 0;
+  // limit of every mbarrier wait in ns (0: kWaitNs)
+  uint64_t wait_ns = 0;
+  // diagnostic only (soup_gemm_wait_expiry_check): the producer skips the copies
+  // and the expected-bytes arrive of its k-block iteration `withhold` (>= 0), so
+  // the MMA issuer's wait for that stage expires; -1 in every normal launch
+  int withhold = -1;
+  // 1: A and B are fp16 (kind::f16 with the f16 operand format) instead of bf16
+  int ab_f16 = 0;
+  __device__ __forceinline__ uint64_t limit() const { return wait_ns ? wait_ns : kWaitNs; }
+  // the instruction descriptor with the operand format of this launch
+  __device__ __forceinline__ uint32_t idesc(uint32_t bf16_desc) const {
+    return ab_f16 ? (bf16_desc & ~((7u << 7) | (7u << 10))) : bf16_desc;
+  }
   // maps and k offset of block kb
   __device__ __forceinline__ bool second(int kb) const { return kb >= kb_total - kb2; }
   __device__ __forceinline__ int k_elem(int kb) const {
@@ -276,7 +291,8 @@ struct SmemLayout {
 // elsewhere); on a local timeout it records `code` and raises the flag.
 template <bool CLUSTER = false>
 __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity,
-                                             volatile int* abort_flag, int* err, int code) {
+                                             volatile int* abort_flag, int* err, int code,
+                                             uint64_t limit_ns) {
   auto try_wait = [&]() {
     return CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
   };
@@ -285,7 +301,7 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity,
   while (true) {
     if (try_wait()) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicCAS(err, 0, code);
       return false;
@@ -368,6 +384,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int n_units = sched.units();
+  const uint64_t wait_ns = sched.limit();
+  const uint32_t idesc = sched.idesc(kIdesc);
   pdl_wait();  // no thread touches global memory before this (see gemm_pair_kernel)
 
   if (warp == 0) {
@@ -382,10 +400,11 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
-          if (!bounded_wait(empty_bar(s), ph ^ 1u, abort_flag, err, kErrWaitProducer)) {
+          if (!bounded_wait(empty_bar(s), ph ^ 1u, abort_flag, err, kErrWaitProducer, wait_ns)) {
             ok = false;
             break;
           }
+          if (static_cast<int>(it) == sched.withhold) continue;  // diagnostic launch only
           const uint32_t a_dst = sbase + s * L::kStageBytes;
           const uint32_t b_dst = a_dst + L::kABytes;
           mbar_arrive_expect_tx(full_bar(s), L::kStageBytes);
@@ -417,7 +436,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
           uint32_t j = it - i;
           uint32_t bar = full_bar(j % STAGES), ph = (j / STAGES) & 1u;
           uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(bar, ph) && globaltimer() - t0 < kWaitNs) {
+          while (!mbar_try_wait(bar, ph) && globaltimer() - t0 < wait_ns) {
           }
         }
       }
@@ -433,7 +452,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
         sched.k_range(ks, kb0, kb1);
         const uint32_t acc = lt & 1u;
         const uint32_t acc_ph = (lt >> 1) & 1u;
-        if (!bounded_wait(tempty_bar(acc), acc_ph ^ 1u, abort_flag, err, kErrWaitMma)) {
+        if (!bounded_wait(tempty_bar(acc), acc_ph ^ 1u, abort_flag, err, kErrWaitMma, wait_ns)) {
           ok = false;
           break;
         }
@@ -442,7 +461,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
-          if (!bounded_wait(full_bar(s), ph, abort_flag, err, kErrWaitMma)) {
+          if (!bounded_wait(full_bar(s), ph, abort_flag, err, kErrWaitMma, wait_ns)) {
             ok = false;
             break;
           }
@@ -456,7 +475,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
             else ad = smem_desc_sw128(a_addr + k * 32, 16, 1024);
             if (B_MN) bd = smem_desc_sw128(b_addr + k * 2048, 8192, 1024);
             else bd = smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            tc_mma_bf16(tmem_d, ad, bd, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            tc_mma_bf16(tmem_d, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           tc_commit(empty_bar(s));  // frees the stage once these MMAs finish
         }
@@ -466,7 +485,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       if (!ok) {
         tc_commit(drain_bar);
         uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(drain_bar, 0) && globaltimer() - t0 < kWaitNs) {
+        while (!mbar_try_wait(drain_bar, 0) && globaltimer() - t0 < wait_ns) {
         }
       }
     }
@@ -487,7 +506,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       const uint32_t acc = lt & 1u;
       const uint32_t acc_ph = (lt >> 1) & 1u;
       bool ok = true;
-      if (lane == 0) ok = bounded_wait(tfull_bar(acc), acc_ph, abort_flag, err, kErrWaitEpilogue);
+      if (lane == 0) ok = bounded_wait(tfull_bar(acc), acc_ph, abort_flag, err, kErrWaitEpilogue, wait_ns);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
       tc_fence_after();
@@ -660,6 +679,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int n_units = sched.units();
+  const uint64_t wait_ns = sched.limit();
+  const uint32_t idesc = sched.idesc(kIdesc);
   // Launched with programmatic dependent launch: the prologue above (barriers,
   // TMEM, descriptor prefetch) may overlap the previous kernel; no thread
   // touches global memory before this wait.
@@ -679,10 +700,11 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
-          if (!bounded_wait(empty_bar(s), ph ^ 1u, abort_flag, err, kErrWaitProducer)) {
+          if (!bounded_wait(empty_bar(s), ph ^ 1u, abort_flag, err, kErrWaitProducer, wait_ns)) {
             ok = false;
             break;
           }
+          if (static_cast<int>(it) == sched.withhold) continue;  // diagnostic launch only
           const uint32_t a_dst = sbase + s * L::kStageBytes;
           const uint32_t b_dst = a_dst + L::kABytes;
           const uint32_t fb = cluster_addr(full_bar(s), 0);
@@ -715,7 +737,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
           uint32_t j = it - i;
           uint32_t bar = full_bar(j % STAGES), ph = (j / STAGES) & 1u;
           uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(bar, ph) && globaltimer() - t0 < kWaitNs) {
+          while (!mbar_try_wait(bar, ph) && globaltimer() - t0 < wait_ns) {
           }
         }
       }
@@ -732,7 +754,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
         sched.k_range(ks, kb0, kb1);
         const uint32_t acc = lt & 1u;
         const uint32_t acc_ph = (lt >> 1) & 1u;
-        if (!bounded_wait<true>(tempty_bar(acc), acc_ph ^ 1u, abort_flag, err, kErrWaitMma)) {
+        if (!bounded_wait<true>(tempty_bar(acc), acc_ph ^ 1u, abort_flag, err, kErrWaitMma, wait_ns)) {
           ok = false;
           break;
         }
@@ -741,7 +763,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
-          if (!bounded_wait<true>(full_bar(s), ph, abort_flag, err, kErrWaitMma)) {
+          if (!bounded_wait<true>(full_bar(s), ph, abort_flag, err, kErrWaitMma, wait_ns)) {
             ok = false;
             break;
           }
@@ -755,7 +777,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
             else ad = smem_desc_sw128(a_addr + k * 32, 16, 1024);
             if (B_MN) bd = smem_desc_sw128(b_addr + k * 2048, 8192, 1024);
             else bd = smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            tc_mma_bf16_pair(tmem_d, ad, bd, kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            tc_mma_bf16_pair(tmem_d, ad, bd, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           issued = true;
           // stage s of both CTAs is free once these MMAs finish
@@ -767,7 +789,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       if (!ok && issued) {
         tc_commit_pair(cluster_addr(drain_bar, 0));
         uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(drain_bar, 0) && globaltimer() - t0 < kWaitNs) {
+        while (!mbar_try_wait(drain_bar, 0) && globaltimer() - t0 < wait_ns) {
         }
       }
     }
@@ -789,7 +811,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       const uint32_t acc = lt & 1u;
       const uint32_t acc_ph = (lt >> 1) & 1u;
       bool ok = true;
-      if (lane == 0) ok = bounded_wait(tfull_bar(acc), acc_ph, abort_flag, err, kErrWaitEpilogue);
+      if (lane == 0) ok = bounded_wait(tfull_bar(acc), acc_ph, abort_flag, err, kErrWaitEpilogue, wait_ns);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
       tc_fence_after();

@@ -14,8 +14,10 @@ re-streaming the 467 MB lm_head twice per chunk. Here all tokens of a call go
 through one ``soup_ce_linear`` launch sequence (tcgen05 logits GEMM with the
 online-softmax epilogue storing row-shifted exponentials exp(z - c), a per-row
 statistics pass, split-K dX GEMM with the per-row gradient factor applied in
-its reduce, dW GEMM) in bf16 with fp32 accumulation and fp32 metrics; no pass
-rewrites the [rows, vocab] buffer between the GEMMs. ``chunk``
+its reduce, dW GEMM) with fp32 accumulation and fp32 metrics; no pass
+rewrites the [rows, vocab] buffer between the GEMMs. bf16 activations with a
+bf16 head are multiplied as they are; other dtypes enter the logits GEMM as
+fp16, as in the reference (see :func:`ce_operands`). ``chunk``
 stays in the signature; token rows are processed in blocks sized by
 ``CE_WORKSPACE_BYTES`` instead, which bounds the logits buffer the way
 ``chunk`` bounds it in the reference. With a trainable head the lm_head
@@ -38,7 +40,8 @@ IGNORE_INDEX = -100
 #: are processed in blocks that fit. 0 selects all rows at once.
 CE_WORKSPACE_BYTES = 8 << 30
 
-_BF16_CACHE = {"key": None, "tensor": None}
+# dtype -> (key of the weight it was cast from, cast copy); one entry per dtype
+_HEAD_CACHE = {}
 
 
 def _extract_head_weight(head: Any) -> Optional[torch.Tensor]:
@@ -83,16 +86,41 @@ def _tma_rows_ok(t: torch.Tensor) -> bool:
             and t.data_ptr() % 16 == 0)
 
 
-def _bf16_weight(weight: torch.Tensor) -> torch.Tensor:
-    """bf16 view of the head weight; a cast copy is cached while unchanged."""
+def _cached_cast(weight: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """The head weight in `dtype`: the tensor itself when it already is (with
+    TMA-ready rows), else a cast copy kept while the weight is unchanged (the
+    reference keeps its fp16 copy the same way, ``chunked_ce.py:170-180``)."""
     w = weight.detach()
-    if w.dtype == torch.bfloat16 and _tma_rows_ok(w):
+    if w.dtype == dtype and _tma_rows_ok(w):
         return w
     key = (id(weight), weight._version, weight.data_ptr(), weight.dtype)
-    if _BF16_CACHE["key"] != key:
-        _BF16_CACHE["tensor"] = w.to(torch.bfloat16).contiguous()
-        _BF16_CACHE["key"] = key
-    return _BF16_CACHE["tensor"]
+    ent = _HEAD_CACHE.get(dtype)
+    if ent is None or ent[0] != key:
+        ent = (key, w.to(dtype).contiguous())
+        _HEAD_CACHE[dtype] = ent
+    return ent[1]
+
+
+def ce_operands(hidden2d: torch.Tensor, weight: torch.Tensor, need_dx: bool):
+    """``(h, w, w_bwd, in_dtype)`` for the fused CE entry points.
+
+    bf16 hidden rows with a bf16 weight are used as they are. Anything else goes
+    through the logits GEMM as fp16 operands, the reference's own arithmetic
+    (``chunked_ce.py:196-199`` rounds the chunk and a cached copy of W to fp16):
+    the rows rounded to fp16 and a cached fp16 copy of W, plus a cached bf16 copy
+    of W for the dX GEMM (the logits' gradient is kept in bf16).
+    """
+    if hidden2d.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16:
+        h = hidden2d.detach()
+        if not _tma_rows_ok(h):
+            h = h.contiguous()
+        return h, _cached_cast(weight, torch.bfloat16), None, _lib.BF16
+    h = hidden2d.detach()
+    if h.dtype != torch.float16 or not _tma_rows_ok(h):
+        h = h.to(torch.float16).contiguous()
+    w = _cached_cast(weight, torch.float16)
+    wb = _cached_cast(weight, torch.bfloat16) if need_dx else None
+    return h, w, wb, _lib.F16
 
 
 def _rows_per_block(rows: int, vocab: int, dim: int, budget: int) -> int:
@@ -111,21 +139,23 @@ def fused_linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, targe
                                denominator: float = 1.0, ignore_index: int = IGNORE_INDEX,
                                with_grad: bool = True, compute_dw: bool = False,
                                dw_dtype: torch.dtype = torch.float32,
-                               workspace_bytes: Optional[int] = None):
+                               workspace_bytes: Optional[int] = None,
+                               dh_dtype: Optional[torch.dtype] = None):
     """Tensor-level fused head CE over hidden [N, D] and weight [V, D].
 
     Returns ``(losses [N] f32, entropies [N] f32, correct [N] i32, sums [2] f32
-    = (sum loss, hits), dhidden [N, D] bf16 | None, dW [V, D] | None)``.
-    Gradients are scaled by 1/denominator (denominator <= 0 counts as 1).
+    = (sum loss, hits), dhidden [N, D] | None, dW [V, D] | None)``. dhidden is
+    ``dh_dtype`` (bf16 or fp32; default bf16 for bf16 hidden states, fp32
+    otherwise). Operands: see :func:`ce_operands`. Gradients are scaled by
+    1/denominator (denominator <= 0 counts as 1).
     """
     if not hidden.is_cuda:
         raise RuntimeError("fused_linear_cross_entropy needs CUDA tensors")
     n, d = hidden.shape
     v = weight.shape[0]
-    h = hidden.detach()
-    if h.dtype != torch.bfloat16 or not _tma_rows_ok(h):
-        h = h.to(torch.bfloat16).contiguous()
-    w = _bf16_weight(weight)
+    if dh_dtype is None:
+        dh_dtype = torch.bfloat16 if hidden.dtype == torch.bfloat16 else torch.float32
+    h, w, wb, in_dt = ce_operands(hidden, weight, with_grad)
     t = targets.reshape(-1)
     if t.dtype != torch.int64 or not t.is_contiguous():
         t = t.to(torch.int64).contiguous()
@@ -133,7 +163,7 @@ def fused_linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, targe
     losses = torch.empty(n, dtype=torch.float32, device=dev)
     ents = torch.empty(n, dtype=torch.float32, device=dev)
     corr = torch.empty(n, dtype=torch.int32, device=dev)
-    dh = torch.empty(n, d, dtype=torch.bfloat16, device=dev) if with_grad else None
+    dh = torch.empty(n, d, dtype=dh_dtype, device=dev) if with_grad else None
     dw = torch.empty(v, d, dtype=dw_dtype, device=dev) if (with_grad and compute_dw) else None
     budget = CE_WORKSPACE_BYTES if workspace_bytes is None else workspace_bytes
     rb = _rows_per_block(n, v, d, budget)
@@ -147,9 +177,10 @@ def fused_linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, targe
         ws_bytes = lib.soup_ce_linear_workspace_bytes(r, v, d)
         ws = _lib.scratch(dev, ws_bytes)
         _lib.call("soup_ce_linear", dev, h[r0].data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
-                  t[r0:].data_ptr(), r, v, d, float(denominator), int(ignore_index),
-                  losses[r0:].data_ptr(), ents[r0:].data_ptr(), corr[r0:].data_ptr(),
-                  sums[b].data_ptr(), _lib.ptr(dh[r0] if dh is not None else None),
+                  in_dt, _lib.ptr(wb), wb.stride(0) if wb is not None else 0, t[r0:].data_ptr(), r,
+                  v, d, float(denominator), int(ignore_index), losses[r0:].data_ptr(),
+                  ents[r0:].data_ptr(), corr[r0:].data_ptr(), sums[b].data_ptr(),
+                  _lib.ptr(dh[r0] if dh is not None else None), _lib.dtype_code(dh_dtype),
                   _lib.ptr(dw), _lib.dtype_code(dw_dtype), 1 if b > 0 else 0, ws.data_ptr(),
                   ws_bytes, stream)
     total = sums.sum(0) if nblk > 1 else sums[0]
@@ -157,18 +188,18 @@ def fused_linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, targe
 
 
 def _fused_forward_keep_grad_state(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
-                                denominator: float, ignore_index: int):
+                                denominator: float, ignore_index: int,
+                                dh_dtype: Optional[torch.dtype] = None):
     """Forward + dhidden in one pass, leaving the gradient state in a workspace owned by the caller.
 
     Returns ``(losses, ents, corr, sums, dh, state)`` where ``state`` holds the
-    workspace and the bf16 hidden rows needed by :func:`_dweight_from_state`.
+    workspace and the operand-typed hidden rows needed by :func:`_dweight_from_state`.
     """
     n, d = hidden.shape
     v = weight.shape[0]
-    h = hidden.detach()
-    if h.dtype != torch.bfloat16 or not _tma_rows_ok(h):
-        h = h.to(torch.bfloat16).contiguous()
-    w = _bf16_weight(weight)
+    if dh_dtype is None:
+        dh_dtype = torch.bfloat16 if hidden.dtype == torch.bfloat16 else torch.float32
+    h, w, wb, in_dt = ce_operands(hidden, weight, True)
     t = targets.reshape(-1)
     if t.dtype != torch.int64 or not t.is_contiguous():
         t = t.to(torch.int64).contiguous()
@@ -180,12 +211,14 @@ def _fused_forward_keep_grad_state(hidden: torch.Tensor, weight: torch.Tensor, t
     ents = torch.empty(n, dtype=torch.float32, device=dev)
     corr = torch.empty(n, dtype=torch.int32, device=dev)
     sums = torch.empty(2, dtype=torch.float32, device=dev)
-    dh = torch.empty(n, d, dtype=torch.bfloat16, device=dev)
-    _lib.call("soup_ce_linear", dev, h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
-              t.data_ptr(), n, v, d, float(denominator), int(ignore_index), losses.data_ptr(),
-              ents.data_ptr(), corr.data_ptr(), sums.data_ptr(), dh.data_ptr(), 0, _lib.F32, 0,
-              ws.data_ptr(), ws_bytes, _lib.stream_of(hidden))
-    return losses, ents, corr, sums, dh, {"ws": ws, "h": h, "rows": n, "vocab": v, "dim": d}
+    dh = torch.empty(n, d, dtype=dh_dtype, device=dev)
+    _lib.call("soup_ce_linear", dev, h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0), in_dt,
+              _lib.ptr(wb), wb.stride(0) if wb is not None else 0, t.data_ptr(), n, v, d,
+              float(denominator), int(ignore_index), losses.data_ptr(), ents.data_ptr(),
+              corr.data_ptr(), sums.data_ptr(), dh.data_ptr(), _lib.dtype_code(dh_dtype), 0,
+              _lib.F32, 0, ws.data_ptr(), ws_bytes, _lib.stream_of(hidden))
+    return losses, ents, corr, sums, dh, {"ws": ws, "h": h, "in_dtype": in_dt, "rows": n,
+                                          "vocab": v, "dim": d}
 
 
 def _dweight_from_state(state, weight: torch.Tensor, grad_scale: torch.Tensor) -> None:
@@ -199,16 +232,17 @@ def _dweight_from_state(state, weight: torch.Tensor, grad_scale: torch.Tensor) -
             target = torch.empty_like(weight)
             accumulate = 0
         _lib.call("soup_ce_linear_dweight", dev, state["ws"].data_ptr(), state["ws"].numel(),
-                  state["h"].data_ptr(), state["h"].stride(0), state["rows"], state["vocab"],
-                  state["dim"], scale.data_ptr(), target.data_ptr(), _lib.dtype_code(weight.dtype),
-                  accumulate, _lib.stream_of(weight))
+                  state["h"].data_ptr(), state["h"].stride(0), state["in_dtype"], state["rows"],
+                  state["vocab"], state["dim"], scale.data_ptr(), target.data_ptr(),
+                  _lib.dtype_code(weight.dtype), accumulate, _lib.stream_of(weight))
         if weight.grad is None:
             weight.grad = target
         return
     tmp = torch.empty(weight.shape, dtype=torch.float32, device=dev)
     _lib.call("soup_ce_linear_dweight", dev, state["ws"].data_ptr(), state["ws"].numel(),
-              state["h"].data_ptr(), state["h"].stride(0), state["rows"], state["vocab"],
-              state["dim"], scale.data_ptr(), tmp.data_ptr(), _lib.F32, 0, _lib.stream_of(weight))
+              state["h"].data_ptr(), state["h"].stride(0), state["in_dtype"], state["rows"],
+              state["vocab"], state["dim"], scale.data_ptr(), tmp.data_ptr(), _lib.F32, 0,
+              _lib.stream_of(weight))
     g = tmp.to(weight.dtype)
     weight.grad = g if weight.grad is None else weight.grad.add_(g)
 
@@ -220,17 +254,23 @@ def chunk_cross_entropy_triton(head: Any, piece: torch.Tensor, target: torch.Ten
                                           Optional[torch.Tensor]]:
     """CE loss, metrics and input gradient of one chunk (reference ``chunked_ce.py:183-264``).
 
-    Returns ``(total_loss, entropy, token_loss, hits, piece_grad)`` with
-    entropy/token_loss shaped ``piece.shape[:-1]``.
+    Returns ``(total_loss, entropy, token_loss, hits, piece_grad)`` as the
+    reference does: total_loss the fp32 sum of the per-token losses (not
+    divided by the denominator), entropy/token_loss fp32 shaped
+    ``piece.shape[:-1]``, hits an int64 count, and piece_grad (None without
+    gradient) the input gradient ``(softmax - onehot) / denominator @ W`` in
+    fp16 like the reference's fp16 GEMM result (``chunked_ce.py:246-249``),
+    here rounded once from fp32.
     """
     weight = _extract_head_weight(head)
     shape = piece.shape
     if weight is not None and piece.is_cuda:
         flat = piece.reshape(-1, shape[-1])
         losses, ents, corr, sums, dh, _ = fused_linear_cross_entropy(
-            flat, weight, target.reshape(-1), denominator, ignore_index, with_grad)
+            flat, weight, target.reshape(-1), denominator, ignore_index, with_grad,
+            dh_dtype=torch.float32)
         hits = corr.sum()
-        grad = dh.view(shape) if dh is not None else None
+        grad = dh.view(shape).to(torch.float16) if dh is not None else None
         return sums[0], ents.view(shape[:-1]), losses.view(shape[:-1]), hits, grad
     # A head that is a plain callable: its own logits, then the CE kernel in place.
     if with_grad:

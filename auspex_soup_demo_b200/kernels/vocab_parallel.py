@@ -42,30 +42,46 @@ def shard_range(vocab: int, rank: int, world: int):
 class ShardState:
     """Workspace and inputs one rank keeps between its forward and backward stages."""
 
-    def __init__(self, hidden, weight_shard, targets, offset, ws):
+    def __init__(self, hidden, weight_shard, targets, offset, ws, weight_bwd=None, in_dtype=None):
         self.hidden = hidden
         self.weight_shard = weight_shard
         self.targets = targets
         self.offset = offset
         self.ws = ws
+        self.weight_bwd = weight_bwd
+        self.in_dtype = _lib.BF16 if in_dtype is None else in_dtype
 
 
 def _prep(hidden, weight_shard, targets):
-    h = hidden.detach()
-    if h.dtype != torch.bfloat16 or not _tma_rows_ok(h):
-        h = h.to(torch.bfloat16).contiguous()
-    w = weight_shard.detach()
-    if w.dtype != torch.bfloat16 or not _tma_rows_ok(w):
-        w = w.to(torch.bfloat16).contiguous()
+    """(h, w, w_bwd, in_dtype, t): operands as the single-GPU path takes them
+    (bf16 hidden with a bf16 shard as they are; otherwise fp16 operands for the
+    logits GEMM and a bf16 copy of the shard for the dX GEMM)."""
+    if hidden.dtype == torch.bfloat16 and weight_shard.dtype == torch.bfloat16:
+        h = hidden.detach()
+        if not _tma_rows_ok(h):
+            h = h.contiguous()
+        w = weight_shard.detach()
+        if not _tma_rows_ok(w):
+            w = w.contiguous()
+        wb, in_dt = None, _lib.BF16
+    else:
+        h = hidden.detach()
+        if h.dtype != torch.float16 or not _tma_rows_ok(h):
+            h = h.to(torch.float16).contiguous()
+        w = weight_shard.detach()
+        if w.dtype != torch.float16 or not _tma_rows_ok(w):
+            w = w.to(torch.float16).contiguous()
+        wb = weight_shard.detach().to(torch.bfloat16).contiguous()
+        in_dt = _lib.F16
     t = targets.reshape(-1)
     if t.dtype != torch.int64 or not t.is_contiguous():
         t = t.to(torch.int64).contiguous()
-    return h, w, t
+    return h, w, wb, in_dt, t
 
 
 def vp_forward_shard(hidden, weight_shard, targets, offset: int, workspace: Optional[torch.Tensor] = None):
     """Stage 1 on one rank: returns (records [rows, 5] fp32, ShardState)."""
-    h, w, t = _prep(hidden, weight_shard, targets)
+    h, w, wb, in_dt, t = _prep(hidden, weight_shard, targets)
     n, d = h.shape
     v = w.shape[0]
     nbytes = _lib.lib().soup_ce_vp_workspace_bytes(n, v, d)
@@ -73,9 +89,9 @@ def vp_forward_shard(hidden, weight_shard, targets, offset: int, workspace: Opti
         workspace = torch.empty(nbytes, dtype=torch.uint8, device=h.device)
     states = torch.empty(n, 5, dtype=torch.float32, device=h.device)
     _lib.call("soup_ce_vp_forward", h.device, h.data_ptr(), h.stride(0), w.data_ptr(), w.stride(0),
-              t.data_ptr(), n, v, int(offset), d, states.data_ptr(), workspace.data_ptr(),
+              in_dt, t.data_ptr(), n, v, int(offset), d, states.data_ptr(), workspace.data_ptr(),
               workspace.numel(), _lib.stream_of(h))
-    return states, ShardState(h, w, t, int(offset), workspace)
+    return states, ShardState(h, w, t, int(offset), workspace, wb, in_dt)
 
 
 def vp_combine(states_all: torch.Tensor, targets: torch.Tensor, vocab_total: int,
@@ -105,8 +121,10 @@ def vp_backward_shard(state: ShardState, lse: torch.Tensor, denominator: float,
     v = w.shape[0]
     dh = torch.empty(n, d, dtype=dh_dtype, device=h.device)
     dw = torch.empty(v, d, dtype=dw_dtype, device=h.device) if compute_dw else None
+    wb = state.weight_bwd
     _lib.call("soup_ce_vp_backward", h.device, state.ws.data_ptr(), state.ws.numel(), h.data_ptr(),
-              h.stride(0), w.data_ptr(), w.stride(0), state.targets.data_ptr(), n, v, state.offset, d,
+              h.stride(0), w.data_ptr(), w.stride(0), state.in_dtype, _lib.ptr(wb),
+              wb.stride(0) if wb is not None else 0, state.targets.data_ptr(), n, v, state.offset, d,
               lse.data_ptr(), float(denominator), int(ignore_index), dh.data_ptr(),
               _lib.dtype_code(dh_dtype), _lib.ptr(dw), _lib.dtype_code(dw_dtype), 0,
               _lib.stream_of(h))

@@ -39,8 +39,19 @@ int soup_version(void);
 const char* soup_last_error(void);
 
 /* Device error word written by bounded waits in the GEMM kernels (0 = none).
- * Reading it synchronises the given stream. */
+ * Reads and clears it in one atomic step on the device (a code written
+ * meanwhile by a kernel on another stream stays for the next read), then
+ * synchronises the given stream. Codes: 0x101 producer, 0x102 MMA issuer,
+ * 0x103 epilogue wait expired. No counterpart in the reference (its Triton
+ * kernels have no device-side waits). */
 int soup_device_error(void* stream, int* out_code);
+
+/* Time limit of every mbarrier wait inside the GEMM kernels launched after
+ * this call (all devices): 0 restores the default of 2 s; otherwise at least
+ * 1 ms. A wait that expires records its code in the device error word, the
+ * kernel drains its copies and MMAs (each drain wait bounded by the same
+ * limit), frees its TMEM and returns. No counterpart in the reference. */
+int soup_set_wait_limit_ns(uint64_t ns);
 
 /* ---- RMSNorm -------------------------------------------------------------
  * Replaces solution/kernels/rmsnorm.py:22-57 (_rms_norm_fwd_kernel) and the
@@ -73,7 +84,10 @@ int soup_rmsnorm_bwd(const void* dy, int64_t dy_row_stride, const void* x, int64
  * `cols` per CTA, at most 3 CTAs per SM on the vector path (cols up to about
  * 2360 on a 148-SM B200, e.g. hidden sizes 1536 and 2048); calls needing more
  * than 4 MiB return SOUP_ERR_WORKSPACE. The first call on a device looks up the array's device
- * address; make that first call before any stream capture. All calls share
+ * address (under a lock, so first calls from several host threads are safe) and
+ * keeps it for the life of the process; make that first call before any stream
+ * capture, and do not call this entry point again on a device after a
+ * cudaDeviceReset of it (the kept address would be stale). All calls share
  * the array, so calls whose kernels overlap on the GPU (other streams, other
  * host threads) race: serialise them. */
 int soup_rmsnorm_bwd_noalloc(const void* dy, int64_t dy_row_stride, const void* x,
@@ -125,21 +139,27 @@ int soup_ce_rows(void* logits, int64_t row_stride, const int64_t* targets, float
  * factored: per-row factors times the stored exponentials exp(z - c_row), no
  * [rows, vocab] pass between the GEMMs), the input gradient and (new, no
  * reference counterpart) the lm_head gradient.
- * hidden [rows, dim] bf16 (row stride h_ld), weight [vocab, dim] bf16
- * (row stride w_ld), targets [rows] int64.
+ * hidden [rows, dim] (row stride h_ld) and weight [vocab, dim] (row stride
+ * w_ld) are both in_dtype: BF16, or F16 (the reference's own operand type: it
+ * rounds the chunk and a cached copy of W to fp16 for its GEMMs,
+ * chunked_ce.py:170-180,196-199); fp32 accumulation either way. The logits'
+ * gradient is kept in bf16, so with F16 operands the dX GEMM reads weight_bwd,
+ * a bf16 copy of the weight [vocab, dim] (row stride wb_ld); with BF16 it is
+ * ignored (may be NULL). targets [rows] int64.
  * Outputs: losses/entropies [rows] fp32, correct [rows] int32,
  * sums[2] fp32 = {sum of losses, sum of hits} (may be NULL),
- * dhidden [rows, dim] bf16 (NULL: no input gradient), dweight [vocab, dim]
- * (NULL: no lm_head gradient; dtype dw_dtype F32 or BF16; accumulate_dw != 0
- * adds to its contents). Gradients are scaled by 1/denominator (the caller's
- * grad_output scale is applied outside). workspace: see
- * soup_ce_linear_workspace_bytes. */
+ * dhidden [rows, dim] in dh_dtype F32 or BF16 (NULL: no input gradient),
+ * dweight [vocab, dim] (NULL: no lm_head gradient; dtype dw_dtype F32 or
+ * BF16; accumulate_dw != 0 adds to its contents). Gradients are scaled by
+ * 1/denominator (the caller's grad_output scale is applied outside).
+ * workspace: see soup_ce_linear_workspace_bytes. */
 size_t soup_ce_linear_workspace_bytes(int64_t rows, int64_t vocab, int64_t dim);
-int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t w_ld,
-                   const int64_t* targets, int64_t rows, int64_t vocab, int64_t dim,
-                   float denominator, int64_t ignore_index, float* losses, float* entropies,
-                   int32_t* correct, float* sums, void* dhidden, void* dweight, int dw_dtype,
-                   int accumulate_dw, void* workspace, size_t workspace_bytes, void* stream);
+int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t w_ld, int in_dtype,
+                   const void* weight_bwd, int64_t wb_ld, const int64_t* targets, int64_t rows,
+                   int64_t vocab, int64_t dim, float denominator, int64_t ignore_index,
+                   float* losses, float* entropies, int32_t* correct, float* sums, void* dhidden,
+                   int dh_dtype, void* dweight, int dw_dtype, int accumulate_dw, void* workspace,
+                   size_t workspace_bytes, void* stream);
 
 /* The lm_head gradient from the state that a preceding soup_ce_linear call
  * with a non-NULL dhidden left in `workspace` (same rows/vocab/dim/hidden):
@@ -150,10 +170,11 @@ int soup_ce_linear(const void* hidden, int64_t h_ld, const void* weight, int64_t
  * this call scales the hidden rows by s into the workspace and runs one GEMM.
  * Lets an autograd backward apply its upstream gradient inside the GEMM
  * epilogue instead of in a separate pass over the [vocab, dim] gradient.
+ * hidden has the in_dtype (BF16 or F16) given to soup_ce_linear.
  * Extends chunked_ce.py:307-311 (the reference's head is frozen and has no
  * gradient). */
 int soup_ce_linear_dweight(void* workspace, size_t workspace_bytes, const void* hidden,
-                           int64_t h_ld, int64_t rows, int64_t vocab, int64_t dim,
+                           int64_t h_ld, int in_dtype, int64_t rows, int64_t vocab, int64_t dim,
                            const float* grad_scale, void* dweight, int dw_dtype, int accumulate_dw,
                            void* stream);
 
@@ -173,18 +194,23 @@ int soup_ce_linear_dweight(void* workspace, size_t workspace_bytes, const void* 
  *      (the shard's buffer is not rewritten), this rank's partial dhidden =
  *      dL_shard W_shard (F32 or BF16) and its dW_shard = dL_shard^T H (local,
  *      no exchange);
- *   5. (caller) sum the partial dhidden over ranks (all-reduce).
+ *   5. (caller) sum the partial dhidden over ranks (a reduce-scatter over
+ *      token blocks, or an all-reduce).
+ * hidden and the shard are in_dtype (BF16 or F16, as for soup_ce_linear);
+ * with F16 the backward's dX GEMM reads weight_shard_bwd, a bf16 copy of the
+ * shard (NULL with BF16).
  * Same row semantics as chunked_ce.py:46-128. */
 size_t soup_ce_vp_workspace_bytes(int64_t rows, int64_t vocab_shard, int64_t dim);
 int soup_ce_vp_forward(const void* hidden, int64_t h_ld, const void* weight_shard, int64_t w_ld,
-                       const int64_t* targets, int64_t rows, int64_t vocab_shard,
+                       int in_dtype, const int64_t* targets, int64_t rows, int64_t vocab_shard,
                        int64_t vocab_offset, int64_t dim, float* states, void* workspace,
                        size_t workspace_bytes, void* stream);
 int soup_ce_vp_combine(const float* states_all, int nranks, const int64_t* targets, int64_t rows,
                        int64_t vocab_total, int64_t ignore_index, float* losses, float* entropies,
                        int32_t* correct, float* lse, float* sums, void* stream);
 int soup_ce_vp_backward(void* workspace, size_t workspace_bytes, const void* hidden, int64_t h_ld,
-                        const void* weight_shard, int64_t w_ld, const int64_t* targets,
+                        const void* weight_shard, int64_t w_ld, int in_dtype,
+                        const void* weight_shard_bwd, int64_t wb_ld, const int64_t* targets,
                         int64_t rows, int64_t vocab_shard, int64_t vocab_offset, int64_t dim,
                         const float* lse, float denominator, int64_t ignore_index,
                         void* dhidden_partial, int dh_dtype, void* dweight_shard, int dw_dtype,
@@ -219,6 +245,18 @@ int soup_nf4_dequant(const uint8_t* packed, const float* absmax, int64_t n, int 
 int soup_gemm_bf16(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb,
                    int b_mn_major, void* c, int64_t ldc, int c_dtype, int64_t m, int64_t n,
                    int64_t k, float alpha, int accumulate, void* stream);
+
+/* Diagnostic launch of the expiry path of the bounded waits: the same GEMM as
+ * soup_gemm_bf16 (A [m, k] and B [n, k] K-major bf16, C [m, n] bf16, row
+ * strides k, k, n) whose TMA producer withholds the second k-block of its
+ * first tile, so the MMA issuer's wait for it can never be satisfied and
+ * expires after wait_ns (1 ms .. 2 s). The kernel then records the code in the
+ * device error word (read it with soup_device_error) and returns; C is left
+ * partly unwritten. Requires k >= 128. Nothing in the fused ops calls it; it
+ * exists so a test can show that an expired wait ends the kernel with an error
+ * status and leaves the device usable. No counterpart in the reference. */
+int soup_gemm_wait_expiry_check(const void* a, const void* b, void* c, int64_t m, int64_t n,
+                                int64_t k, uint64_t wait_ns, void* stream);
 
 /* ---- Base GEMM plus a rank-r update in the same accumulator (QLoRA linears) --
  * C[m, n] = alpha * (sum_k A(m,k) B(n,k) + sum_{j<r} A2(m,j) B2(n,j)) + bias[n]

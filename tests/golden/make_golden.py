@@ -23,7 +23,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True,
+                    help="checkout of the reference project (its solution/ package is imported)")
     args = ap.parse_args()
     os.environ["TRITON_INTERPRET"] = "1"
     # Triton's cache goes to a throwaway folder; nothing in it is read.

@@ -354,3 +354,88 @@ def test_fused_ce_benchmark_configuration_against_torch_fp32():
     assert int(sums[1]) == int(hits.sum())
     assert cosine(dh, dh_ref) >= 0.9999
     assert cosine(dw, dw_ref) >= 0.9999
+
+
+def _planted_chunk(dtype, seed):
+    """One 128-row chunk (B=4 x chunk 32) at the benchmark's vocab and dim; a third
+    of the labelled rows have their target at the row's arg-max, so the hit count
+    is far from zero and must agree exactly."""
+    B, C, D, V = 4, 32, 1536, 151936
+    g = torch.Generator(device="cuda").manual_seed(seed)  # the host generator is slow at this size
+    piece = torch.randn(B, C, D, device="cuda", generator=g).to(dtype)
+    W = (0.02 * torch.randn(V, D, device="cuda", generator=g)).to(dtype)
+    target = torch.randint(0, V, (B, C), device="cuda", generator=g)
+    opd = torch.bfloat16 if dtype == torch.bfloat16 else torch.float16
+    logits = piece.to(opd).float().reshape(-1, D) @ W.to(opd).float().t()
+    am = logits.argmax(-1).view(B, C)
+    plant = torch.rand(B, C, device="cuda", generator=g) < 0.35
+    target[plant] = am[plant]
+    target[torch.rand(B, C, device="cuda", generator=g) < 0.1] = -100
+    target[0, 0] = -100
+    return piece.cpu(), W.cpu(), target.cpu(), logits
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_chunk_cross_entropy_triton_fused_branch(dtype):
+    """The reference's one-chunk entry point with a module head (chunked_ce.py:183-264):
+    total_loss = sum of the per-token losses (fp32), entropy / token_loss fp32 of
+    the piece's leading shape, hits an int64 count, piece_grad fp16 (the reference's
+    fp16 GEMM output) and None without gradient. The oracle gets the operands the
+    GEMM multiplies: bf16 as given, other dtypes rounded to fp16 as the reference
+    rounds them (chunked_ce.py:196-199)."""
+    from auspex_soup_demo_b200.kernels import chunk_cross_entropy_triton
+
+    piece, W, target, logits = _planted_chunk(dtype, seed=21 + int(dtype.itemsize))
+    den = float((target != -100).sum())
+    opd = torch.bfloat16 if dtype == torch.bfloat16 else torch.float16
+    ref = oracle.chunked_ce(piece.to(opd), W.to(opd), target, 32, den, compute_dw=False)
+    ref_total = float(ref[2].sum())
+    head = torch.nn.Linear(W.shape[1], W.shape[0], bias=False, dtype=dtype, device="cuda")
+    with torch.no_grad():
+        head.weight.copy_(W.cuda())
+    total, ent, tok, hits, grad = chunk_cross_entropy_triton(head, piece.cuda(), target.cuda(),
+                                                             -100, den, True)
+    torch.cuda.synchronize()
+    assert total.dtype == torch.float32 and total.dim() == 0
+    assert abs(float(total) - ref_total) <= 1e-4 * abs(ref_total), (float(total), ref_total)
+    assert abs(float(total) - float(tok.sum())) <= 1e-5 * abs(ref_total)
+    assert ent.shape == tok.shape == target.shape
+    assert ent.dtype == tok.dtype == torch.float32
+    torch.testing.assert_close(tok.cpu(), ref[2], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(ent.cpu(), ref[1], rtol=2e-3, atol=2e-3)
+    assert hits.dtype == torch.int64
+    assert int(hits) == int(ref[3]) and int(hits) > 20
+    assert grad.shape == piece.shape and grad.dtype == torch.float16
+    assert cosine(grad, ref[4]) >= 0.9999
+    # without gradient: same metrics, no piece_grad
+    total2, _, tok2, hits2, grad2 = chunk_cross_entropy_triton(head, piece.cuda(), target.cuda(),
+                                                               -100, den, False)
+    assert grad2 is None
+    assert int(hits2) == int(hits)
+    torch.testing.assert_close(tok2, tok, rtol=1e-6, atol=1e-6)
+    assert _lib.device_error(torch.device("cuda")) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_fused_ce_fp16_operands_match_the_reference_rounding(dtype):
+    """fp16 / fp32 activations enter the logits GEMM as fp16 operands (kind::f16 with
+    the f16 format), the reference's own rounding: against the oracle on the
+    fp16-rounded operands the loss is within 1e-4, hits bit-exact, and dhidden (fp32
+    for fp32 input) within cosine 0.9999."""
+    piece, W, target, _ = _planted_chunk(dtype, seed=33)
+    B, C, D = piece.shape
+    den = float((target != -100).sum())
+    ref = oracle.chunked_ce(piece.half(), W.half(), target, 32, den, compute_dw=False)
+    head = torch.nn.Linear(D, W.shape[0], bias=False, dtype=dtype, device="cuda")
+    with torch.no_grad():
+        head.weight.copy_(W.cuda())
+    head.weight.requires_grad_(False)
+    Fn = make_triton_chunked_loss_function()
+    h = piece.cuda().requires_grad_(True)
+    loss, ent, tok, corr = Fn.apply(h, head, target.cuda(), 32, den, -100, True)
+    loss.backward()
+    assert abs(float(loss.detach()) - float(ref[0])) <= 1e-4 * abs(float(ref[0]))
+    torch.testing.assert_close(tok.cpu(), ref[2], rtol=1e-4, atol=1e-4)
+    assert int(corr) == int(ref[3])
+    assert h.grad.dtype == dtype
+    assert cosine(h.grad, ref[4]) >= 0.9999

@@ -45,8 +45,8 @@ def test_null_pointers_are_rejected_without_a_gpu():
     assert st == _lib.SOUP_ERR_INVALID
     st = lib.soup_ce_rows(None, 8, None, None, None, None, 4, 8, 1.0, -100, 2, 1, None)
     assert st == _lib.SOUP_ERR_INVALID
-    st = lib.soup_ce_linear(None, 8, None, 8, None, 4, 8, 8, 1.0, -100, None, None, None, None,
-                            None, None, 0, 0, None, 0, None)
+    st = lib.soup_ce_linear(None, 8, None, 8, _lib.BF16, None, 0, None, 4, 8, 8, 1.0, -100, None,
+                            None, None, None, None, _lib.BF16, None, 0, 0, None, 0, None)
     assert st == _lib.SOUP_ERR_INVALID
     st = lib.soup_gemm_bf16(None, 8, 0, None, 8, 0, None, 8, 0, 4, 4, 4, 1.0, 0, None)
     assert st == _lib.SOUP_ERR_INVALID
@@ -102,35 +102,66 @@ def test_ce_gradient_state_entry_points_validate_before_the_gpu():
     lib = _lib.lib()
     fake = ctypes.c_void_p(16)  # 16-byte aligned, never dereferenced
     n, v, d = 4, 64, 8
-    # soup_ce_linear_dweight(workspace, bytes, hidden, h_ld, rows, vocab, dim, grad_scale,
-    #                        dweight, dw_dtype, accumulate, stream)
-    st = lib.soup_ce_linear_dweight(None, 1 << 20, fake, d, n, v, d, None, fake, _lib.F32, 0, None)
+    BF = _lib.BF16
+    # soup_ce_linear_dweight(workspace, bytes, hidden, h_ld, in_dtype, rows, vocab, dim,
+    #                        grad_scale, dweight, dw_dtype, accumulate, stream)
+    st = lib.soup_ce_linear_dweight(None, 1 << 20, fake, d, BF, n, v, d, None, fake, _lib.F32, 0, None)
     assert st == _lib.SOUP_ERR_INVALID
-    st = lib.soup_ce_linear_dweight(fake, 1 << 20, fake, d, n, v, d, None, fake, 7, 0, None)
+    st = lib.soup_ce_linear_dweight(fake, 1 << 20, fake, d, BF, n, v, d, None, fake, 7, 0, None)
     assert st == _lib.SOUP_ERR_INVALID
-    st = lib.soup_ce_linear_dweight(fake, 1 << 20, fake, d, n, v, 12, None, fake, _lib.F32, 0, None)
+    st = lib.soup_ce_linear_dweight(fake, 1 << 20, fake, d, _lib.F32, n, v, d, None, fake, _lib.F32,
+                                    0, None)
+    assert st == _lib.SOUP_ERR_INVALID  # operands are bf16 or fp16
+    st = lib.soup_ce_linear_dweight(fake, 1 << 20, fake, d, BF, n, v, 12, None, fake, _lib.F32, 0,
+                                    None)
     assert st in (_lib.SOUP_ERR_INVALID, _lib.SOUP_ERR_UNSUPPORTED)  # dim % 8 != 0, h_ld < dim
     need = lib.soup_ce_linear_workspace_bytes(n, v, d)
-    st = lib.soup_ce_linear_dweight(fake, need - 1, fake, d, n, v, d, None, fake, _lib.F32, 0, None)
+    st = lib.soup_ce_linear_dweight(fake, need - 1, fake, d, BF, n, v, d, None, fake, _lib.F32, 0,
+                                    None)
     assert st == _lib.SOUP_ERR_WORKSPACE
-    # soup_ce_vp_forward(hidden, h_ld, weight_shard, w_ld, targets, rows, vocab_shard,
+    # soup_ce_linear(hidden, h_ld, weight, w_ld, in_dtype, weight_bwd, wb_ld, targets, rows, vocab,
+    #                dim, den, ignore, losses, entropies, correct, sums, dhidden, dh_dtype,
+    #                dweight, dw_dtype, accumulate, workspace, bytes, stream)
+    st = lib.soup_ce_linear(fake, d, fake, d, _lib.F16, None, 0, fake, n, v, d, 1.0, -100, fake,
+                            fake, fake, None, fake, _lib.BF16, None, _lib.F32, 0, fake, need, None)
+    assert st == _lib.SOUP_ERR_INVALID  # fp16 operands with dhidden need the bf16 weight copy
+    assert b"weight_bwd" in lib.soup_last_error()
+    st = lib.soup_ce_linear(fake, d, fake, d, BF, None, 0, fake, n, v, d, 1.0, -100, fake, fake,
+                            fake, None, fake, 7, None, _lib.F32, 0, fake, need, None)
+    assert st == _lib.SOUP_ERR_INVALID  # bad dhidden dtype
+    # soup_ce_vp_forward(hidden, h_ld, weight_shard, w_ld, in_dtype, targets, rows, vocab_shard,
     #                    vocab_offset, dim, states, workspace, bytes, stream)
-    st = lib.soup_ce_vp_forward(None, d, fake, d, fake, n, v, 0, d, fake, fake, 1 << 20, None)
+    st = lib.soup_ce_vp_forward(None, d, fake, d, BF, fake, n, v, 0, d, fake, fake, 1 << 20, None)
     assert st == _lib.SOUP_ERR_INVALID
-    st = lib.soup_ce_vp_forward(fake, d, fake, d, fake, n, v, -1, d, fake, fake, 1 << 20, None)
+    st = lib.soup_ce_vp_forward(fake, d, fake, d, BF, fake, n, v, -1, d, fake, fake, 1 << 20, None)
     assert st == _lib.SOUP_ERR_INVALID  # negative vocab offset
     need_vp = lib.soup_ce_vp_workspace_bytes(n, v, d)
-    st = lib.soup_ce_vp_forward(fake, d, fake, d, fake, n, v, 0, d, fake, fake, need_vp - 1, None)
+    st = lib.soup_ce_vp_forward(fake, d, fake, d, BF, fake, n, v, 0, d, fake, fake, need_vp - 1,
+                                None)
     assert st == _lib.SOUP_ERR_WORKSPACE
-    # soup_ce_vp_backward(workspace, bytes, hidden, h_ld, weight_shard, w_ld, targets, rows,
-    #                     vocab_shard, vocab_offset, dim, lse, denominator, ignore_index,
-    #                     dhidden_partial, dh_dtype, dweight_shard, dw_dtype, accumulate, stream)
-    st = lib.soup_ce_vp_backward(fake, need_vp, fake, d, fake, d, fake, n, v, 0, d, None, 1.0, -100,
-                                 fake, _lib.F32, None, _lib.BF16, 0, None)
+    # soup_ce_vp_backward(workspace, bytes, hidden, h_ld, weight_shard, w_ld, in_dtype,
+    #                     weight_shard_bwd, wb_ld, targets, rows, vocab_shard, vocab_offset, dim,
+    #                     lse, denominator, ignore_index, dhidden_partial, dh_dtype,
+    #                     dweight_shard, dw_dtype, accumulate, stream)
+    st = lib.soup_ce_vp_backward(fake, need_vp, fake, d, fake, d, BF, None, 0, fake, n, v, 0, d,
+                                 None, 1.0, -100, fake, _lib.F32, None, BF, 0, None)
     assert st == _lib.SOUP_ERR_INVALID  # no lse
-    st = lib.soup_ce_vp_backward(fake, need_vp, fake, d, fake, d, fake, n, v, 0, d, fake, 1.0, -100,
-                                 fake, 7, None, _lib.BF16, 0, None)
+    st = lib.soup_ce_vp_backward(fake, need_vp, fake, d, fake, d, BF, None, 0, fake, n, v, 0, d,
+                                 fake, 1.0, -100, fake, 7, None, BF, 0, None)
     assert st == _lib.SOUP_ERR_INVALID  # bad dhidden dtype
-    st = lib.soup_ce_vp_backward(fake, need_vp - 1, fake, d, fake, d, fake, n, v, 0, d, fake, 1.0,
-                                 -100, fake, _lib.F32, None, _lib.BF16, 0, None)
+    st = lib.soup_ce_vp_backward(fake, need_vp, fake, d, fake, d, _lib.F16, None, 0, fake, n, v, 0,
+                                 d, fake, 1.0, -100, fake, _lib.F32, None, BF, 0, None)
+    assert st == _lib.SOUP_ERR_INVALID  # fp16 shard without its bf16 copy
+    st = lib.soup_ce_vp_backward(fake, need_vp - 1, fake, d, fake, d, BF, None, 0, fake, n, v, 0, d,
+                                 fake, 1.0, -100, fake, _lib.F32, None, BF, 0, None)
     assert st == _lib.SOUP_ERR_WORKSPACE
+
+
+def test_wait_limit_setting_is_validated_on_the_host():
+    lib = _lib.lib()
+    assert lib.soup_set_wait_limit_ns(500_000) == _lib.SOUP_ERR_INVALID  # below 1 ms
+    assert b"wait_limit" in lib.soup_last_error()
+    assert lib.soup_set_wait_limit_ns(10_000_000) == _lib.SOUP_OK
+    assert lib.soup_set_wait_limit_ns(0) == _lib.SOUP_OK  # back to the 2 s default
+    st = lib.soup_gemm_wait_expiry_check(None, None, None, 256, 256, 256, 1_000_000, None)
+    assert st == _lib.SOUP_ERR_INVALID

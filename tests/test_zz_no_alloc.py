@@ -5,13 +5,14 @@ memory (for example code running under an allocator that already owns the
 whole GPU, or host code that must not call cudaMalloc because it can
 synchronise the device). It keeps its dw partial rows in a 4 MiB array built
 into the library. This test compares it with soup_rmsnorm_bwd, which takes a
-caller workspace, on two calls in a row, and checks the size limit. The file
-is named so pytest collects it last.
+caller workspace, and with the CPU oracle, on two calls in a row, and checks
+the size limit. The file is named so pytest collects it last.
 """
 
 import pytest
 import torch
 
+import oracle
 from auspex_soup_demo_b200 import _lib
 
 pytestmark = pytest.mark.gpu
@@ -71,6 +72,10 @@ def test_noalloc_matches_workspace_entry_point_twice(rows, cols, dtype):
         tol = FP32_TOL if dtype == torch.float32 else 8e-3
         assert _close(dx, ref_dx) <= tol, f"call {call}: dx"
         assert _close(dw, ref_dw) <= tol, f"call {call}: dw"
+        # and against the CPU restatement of the reference's backward
+        o_dx, o_dw = oracle.rmsnorm_bwd(dy.cpu(), x.cpu(), w.cpu(), rstd.cpu())
+        assert _close(dx.cpu(), o_dx) <= tol, f"call {call}: dx vs oracle"
+        assert _close(dw.cpu(), o_dw) <= tol, f"call {call}: dw vs oracle"
 
 
 def test_noalloc_rejects_sizes_beyond_its_buffer():

@@ -83,6 +83,12 @@ _SIGNATURES = {
                                     c_i64, c_i64, c_i64, c_i64, c_vp, c_f, c_i64, c_vp, c_int, c_vp,
                                     c_int, c_int, c_vp]),
     "soup_set_stage_events": (c_int, [ctypes.POINTER(c_vp), c_int]),
+    "soup_attention_fwd": (c_int, [c_vp, P_I64, c_vp, P_I64, c_vp, P_I64, c_i64, c_i64, c_i64, c_i64,
+                                   c_i64, c_f, c_int, c_vp, c_vp, c_vp]),
+    "soup_attention_bwd_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64]),
+    "soup_attention_bwd": (c_int, [c_vp, P_I64, c_vp, P_I64, c_vp, P_I64, c_vp, c_vp, c_vp, c_i64,
+                                   c_i64, c_i64, c_i64, c_i64, c_f, c_int, c_vp, c_vp, c_vp, c_vp,
+                                   c_sz, c_vp]),
     "soup_nf4_quantize": (c_int, [c_vp, c_i64, c_int, c_int, ctypes.POINTER(c_f), c_vp, c_vp, c_vp]),
     "soup_nf4_dequant": (c_int, [c_vp, c_vp, c_i64, c_int, ctypes.POINTER(c_f), c_vp, c_int, c_vp]),
     "soup_gemm_bf16": (c_int, [c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_i64,

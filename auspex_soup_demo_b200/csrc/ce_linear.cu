@@ -619,6 +619,7 @@ static int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t 
     set_last_error("cuTensorMapEncodeTiled is not available from the driver");
     return SOUP_ERR_CUDA;
   }
+  if (int rc = bind_context()) return rc;
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {ld * 2};
   cuuint32_t box[2] = {64, box_outer};

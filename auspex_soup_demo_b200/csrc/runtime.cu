@@ -37,6 +37,16 @@ int* device_err_ptr() {
   return cached[dev];
 }
 
+// Make the current device's primary context current on this host thread. The
+// driver-API tensor-map encoder needs one, and a thread such as autograd's
+// backward worker may reach a library call before any runtime call bound it.
+int bind_context() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaSetDevice(dev);
+  return cuda_status(e);
+}
+
 static std::atomic<unsigned long long> g_wait_limit_ns{0};
 
 uint64_t wait_limit_ns() { return g_wait_limit_ns.load(std::memory_order_relaxed); }

@@ -24,6 +24,7 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 int num_sms();                                       // of the current device (cached)
 int* device_err_ptr();                               // device error word of the current device
 std::mutex& cache_mutex();                           // guards the library's per-device caches
+int bind_context();                                  // current device's context on this thread
 uint64_t wait_limit_ns();                            // soup_set_wait_limit_ns (0: the default)
 
 // ---------------------------------------------------------------- dtypes ----

@@ -224,6 +224,37 @@ int soup_ce_vp_backward(void* workspace, size_t workspace_bytes, const void* hid
  * cudaEvent_t handles owned by the caller. */
 int soup_set_stage_events(void** events, int n);
 
+/* ---- Causal grouped-query flash attention (head dim 128, bf16) ---------------
+ * No kernel in the reference: its Qwen2 attention is torch SDPA, called by
+ * transformers' sdpa_attention_forward from Qwen2Attention.forward. q is
+ * [batch, heads, seq, 128], k and v [batch, kv_heads, seq, 128] (heads a
+ * multiple of kv_heads), each with element strides {b, h, s} (multiples of 8)
+ * and a contiguous last dimension, 16-byte aligned. out = softmax(scale q k^T
+ * [+ causal mask]) v as bf16 [batch, seq, heads, 128] (contiguous), lse =
+ * log-sum-exp of the scaled logits per query, fp32 [batch, heads, S_pad] with
+ * rows padded to S_pad = seq rounded up to 128 (the padding is not written). */
+int soup_attention_fwd(const void* q, const int64_t* q_strides, const void* k,
+                       const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                       int64_t batch, int64_t heads, int64_t kv_heads, int64_t seq,
+                       int64_t head_dim, float scale, int causal, void* out, float* lse,
+                       void* stream);
+
+/* Backward of soup_attention_fwd: dq [batch, seq, heads, 128], dk and dv
+ * [batch, seq, kv_heads, 128] (bf16, contiguous) from q, k, v (as given to the
+ * forward), its out and lse, and dout = dL/d out ([batch, seq, heads, 128]
+ * contiguous). P is recomputed from lse; dK / dV are accumulated per query
+ * head in fp32 and summed over each KV head's group in a fixed order, dQ per
+ * query tile over the key tiles (no atomics: reproducible). workspace: see
+ * soup_attention_bwd_workspace_bytes (row dot products dout . out and the
+ * fp32 per-head partials). */
+size_t soup_attention_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq);
+int soup_attention_bwd(const void* q, const int64_t* q_strides, const void* k,
+                       const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                       const void* out, const void* dout, const float* lse, int64_t batch,
+                       int64_t heads, int64_t kv_heads, int64_t seq, int64_t head_dim, float scale,
+                       int causal, void* dq, void* dk, void* dv, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 /* ---- NF4 base weights for the QLoRA step ------------------------------------
  * No kernel in the reference: there the 4-bit base layers come from
  * bitsandbytes (Linear4bit, blocksize 64; harness/eval_adapter.py:26-28 loads

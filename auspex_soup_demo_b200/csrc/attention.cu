@@ -103,6 +103,28 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 32 lanes x 32 fp32 columns from TMEM without waiting: several loads are
+// issued back to back and completed by one tmem_ld_wait (the registers may
+// not be read before it).
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, float (&v)[32]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  __syncwarp();
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&p);
@@ -321,29 +343,34 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       tc_fence_after();
       float s[kTile];
 #pragma unroll
-      for (int c = 0; c < kTile / 32; ++c) {
-        float t[32];
-        tmem_ld32(tmem + sb * 128 + c * 32 + lane_off, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
-      }
+      for (int c = 0; c < kTile / 32; ++c)
+        tmem_ld32_async(tmem + sb * 128 + c * 32 + lane_off,
+                        *reinterpret_cast<float(*)[32]>(s + c * 32));
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_empty(sb));
       // masks: keys beyond the sequence, and (causal) keys after the query
       const int k0 = j * kTile;
       const bool edge = (k0 + kTile > a.S) || (a.causal && j == qt);
-      float mt = -INFINITY;
+      if (edge) {
 #pragma unroll
-      for (int i = 0; i < kTile; ++i) {
-        float v = s[i] * a.scale_log2;
-        if (edge) {
+        for (int i = 0; i < kTile; ++i) {
           const int key = k0 + i;
-          if (key >= a.S || (a.causal && key > q)) v = -INFINITY;
+          if (key >= a.S || (a.causal && key > q)) s[i] = -INFINITY;
         }
-        s[i] = v;
-        mt = fmaxf(mt, v);
       }
+      // row maximum of the raw logits (the scale is positive), eight chains
+      float mx[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mx[u] = s[u];
+#pragma unroll
+      for (int i = 8; i < kTile; i += 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) mx[u] = fmaxf(mx[u], s[i + u]);
+      }
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * a.scale_log2;
       bool rescale = false;
       float alpha = 1.f;
       if (mt > m_used + 8.f) {  // also when m_used is still -inf
@@ -351,12 +378,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         m_used = mt;
         rescale = true;
       }
-      float sum = 0.f;
+      float sm[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < kTile; ++i) {
-        s[i] = fast_exp2(s[i] - m_used);
-        sum += s[i];
+      for (int i = 0; i < kTile; i += 8) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          s[i + u] = fast_exp2(fmaf(s[i + u], a.scale_log2, -m_used));
+          sm[u] += s[i + u];
+        }
       }
+      const float sum = ((sm[0] + sm[1]) + (sm[2] + sm[3])) + ((sm[4] + sm[5]) + (sm[6] + sm[7]));
       l = rescale ? l * alpha + sum : l + sum;
       // P V of the previous tile must be done: the P buffer and O are reused
       if (j > 0) {
@@ -368,14 +399,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // tcgen05.ld / st are warp-collective (.sync.aligned): the whole warp
         // rescales when any of its rows needs it (alpha = 1 for the others)
         if (__any_sync(0xffffffffu, rescale)) {
+          float o[kHeadDim];
 #pragma unroll
-          for (int c = 0; c < kHeadDim / 32; ++c) {
-            float o[32];
-            tmem_ld32(tmem + 256 + c * 32 + lane_off, o);
+          for (int c = 0; c < kHeadDim / 32; ++c)
+            tmem_ld32_async(tmem + 256 + c * 32 + lane_off,
+                            *reinterpret_cast<float(*)[32]>(o + c * 32));
+          tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tmem + 256 + c * 32 + lane_off, o);
-          }
+          for (int i = 0; i < kHeadDim; ++i) o[i] *= alpha;
+#pragma unroll
+          for (int c = 0; c < kHeadDim / 32; ++c)
+            tmem_st32(tmem + 256 + c * 32 + lane_off, *reinterpret_cast<float(*)[32]>(o + c * 32));
           tmem_st_wait();
         }
       }
@@ -706,16 +740,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
       for (int c = 0; c < kTile / 32; ++c) {
         float sv[32], dp[32];
-        tmem_ld32(tmem + c * 32 + lane_off, sv);
-        tmem_ld32(tmem + 128 + c * 32 + lane_off, dp);
+        tmem_ld32_async(tmem + c * 32 + lane_off, sv);
+        tmem_ld32_async(tmem + 128 + c * 32 + lane_off, dp);
+        tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float p2[2], d2[2];
+          const float2 l2 = *reinterpret_cast<const float2*>(vlse + c * 32 + e);
+          const float2 dd = *reinterpret_cast<const float2*>(vD + c * 32 + e);
+          const float lv[2] = {l2.x, l2.y}, dvv[2] = {dd.x, dd.y};
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int qi = c * 32 + e + u;
-            float pv = fast_exp2(sv[e + u] * a.scale_log2 - vlse[qi] * 1.4426950408889634f);
-            float dv = pv * (dp[e + u] - vD[qi]);
+            float pv = fast_exp2(fmaf(sv[e + u], a.scale_log2, -lv[u] * 1.4426950408889634f));
+            float dv = pv * (dp[e + u] - dvv[u]);
             if (edge) {  // padding rows of lse / D may hold anything: select, do not scale
               const int q = q0 + qi;
               if (q >= a.S || (a.causal && q < key)) pv = dv = 0.f;
@@ -962,8 +1000,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
       for (int c = 0; c < kTile / 32; ++c) {
         float sv[32], dp[32];
-        tmem_ld32(tmem + c * 32 + lane_off, sv);
-        tmem_ld32(tmem + 128 + c * 32 + lane_off, dp);
+        tmem_ld32_async(tmem + c * 32 + lane_off, sv);
+        tmem_ld32_async(tmem + 128 + c * 32 + lane_off, dp);
+        tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float d2[2];

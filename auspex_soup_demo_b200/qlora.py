@@ -682,7 +682,13 @@ def group_projections(model, kinds=("qkv", "gate_up")):
     return groups
 
 
-def qwen2_1p5b_config(num_layers: int = 28, **overrides):
+def qwen2_1p5b_config(num_layers: int = 28, attention: str = "sdpa", **overrides):
+    """Qwen2.5-1.5B shapes with ``num_layers`` decoder layers.
+
+    attention: ``"sdpa"`` (transformers' SDPA, cuDNN on B200; the default: it is
+    faster than this library's kernels at the step's shapes) or ``"soup"``
+    (the tcgen05 flash attention of ``kernels.attention``, registered with
+    transformers under its interface name)."""
     from transformers import Qwen2Config
 
     kw = dict(hidden_size=1536, intermediate_size=8960, num_hidden_layers=num_layers,
@@ -692,7 +698,14 @@ def qwen2_1p5b_config(num_layers: int = 28, **overrides):
               initializer_range=0.02, hidden_act="silu", use_cache=False)
     kw.update(overrides)
     cfg = Qwen2Config(**kw)
-    cfg._attn_implementation = "sdpa"
+    if attention == "soup":
+        from .kernels.attention import register
+
+        cfg._attn_implementation = register()
+    elif attention == "sdpa":
+        cfg._attn_implementation = "sdpa"
+    else:
+        raise ValueError(f"attention must be 'sdpa' or 'soup', not {attention!r}")
     return cfg
 
 

@@ -319,8 +319,9 @@ def measure_qlora(args, R: Ranks, batch: int, seq: int, with_extras: bool = True
         from auspex_soup_demo_b200.kernels import swiglu as _swiglu
         _swiglu.RECOMPUTE = False
     dev = R.dev
-    model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=args.layers), device=dev,
-                                    seed=0)
+    model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=args.layers,
+                                                            attention=args.attention),
+                                    device=dev, seed=0)
     trainer = qlora.QLoRATrainer(model, lr=2e-4, ddp=R.world > 1)
     g = torch.Generator().manual_seed(1234 + R.rank)
     ids_cpu = torch.randint(0, VOCAB, (batch, seq), generator=g)
@@ -827,6 +828,65 @@ def measure_mem_op(wl: str, batch: int, seq: int, steps: int, warmup: int, dev):
     return res
 
 
+# ============================================================= attention ====
+def measure_attention(args, R: Ranks, batch: int = QLORA_BATCH, seq: int = QLORA_SEQ):
+    """The step's attention alone (B x S tokens, 12 query / 2 KV heads of 128, causal):
+    this library's tcgen05 kernels against torch SDPA (cuDNN) on the same inputs,
+    forward and forward + backward, CUDA events. FLOPs: forward 4 B H S^2 D / 2
+    (causal), backward 2.5x that (5 products, the causal half)."""
+    import math
+
+    from auspex_soup_demo_b200.kernels.attention import attention_forward, flash_attention
+
+    dev = R.dev
+    H, Hk, D = 12, 2, 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(batch, seq, H, D, device=dev, generator=g).to(torch.bfloat16).transpose(1, 2)
+    k = torch.randn(batch, seq, Hk, D, device=dev, generator=g).to(torch.bfloat16).transpose(1, 2)
+    v = torch.randn(batch, seq, Hk, D, device=dev, generator=g).to(torch.bfloat16).transpose(1, 2)
+    do = torch.randn(batch, seq, H, D, device=dev, generator=g).to(torch.bfloat16)
+    sc = 1.0 / math.sqrt(D)
+    qg, kg, vg = (t.detach().clone().requires_grad_(True) for t in (q, k, v))
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    def soup_fb():
+        flash_attention(qg, kg, vg, sc, True).backward(do)
+
+    def sdpa_fb():
+        sdpa(qg, kg, vg, is_causal=True, scale=sc, enable_gqa=True).transpose(1, 2).backward(do)
+
+    n = max(args.steps, 5)
+    t = {"soup_fwd": timed(lambda: attention_forward(q, k, v, sc, True), n),
+         "sdpa_fwd": timed(lambda: sdpa(q, k, v, is_causal=True, scale=sc, enable_gqa=True), n),
+         "soup_fwd_bwd": timed(soup_fb, n), "sdpa_fwd_bwd": timed(sdpa_fb, n)}
+    fwd_flop = 4.0 * batch * H * seq * seq * D / 2
+    peak, _, src = _peaks()
+    out = {"config": f"batch {batch} x seq {seq}, 12 query / 2 KV heads of 128, causal, bf16",
+           "unit": "us / TFLOP/s", "peak": peak, "peak_source": f"{src} bf16_tflops (burst)",
+           "in_step": "sdpa (cuDNN): faster at this shape; the tcgen05 kernels run with "
+                      "--attention soup"}
+    for key, ms in t.items():
+        flop = fwd_flop * (3.5 if key.endswith("fwd_bwd") else 1.0)
+        out[key] = {"us": round(ms * 1e3, 1), "tflops": round(flop / (ms * 1e-3) / 1e12, 1),
+                    "frac": round(flop / (ms * 1e-3) / 1e12 / peak, 4)}
+    del q, k, v, do, qg, kg, vg
+    _free()
+    return out
+
+
 # ===================================================== vocab-parallel CE ====
 def measure_ce_vp(args, R: Ranks):
     """Vocab-parallel fused CE: T tokens, W [151936, 1536] bf16 sharded over the ranks.
@@ -919,6 +979,7 @@ def run_step(args):
         extras["mem_ops"] = {wl: measure_mem_op(wl, 4, 512, args.steps, args.warmup, R.dev)
                              for wl in ("rmsnorm", "swiglu", "rope")}
         extras["ce_vp"] = measure_ce_vp(args, R)
+        extras["attention"] = measure_attention(args, R)
     B = args.batch
     own = q.get("own_kernels_per_step", 0)
     line = {
@@ -931,7 +992,7 @@ def run_step(args):
                    "batch_per_gpu": B, "seq_len": seq, "global_batch": B * R.world,
                    "lora": "r16 a32 q/k/v/o/gate/up/down", "lora_params": q["lora_params"],
                    "base": "NF4 blocksize 64, dequantised per use", "optimizer": "AdamW 2e-4",
-                   "mlp_recompute": not args.no_recompute,
+                   "mlp_recompute": not args.no_recompute, "attention": args.attention,
                    "parallelism": f"dp{R.world}" + (" (one NCCL all-reduce of the flat fp32 LoRA "
                                                     "gradient per step)" if R.world > 1 else ""),
                    "l2": "weights and activations far larger than L2"},
@@ -1024,6 +1085,9 @@ def main():
                          "length of the op's shape (512)")
     ap.add_argument("--layers", type=int, default=QLORA_LAYERS, help="step/qlora: decoder layers")
     ap.add_argument("--no-graph", action="store_true", help="step/qlora: launch eagerly, no CUDA graph")
+    ap.add_argument("--attention", default="sdpa", choices=["sdpa", "soup"],
+                    help="step/qlora: transformers' SDPA (cuDNN; default) or this library's tcgen05 "
+                         "flash attention")
     ap.add_argument("--no-recompute", action="store_true",
                     help="step/qlora: keep MLP activations instead of recomputing gate/up in backward")
     ap.add_argument("--profile", action="store_true",

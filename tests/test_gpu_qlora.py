@@ -339,3 +339,30 @@ def test_adamw_flat_matches_torch_adamw(n, n_scaled, wd):
     torch.testing.assert_close(v, st["exp_avg_sq"], rtol=1e-5, atol=1e-6)
     want16 = torch.cat([p[:n_scaled] * scale, p[n_scaled:]]).to(torch.bfloat16)
     assert torch.equal(p16, want16)
+
+
+def test_qlora_model_with_soup_attention_matches_sdpa():
+    """The same small model (head dim 128) with the tcgen05 attention and with
+    transformers' SDPA: loss and LoRA gradients agree."""
+    from auspex_soup_demo_b200.kernels import make_triton_chunked_loss_function
+
+    apply()
+    results = []
+    for attention in ("sdpa", "soup"):
+        cfg = qlora.qwen2_1p5b_config(num_layers=2, hidden_size=512, intermediate_size=1024,
+                                      num_attention_heads=4, num_key_value_heads=2,
+                                      vocab_size=2048, attention=attention)
+        model = qlora.build_qwen2_qlora(cfg, device="cuda", seed=6)
+        torch.manual_seed(7)  # the same non-zero B factors in both models
+        for m in model.modules():
+            if isinstance(m, qlora.LoRANF4Linear):
+                torch.nn.init.normal_(m.lora_B, std=0.02)
+        model.train()
+        g = torch.Generator().manual_seed(8)
+        ids = torch.randint(0, 2048, (2, 256), generator=g).cuda()
+        labels = qlora.causal_labels(ids)
+        results.append(_grads(model, ids, labels, make_triton_chunked_loss_function()))
+    (l_sdpa, g_sdpa), (l_soup, g_soup) = results
+    assert abs(l_soup - l_sdpa) <= 2e-3 * abs(l_sdpa), (l_soup, l_sdpa)
+    cos = [cosine(g_soup[k], g_sdpa[k]) for k in g_sdpa]
+    assert min(cos) > 0.99 and sum(cos) / len(cos) > 0.999, min(cos)

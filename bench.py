@@ -8,7 +8,8 @@ decoder layers with NF4 (blocksize 64) base weights, LoRA r16 / alpha 32 on
 q/k/v/o/gate/up/down, the fused RMSNorm / RoPE / SwiGLU / head-CE ops, AdamW
 2e-4, and with N > 1 one NCCL all-reduce of the flat 73.9 MB LoRA gradient
 per step. The whole step (forward, backward, all-reduce, AdamW) is one CUDA
-graph replay.
+graph replay. The MLP keeps [g | u] for its backward (the reference recomputes it
+to save memory; the results are bit-identical, ``--recompute`` restores it).
 
 * ``value``: tokens/s of all ranks, device-resident ids, CUDA events around
   exactly K replays (barrier + synchronize on both sides, max over ranks).
@@ -315,9 +316,12 @@ def measure_qlora(args, R: Ranks, batch: int, seq: int, with_extras: bool = True
     from oracle import qlora_step as ref
 
     apply()
-    if args.no_recompute:
-        from auspex_soup_demo_b200.kernels import swiglu as _swiglu
-        _swiglu.RECOMPUTE = False
+    # The reference recomputes gate/up in the MLP backward to fit a 16 GB T4
+    # (solution/kernels/swiglu.py:205-214). Its results are bit-identical to keeping
+    # [g | u] (tests/test_gpu_qlora.py), which at B4 x S2048 costs 294 MB per layer
+    # (8.2 GB for 28 layers) of the B200's 180 GB and saves one gate/up GEMM per layer.
+    from auspex_soup_demo_b200.kernels import swiglu as _swiglu
+    _swiglu.RECOMPUTE = bool(args.recompute)
     dev = R.dev
     model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=args.layers,
                                                             attention=args.attention),
@@ -406,7 +410,7 @@ def measure_qlora(args, R: Ranks, batch: int, seq: int, with_extras: bool = True
         # dominant kernel: the gate/up GEMM with the SwiGLU epilogue, at the step's shape
         grp = model.model.layers[0].mlp.gate_proj.lora_group
         if grp is not None and grp.interleaved:
-            res["dominant"] = time_gate_up_gemm(grp, batch * seq, dev)
+            res["dominant"] = time_gate_up_gemm(grp, batch * seq, dev, recompute=bool(args.recompute))
         if args.profile and R.rank == 0:
             kernel_table(one_step, 2)
         sus_peak, sus_src = _sustained_peak()
@@ -426,9 +430,11 @@ def measure_qlora(args, R: Ranks, batch: int, seq: int, with_extras: bool = True
     return res
 
 
-def time_gate_up_gemm(group, m: int, dev, reps: int = 20):
-    """CUDA-event duration of the gate/up GEMM + SwiGLU epilogue launch (forward and
-    recompute-backward modes) at m tokens: the QLoRA step's largest kernel."""
+def time_gate_up_gemm(group, m: int, dev, reps: int = 20, recompute: bool = False):
+    """CUDA-event duration of the gate/up GEMM + SwiGLU epilogue launch at m tokens,
+    the QLoRA step's largest kernel, in the modes the step runs: the forward that
+    also keeps [g | u] for the backward, or (recompute) the forward that writes h
+    only and the recompute-backward that turns dh into [dg | du]."""
     from auspex_soup_demo_b200 import qlora
 
     k = group.in_features
@@ -443,10 +449,13 @@ def time_gate_up_gemm(group, m: int, dev, reps: int = 20):
     dy = torch.empty(m, group.n_total, device=dev, dtype=torch.bfloat16)
     stream = torch.cuda.current_stream(dev)
     out = {}
-    for mode, name in ((0, "fwd"), (1, "bwd")):
+    modes = ((0, "fwd"), (1, "bwd")) if recompute else ((2, "fwd"),)
+    for mode, name in modes:
         def launch():
             if mode == 0:
                 qlora.swiglu_gemm(x, w, xa, Bblk, None, 0, h)
+            elif mode == 2:  # forward keeping [g | u] for the backward
+                qlora.swiglu_gemm(x, w, xa, Bblk, None, 0, h, dy)
             else:
                 qlora.swiglu_gemm(x, w, xa, Bblk, None, 1, dh, dy)
         for _ in range(3):
@@ -465,16 +474,21 @@ def time_gate_up_gemm(group, m: int, dev, reps: int = 20):
     flop = 2.0 * m * n * (k + r)
     peak, _, src = _peaks()
     sus_peak, sus_src = _sustained_peak()
-    mean_ms = (out["fwd"] + out["bwd"]) / 2
+    mean_ms = sum(out.values()) / len(out)
     achieved = flop / (mean_ms * 1e-3) / 1e12
-    return {"frac_of_sustained": round(achieved / sus_peak, 4), "sustained_peak": sus_peak,
-            "sustained_peak_source": f"{sus_src} bf16_tflops_sustained","kernel": "soup::tc::gemm_pair_kernel<EpiSwiGLU> (gate/up + rank-32 LoRA k-block, "
-                      "SwiGLU epilogue; forward and recompute-backward modes)",
+    modes_text = ("forward (h only) and recompute-backward modes" if recompute
+                  else "forward writing h and [g | u]")
+    return {"kernel": "soup::tc::gemm_pair_kernel<EpiSwiGLU> (gate/up + rank-32 LoRA k-block, "
+                      f"SwiGLU epilogue; {modes_text})",
             "shape": f"M {m} x N {n} (gate/up interleaved) x K {k} + rank {r}",
-            "flop_per_launch": flop, "ms_fwd": round(out["fwd"], 4), "ms_bwd": round(out["bwd"], 4),
+            "flop_per_launch": flop, "ms_fwd": round(out["fwd"], 4),
+            "ms_bwd": round(out["bwd"], 4) if "bwd" in out else None,
             "achieved": round(achieved, 1), "peak": peak, "frac": round(achieved / peak, 4),
             "peak_source": f"{src} bf16_tflops (burst: the launch is timed alone, {reps} back to back)",
-            "traffic": _committed_traffic(f"gemm_pair_kernel_swiglu_m{m}")}
+            "frac_of_sustained": round(achieved / sus_peak, 4), "sustained_peak": sus_peak,
+            "sustained_peak_source": f"{sus_src} bf16_tflops_sustained",
+            "traffic": _committed_traffic(f"gemm_pair_kernel_swiglu_m{m}"
+                                          + ("" if recompute else "_keep"))}
 
 
 # ============================================================== fused CE ====
@@ -994,7 +1008,7 @@ def run_step(args):
                    "batch_per_gpu": B, "seq_len": seq, "global_batch": B * R.world,
                    "lora": "r16 a32 q/k/v/o/gate/up/down", "lora_params": q["lora_params"],
                    "base": "NF4 blocksize 64, dequantised per use", "optimizer": "AdamW 2e-4",
-                   "mlp_recompute": not args.no_recompute, "attention": args.attention,
+                   "mlp_recompute": bool(args.recompute), "attention": args.attention,
                    "parallelism": f"dp{R.world}" + (" (one NCCL all-reduce of the flat fp32 LoRA "
                                                     "gradient per step)" if R.world > 1 else ""),
                    "l2": "weights and activations far larger than L2"},
@@ -1016,7 +1030,8 @@ def run_step(args):
         line["roofline"] = {"bound": "tensor", "achieved": dom["achieved"], "peak": dom["peak"],
                             "unit": "TFLOP/s", "frac": dom["frac"], "traffic": dom["traffic"],
                             "kernel": dom["kernel"], "shape": dom["shape"],
-                            "ms_per_launch": {"fwd": dom["ms_fwd"], "bwd": dom["ms_bwd"]},
+                            "ms_per_launch": {k: v for k, v in (("fwd", dom["ms_fwd"]),
+                                                                ("bwd", dom["ms_bwd"])) if v},
                             "flop_per_launch": dom["flop_per_launch"],
                             "peak_source": dom["peak_source"],
                             "frac_of_sustained": dom["frac_of_sustained"],
@@ -1065,7 +1080,7 @@ def run_section(args):
         model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=1), device=R.dev, seed=0)
         grp = model.model.layers[0].mlp.gate_proj.lora_group
         dom = time_gate_up_gemm(grp, args.batch * (args.seq or QLORA_SEQ), R.dev,
-                                reps=max(args.steps, 1))
+                                reps=max(args.steps, 1), recompute=bool(args.recompute))
         res = {"metric": "gate/up GEMM + SwiGLU epilogue TFLOP/s", "value": dom["achieved"],
                "unit": "TFLOP/s", "dtype": "bf16", **dom}
     else:
@@ -1104,8 +1119,9 @@ def main():
     ap.add_argument("--attention", default="sdpa", choices=["sdpa", "soup"],
                     help="step/qlora: transformers' SDPA (cuDNN; default) or this library's tcgen05 "
                          "flash attention")
-    ap.add_argument("--no-recompute", action="store_true",
-                    help="step/qlora: keep MLP activations instead of recomputing gate/up in backward")
+    ap.add_argument("--recompute", action="store_true",
+                    help="step/qlora: recompute gate/up in the MLP backward, as the reference does "
+                         "(default: keep [g | u] from the forward; same results, more memory)")
     ap.add_argument("--profile", action="store_true",
                     help="step/qlora: after the timed region, print a per-kernel device-time table "
                          "of two steps (torch.profiler, CUDA activity) to stderr")

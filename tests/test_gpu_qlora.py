@@ -310,6 +310,34 @@ def test_grouped_projections_match_separate_modules(recompute, monkeypatch):
             assert cosine(p1[n].grad, p.grad) > 0.99, n
 
 
+def test_mlp_recompute_and_kept_activations_give_identical_gradients(monkeypatch):
+    # the reference recomputes gate/up in the MLP backward (swiglu.py:197-214); keeping
+    # [g | u] from the forward instead runs the same kernels on the same inputs, so the
+    # loss and every LoRA gradient must agree bit for bit
+    from auspex_soup_demo_b200.kernels import make_triton_chunked_loss_function
+    from auspex_soup_demo_b200.kernels import swiglu as sw
+
+    apply()
+    g = torch.Generator().manual_seed(12)
+    ids = torch.randint(0, 2048, (2, 160), generator=g).cuda()
+    labels = qlora.causal_labels(ids)
+    fn = make_triton_chunked_loss_function()
+    out = {}
+    for group in (True, False):
+        for recompute in (True, False):
+            monkeypatch.setattr(sw, "RECOMPUTE", recompute)
+            model = _small_model_grouped(9, group)
+            model.train()
+            out[(group, recompute)] = _grads(model, ids, labels, fn)
+    for group in (True, False):
+        l1, g1 = out[(group, True)]
+        l2, g2 = out[(group, False)]
+        assert l1 == l2, (group, l1, l2)
+        assert g1.keys() == g2.keys()
+        for k in g1:
+            assert torch.equal(g1[k], g2[k]), (group, k)
+
+
 @pytest.mark.parametrize("n,n_scaled,wd", [(4096 * 37, 4096 * 5, 0.0), (100003, 77, 0.01)])
 def test_adamw_flat_matches_torch_adamw(n, n_scaled, wd):
     # the fused flat-buffer AdamW (vector path for n % 4 == 0, scalar otherwise)

@@ -1074,6 +1074,10 @@ def run_section(args):
     elif args.workload == "ce_vp":
         res = measure_ce_vp(args, R)
         res["dtype"] = "bf16"
+    elif args.workload == "attention":
+        att = measure_attention(args, R, args.batch, args.seq or QLORA_SEQ)
+        res = {"metric": "causal GQA attention forward + backward TFLOP/s",
+               "value": att["soup_fwd_bwd"]["tflops"], "unit": "TFLOP/s", "dtype": "bf16", **att}
     elif args.workload == "gateup":
         from auspex_soup_demo_b200 import qlora
 
@@ -1101,11 +1105,13 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="default line: skip the nested ce / mem_ops / ce_vp / qlora_s512 results")
     ap.add_argument("--workload", default="step",
-                    choices=["step", "qlora", "ce", "rmsnorm", "swiglu", "rope", "ce_vp", "gateup"],
+                    choices=["step", "qlora", "ce", "rmsnorm", "swiglu", "rope", "ce_vp", "gateup",
+                             "attention"],
                     help="step (default): the QLoRA train step with the other results nested; "
                          "qlora: the step alone; ce: the fused head CE; rmsnorm/swiglu/rope: one "
                          "memory-bound op's HBM GB/s; ce_vp: the vocab-parallel CE over all ranks; "
-                         "gateup: the step's gate/up GEMM with the SwiGLU epilogue alone")
+                         "gateup: the step's gate/up GEMM with the SwiGLU epilogue alone; attention: "
+                         "this library's attention against torch SDPA at the step's shape")
     ap.add_argument("--sustained-steps", type=int, default=500,
                     help="ce: extra back-to-back steps timed under the power cap (0: skip)")
     ap.add_argument("--tokens", type=int, default=65536, help="ce_vp: tokens per step")

@@ -245,8 +245,8 @@ int soup_attention_fwd(const void* q, const int64_t* q_strides, const void* k,
  * contiguous). P is recomputed from lse; dK / dV are accumulated per query
  * head in fp32 and summed over each KV head's group in a fixed order, dQ per
  * query tile over the key tiles (no atomics: reproducible). workspace: see
- * soup_attention_bwd_workspace_bytes (row dot products dout . out and the
- * fp32 per-head partials). */
+ * soup_attention_bwd_workspace_bytes (row dot products dout . out, the
+ * log-sum-exp in base-2 units, and the fp32 per-head partials). */
 size_t soup_attention_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq);
 int soup_attention_bwd(const void* q, const int64_t* q_strides, const void* k,
                        const int64_t* k_strides, const void* v, const int64_t* v_strides,

@@ -96,6 +96,8 @@ _SIGNATURES = {
     "soup_gemm_bf16_lora_swiglu": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64,
                                            c_vp, c_int, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64,
                                            c_vp]),
+    "soup_gemm_bf16_lora_dswiglu": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64,
+                                            c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp]),
     "soup_adamw_flat": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_f, c_f, c_f, c_f, c_f, c_vp,
                                 c_int, c_i64, c_f, c_vp]),
     "soup_gemm_bf16_lora": (c_int, [c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_vp, c_i64, c_vp, c_i64,

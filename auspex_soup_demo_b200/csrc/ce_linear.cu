@@ -363,6 +363,103 @@ struct EpiSwiGLU {
   }
 };
 
+// SwiGLU backward in the epilogue of the down projection's input-gradient GEMM:
+// the accumulator is dh [M, N] (N = the intermediate size), which is rounded to
+// bf16 as a plain GEMM output would be; with g and u read from y in the
+// interleaved layout of EpiSwiGLU (intermediate column c: g at column
+// 256 (c / 128) + c % 128 of y, u 128 further), dg and du overwrite g and u in y.
+// Every (row, column) pair is read and written by one lane, so the update is in
+// place. Results equal the unfused GEMM + SwiGLU backward kernels bit for bit.
+template <int BN>
+struct EpiDSwiGLU {
+  struct Params {
+    bf16* y;  // [M, 2N]: [g | u] in, [dg | du] out
+    int64_t ldy;
+    int M, N;
+  };
+  // Lane l handles rows 8 i + l / 4 (i = 0..3), columns 8 (l % 4) .. + 7 of a 32 x 32
+  // chunk: g / u are read and dg / du written with 16-byte accesses in that
+  // layout, and only dh (one row per lane from TMEM) goes through shared memory.
+  // The g / u of a warp's next chunk are in flight while it works on this one.
+  struct Carry {
+    uint4 g[4], u[4];
+  };
+  static __device__ __forceinline__ int gcol_of(int icol) { return (icol >> 7) * 256 + (icol & 127); }
+  static __device__ __forceinline__ void load(const Params& p, int lane, int row0, int icol, Carry& c) {
+    if (icol >= p.N) return;
+    const bf16* base = p.y + gcol_of(icol) + 8 * (lane & 3);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int grow = row0 + 8 * i + (lane >> 2);
+      const bool in = grow < p.M;
+      c.g[i] = in ? *reinterpret_cast<const uint4*>(base + (int64_t)grow * p.ldy) : make_uint4(0, 0, 0, 0);
+      c.u[i] = in ? *reinterpret_cast<const uint4*>(base + (int64_t)grow * p.ldy + 128)
+                  : make_uint4(0, 0, 0, 0);
+    }
+  }
+  static __device__ __forceinline__ void prefetch(const Params& p, int row_base, int nt, int quarter,
+                                                  int lane, int group, int ngroups, Carry& c) {
+    load(p, lane, row_base + quarter * 32, nt * BN + group * (BN / 32 / ngroups) * 32, c);
+  }
+  static __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 t = __bfloat1622float2(h[q]);
+      f[2 * q] = t.x;
+      f[2 * q + 1] = t.y;
+    }
+  }
+  static __device__ __forceinline__ void tile(const Params& p, const CUtensorMap* tmc, int row_base, int nt,
+                                              int ks, int quarter, int lane, uint32_t taddr,
+                                              uint8_t* stage, int group, int ngroups, Carry& carry) {
+    const int row0 = row_base + quarter * 32;
+    const int nch = BN / 32 / ngroups;
+    const int c8 = lane & 3;
+#pragma unroll 1
+    for (int cc = group * nch; cc < (group + 1) * nch; ++cc) {
+      const int icol = nt * BN + cc * 32;
+      float d[32];
+      tmem_ld32(taddr + cc * 32, d);
+      if (icol >= p.N) continue;
+      // dh rounded to bf16, as the unfused GEMM would store it
+#pragma unroll
+      for (int j = 0; j < 32; ++j) d[j] = __bfloat162float(__float2bfloat16_rn(d[j]));
+      stage_row(stage, lane, d, 1.f);
+      __syncwarp();
+      uint4 og[4], ou[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 8 * i + (lane >> 2);
+        const float4 a = *reinterpret_cast<const float4*>(stage + stage_off(r, 2 * c8));
+        const float4 b = *reinterpret_cast<const float4*>(stage + stage_off(r, 2 * c8 + 1));
+        const float dv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        float gv[8], uv[8];
+        unpack8(carry.g[i], gv);
+        unpack8(carry.u[i], uv);
+        float dg[8], du[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) swiglu_bwd_f(dv[q], gv[q], uv[q], dg[q], du[q]);
+        og[i] = make_uint4(pack_bf16x2(dg[0], dg[1]), pack_bf16x2(dg[2], dg[3]),
+                           pack_bf16x2(dg[4], dg[5]), pack_bf16x2(dg[6], dg[7]));
+        ou[i] = make_uint4(pack_bf16x2(du[0], du[1]), pack_bf16x2(du[2], du[3]),
+                           pack_bf16x2(du[4], du[5]), pack_bf16x2(du[6], du[7]));
+      }
+      __syncwarp();  // the stage is rewritten by the next chunk
+      if (cc + 1 < (group + 1) * nch) load(p, lane, row0, icol + 32, carry);
+      bf16* base = p.y + gcol_of(icol) + 8 * c8;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int grow = row0 + 8 * i + (lane >> 2);
+        if (grow < p.M) {
+          *reinterpret_cast<uint4*>(base + (int64_t)grow * p.ldy) = og[i];
+          *reinterpret_cast<uint4*>(base + (int64_t)grow * p.ldy + 128) = ou[i];
+        }
+      }
+    }
+  }
+};
+
 // Logits epilogue of the CE forward: online-softmax state per (row, tile),
 // target logit capture, bf16 logits store.
 // Shifted exponentials. With `shift` set, the tile stores E = exp(z - c_row)
@@ -1737,6 +1834,47 @@ int soup_gemm_bf16_lora(const void* a, int64_t lda, int a_mn_major, const void* 
   if (!a_mn_major && b_mn_major) return launch_gemm<false, true, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
   if (a_mn_major && !b_mn_major) return launch_gemm<true, false, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
   return launch_gemm<true, true, E>(ma, mb, ma2, mb2, mc, sc, ep, stream);
+}
+
+int soup_gemm_bf16_lora_dswiglu(const void* a, int64_t lda, const void* b, int64_t ldb,
+                                const void* a2, int64_t lda2, const void* b2, int64_t ldb2,
+                                int64_t r, void* y, int64_t ldy, int64_t m, int64_t inter,
+                                int64_t k, void* stream_) {
+  if (!a || !b || !y || m <= 0 || inter <= 0 || k <= 0 || m > (1 << 30) || inter > (1 << 29) ||
+      k > (1 << 30) || r < 0 || r > 4096 || (r > 0 && (!a2 || !b2))) {
+    set_last_error("soup_gemm_bf16_lora_dswiglu: bad arguments");
+    return SOUP_ERR_INVALID;
+  }
+  if (inter % (kBN / 2) != 0) {
+    set_last_error("soup_gemm_bf16_lora_dswiglu: the intermediate size must be a multiple of 128");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  if (lda < k || ldb < inter || ldy < 2 * inter || (r > 0 && (lda2 < r || ldb2 < inter))) {
+    set_last_error("soup_gemm_bf16_lora_dswiglu: leading dimension too small");
+    return SOUP_ERR_INVALID;
+  }
+  if (!tma_ok(a, lda) || !tma_ok(b, ldb) || (r > 0 && (!tma_ok(a2, lda2) || !tma_ok(b2, ldb2))) ||
+      !aligned16(y) || (ldy * 2) % 16 != 0) {
+    set_last_error("soup_gemm_bf16_lora_dswiglu: operands need 16-byte aligned rows");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  CUtensorMap ma, mb, ma2, mb2;
+  int rc;
+  // dh = a [m, k] b [k, inter] (+ a2 [m, r] b2 [r, inter]): B operands MN-major
+  if ((rc = make_operand_map(&ma, a, false, m, k, lda, BM))) return rc;
+  if ((rc = make_operand_map(&mb, b, true, inter, k, ldb, b_box_rows()))) return rc;
+  if (r > 0) {
+    if ((rc = make_operand_map(&ma2, a2, false, m, r, lda2, BM))) return rc;
+    if ((rc = make_operand_map(&mb2, b2, true, inter, r, ldb2, b_box_rows()))) return rc;
+  } else {
+    ma2 = ma;
+    mb2 = mb;
+  }
+  EpiDSwiGLU<kBN>::Params ep{static_cast<bf16*>(y), ldy, (int)m, (int)inter};
+  const int mt = m_tiles(m), nt = (int)((inter + kBN - 1) / kBN);
+  const int kb1 = (int)((k + BK - 1) / BK), kb2 = (int)((r + BK - 1) / BK);
+  Sched sc{mt, nt, 1, kb1 + kb2, nt > mt ? 0 : 1, kb2};
+  return launch_gemm<false, true, EpiDSwiGLU<kBN>>(ma, mb, ma2, mb2, ma, sc, ep, as_stream(stream_));
 }
 
 int soup_gemm_wait_expiry_check(const void* a, const void* b, void* c, int64_t m, int64_t n,

@@ -112,7 +112,8 @@ def patch_qwen2_mlp():
         if (group is not None and group.kind == "gate_up" and group.members[0] is self.gate_proj
                 and group.members[1] is self.up_proj and group.usable(x)):
             # gate/up as one GEMM feeding the fused SwiGLU; same recompute policy
-            return self.down_proj(group.swiglu(x, recompute))
+            # (without recompute the SwiGLU backward joins down_proj's dX GEMM)
+            return group.mlp(x, self.down_proj, recompute)
         if not recompute:
             return self.down_proj(fast_swiglu(self.gate_proj(x), self.up_proj(x)))
 

@@ -475,6 +475,16 @@ class LoRAProjectionGroup:
         recompute of the MLP, solution/kernels/swiglu.py:197-214)."""
         return _LoRAGateUpFn.apply(x, self, bool(recompute), *self.params())
 
+    def mlp(self, x: torch.Tensor, down, recompute: bool) -> torch.Tensor:
+        """down(silu(gate(x)) * up(x)) for a gate/up group; one Function with the
+        SwiGLU backward fused into down's input-gradient GEMM (FUSE_MLP_BACKWARD)
+        when the activations are kept, bf16, and down is an ungrouped LoRA linear."""
+        if (FUSE_MLP_BACKWARD and not recompute and self.interleaved
+                and isinstance(down, _LoRABase) and down.lora_group is None
+                and x.dtype == torch.bfloat16 and down.in_features == self.outs[0]):
+            return _LoRAMLPFn.apply(x, self, down, down.lora_A, down.lora_B, *self.params())
+        return down(self.swiglu(x, recompute))
+
 
 def _group_gemm(group: LoRAProjectionGroup, x2: torch.Tensor, w: torch.Tensor, As16, Bblk,
                 xa: Optional[torch.Tensor] = None):
@@ -599,6 +609,17 @@ def swiglu_gemm(x2, w, xa, Bblk, bias, mode: int, h, y=None):
               _lib.stream_of(x2))
 
 
+def dswiglu_gemm(d2, w, dxa, As16, y):
+    """soup_gemm_bf16_lora_dswiglu: dh = d2 W + dxa As (the down projection's input
+    gradient) with the SwiGLU backward in the epilogue: [g | u] in y (the
+    interleaved layout of swiglu_gemm) is overwritten by [dg | du]."""
+    m, k = d2.shape
+    inter = w.shape[1]
+    _lib.call("soup_gemm_bf16_lora_dswiglu", d2.device, d2.data_ptr(), d2.stride(0), w.data_ptr(),
+              w.stride(0), dxa.data_ptr(), dxa.stride(0), As16.data_ptr(), As16.stride(0),
+              dxa.shape[1], y.data_ptr(), y.stride(0), m, inter, k, _lib.stream_of(d2))
+
+
 def _swiglu_fused_ok(group, x2, w, xa, Bblk, bias, *outs) -> bool:
     return (group.interleaved and _fused_ok(x2.shape[1], x2, w, xa, Bblk,
                                             bias.view(1, -1) if bias is not None else None, *outs))
@@ -679,6 +700,105 @@ class _LoRAGateUpFn(torch.autograd.Function):
         if dx is not None:
             dx = dx.view(*ctx.lead, x2.shape[1])
         return (dx, None, None, *grads)
+
+
+#: Run the MLP (gate/up + SwiGLU + down_proj) as one autograd Function whose
+#: backward puts the SwiGLU backward into the epilogue of the down projection's
+#: input-gradient GEMM, when the MLP keeps [g | u] (no recompute). False keeps
+#: two Functions (down_proj's backward writes dh, the gate/up backward runs the
+#: SwiGLU backward as an elementwise pass); results are bit-identical.
+FUSE_MLP_BACKWARD = True
+
+
+class _LoRAMLPFn(torch.autograd.Function):
+    """out = down(silu(g) u) with [g | u] = the gate/up group GEMM of x and down a
+    LoRA linear, as one Function (see FUSE_MLP_BACKWARD).
+
+    Forward: the gate/up GEMM with the SwiGLU epilogue writes h and keeps [g | u]
+    (soup_gemm_bf16_lora_swiglu), then down's GEMM as in _LoRALinearFn. Backward:
+    dxa_down = dout B_down, then [dg | du] = SwiGLU'(dout W_down + dxa_down As_down)
+    in place of [g | u] (soup_gemm_bf16_lora_dswiglu: dh never reaches memory),
+    down's LoRA gradients, then the gate/up group backward.
+    """
+
+    @staticmethod
+    def forward(ctx, x, group, down, A_d, B_d, *params):
+        k = group.in_features
+        inter = group.outs[0]
+        x2 = x.reshape(-1, k)
+        m = x2.shape[0]
+        w = group.base_weight(x.dtype)
+        As16, Bblk = group.factors(x.dtype)
+        bias = None if group.bias is None else group.bias.to(x2.dtype)
+        h = torch.empty(m, inter, device=x.device, dtype=x.dtype)
+        y = torch.empty(m, group.n_total, device=x.device, dtype=x.dtype)
+        xa = x2 @ As16.t()
+        if _swiglu_fused_ok(group, x2, w, xa, Bblk, bias, h, y):
+            swiglu_gemm(x2, w, xa, Bblk, bias, 0, h, y)
+        else:
+            from .kernels.swiglu import swiglu_forward
+
+            y, _ = _group_gemm(group, x2, w, As16, Bblk, xa)
+            g, u = _gu_views(group, y)
+            swiglu_forward(g, u, out=h.view(g.shape[0], g.shape[1]))
+        # down: as _LoRALinearFn.forward
+        as16_d, b16_d = down.lora_As16, down.lora_B16
+        if as16_d is None or as16_d.dtype != x.dtype:
+            as16_d = (down.lora_A.detach() * down.scaling).to(x.dtype)
+            b16_d = down.lora_B.detach().to(x.dtype)
+        bias_d = None if down.bias is None else down.bias.to(x.dtype)
+        w_d = down.base_weight(x.dtype)
+        xa_d = h @ as16_d.t()
+        n_out = w_d.shape[0]
+        if _fused_ok(inter, h, w_d, xa_d, b16_d, bias_d.view(1, -1) if bias_d is not None else None):
+            out = lora_gemm(h, w_d, False, xa_d, b16_d,
+                            torch.empty(m, n_out, device=x.device, dtype=x.dtype), bias_d)
+        else:
+            out = F.linear(h, w_d, bias_d)
+            out.addmm_(xa_d, b16_d.t())
+        ctx.save_for_backward(x2, xa, As16, Bblk, y, h, xa_d, as16_d, b16_d)
+        ctx.w = _keep(w)
+        ctx.w_d = _keep(w_d)
+        ctx.group = group
+        ctx.down = down
+        ctx.lead = x.shape[:-1]
+        return out.view(*x.shape[:-1], n_out)
+
+    @staticmethod
+    def backward(ctx, dout):
+        from .kernels.swiglu import swiglu_backward
+
+        x2, xa, As16, Bblk, y, h, xa_d, as16_d, b16_d = ctx.saved_tensors
+        group, down = ctx.group, ctx.down
+        d2 = dout.reshape(-1, dout.shape[-1])
+        if d2.stride(1) != 1 or d2.stride(0) != d2.shape[1]:
+            d2 = d2.contiguous()
+        if d2.dtype != x2.dtype:
+            d2 = d2.to(x2.dtype)
+        w_d = ctx.w_d if ctx.w_d is not None and ctx.w_d.dtype == x2.dtype else down.base_weight(x2.dtype)
+        w = ctx.w if ctx.w is not None and ctx.w.dtype == x2.dtype else group.base_weight(x2.dtype)
+        ctx.w = ctx.w_d = None
+        dxa_d = d2 @ b16_d
+        if _fused_ok(d2.shape[1], d2, w_d, dxa_d, as16_d, y):
+            dswiglu_gemm(d2, w_d, dxa_d, as16_d, y)
+            dy = y  # [dg | du] over [g | u]
+        else:
+            dh = d2 @ w_d
+            dh.addmm_(dxa_d, as16_d)
+            dy = torch.empty_like(y)
+            g, u = _gu_views(group, y)
+            dg, du = _gu_views(group, dy)
+            swiglu_backward(dh.view(g.shape[0], g.shape[1]), g, u, dg=dg, du=du)
+        gA_d = gB_d = None
+        if ctx.needs_input_grad[3]:
+            gA_d = _accumulate_grad(down.lora_A, dxa_d.t(), h, down.scaling)
+        if ctx.needs_input_grad[4]:
+            gB_d = _accumulate_grad(down.lora_B, d2.t(), xa_d, 1.0)
+        dx, grads = _group_backward(group, dy, x2, xa, w, As16, Bblk, ctx.needs_input_grad[0],
+                                    ctx.needs_input_grad[5:])
+        if dx is not None:
+            dx = dx.view(*ctx.lead, x2.shape[1])
+        return (dx, None, None, gA_d, gB_d, *grads)
 
 
 def group_projections(model, kinds=("qkv", "gate_up")):

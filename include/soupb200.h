@@ -326,6 +326,22 @@ int soup_gemm_bf16_lora_swiglu(const void* a, int64_t lda, const void* b, int64_
                                const void* bias, int mode, void* h, int64_t ldh, void* y, int64_t ldy,
                                int64_t m, int64_t inter, int64_t k, void* stream);
 
+/* The down projection's input gradient with the SwiGLU backward in its epilogue:
+ * dh = a [m, k] b [k, inter] (+ a2 [m, r] b2 [r, inter]; b and b2 row-major, i.e.
+ * the down weight [k, inter] and the scaled LoRA A [r, inter] as stored) is
+ * rounded to bf16 as a plain GEMM output would be, and with g, u read from y
+ * [m, 2*inter] (row stride ldy, the interleaved order of
+ * soup_gemm_bf16_lora_swiglu's B rows) dg and du overwrite them in y: the
+ * output of this call is [dg | du] in place of [g | u] (bit-identical to
+ * soup_gemm_bf16_lora + soup_swiglu_bwd). inter % 128 == 0; rows 16-byte
+ * aligned. Replaces the reference MLP's down_proj backward plus its SwiGLU
+ * backward kernel (solution/kernels/swiglu.py:60-95, 197-214), where dh makes a
+ * round trip through memory. */
+int soup_gemm_bf16_lora_dswiglu(const void* a, int64_t lda, const void* b, int64_t ldb,
+                                const void* a2, int64_t lda2, const void* b2, int64_t ldb2,
+                                int64_t r, void* y, int64_t ldy, int64_t m, int64_t inter,
+                                int64_t k, void* stream);
+
 /* ---- AdamW over flat fp32 buffers (the QLoRA step's optimiser) ------------
  * One pass over n elements: param, exp_avg, exp_avg_sq updated in place from
  * grad with torch.optim.AdamW's decoupled weight decay; `step` is a device

@@ -246,3 +246,40 @@ def test_swiglu_epilogue_gemm_equals_gemm_plus_swiglu_kernels(m, inter, k, with_
     assert torch.equal(h, h_ref) and torch.equal(h_only, h_ref)
     assert torch.equal(dy, dy_ref)
     assert _lib.device_error(torch.device("cuda")) == 0
+
+
+@pytest.mark.parametrize("m,inter,k,r", [(300, 640, 1536, 16), (2048, 8960, 1536, 16), (129, 256, 64, 0)])
+def test_dswiglu_epilogue_gemm_equals_gemm_plus_swiglu_backward(m, inter, k, r):
+    # soup_gemm_bf16_lora_dswiglu (the down projection's dX GEMM dh = d W + dxa As
+    # with the SwiGLU backward in its epilogue, [dg | du] over [g | u] in place)
+    # against the plain dX GEMM followed by the SwiGLU backward kernel: bit-identical
+    from auspex_soup_demo_b200 import qlora
+    from auspex_soup_demo_b200.kernels.swiglu import swiglu_backward
+
+    g = torch.Generator(device="cuda").manual_seed(m + inter + r)
+    d = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (0.05 * torch.randn(k, inter, device="cuda", generator=g)).bfloat16()  # down weight [out, in]
+    rr = max(r, 1)
+    dxa = torch.randn(m, rr, device="cuda", generator=g).bfloat16()[:, :r].contiguous() if r else None
+    As = (0.05 * torch.randn(rr, inter, device="cuda", generator=g)).bfloat16()[:r].contiguous() if r else None
+    y = torch.randn(m, 2 * inter, device="cuda", generator=g).bfloat16()  # [g | u], interleaved blocks
+    if r:
+        dh = qlora.lora_gemm(d, w, True, dxa, As, torch.empty(m, inter, device="cuda", dtype=torch.bfloat16))
+    else:
+        dh = (d.float() @ w.float()).bfloat16()
+        # the dX GEMM alone, through the library (no rank term)
+        _lib.call("soup_gemm_bf16", d.device, d.data_ptr(), k, 0, w.data_ptr(), inter, 1, dh.data_ptr(),
+                  inter, _lib.dtype_code(dh.dtype), m, inter, k, 1.0, 0, _lib.stream_of(d))
+    y2 = y.view(-1, 256)
+    dy_ref = torch.empty_like(y)
+    d2 = dy_ref.view(-1, 256)
+    swiglu_backward(dh.view(-1, 128), y2[:, :128], y2[:, 128:], dg=d2[:, :128], du=d2[:, 128:])
+    yy = y.clone()
+    if r:
+        qlora.dswiglu_gemm(d, w, dxa, As, yy)
+    else:
+        _lib.call("soup_gemm_bf16_lora_dswiglu", d.device, d.data_ptr(), k, w.data_ptr(), inter, None, 0,
+                  None, 0, 0, yy.data_ptr(), 2 * inter, m, inter, k, _lib.stream_of(d))
+    torch.cuda.synchronize()
+    assert _lib.device_error(torch.device("cuda")) == 0
+    assert torch.equal(yy, dy_ref)

@@ -338,6 +338,32 @@ def test_mlp_recompute_and_kept_activations_give_identical_gradients(monkeypatch
             assert torch.equal(g1[k], g2[k]), (group, k)
 
 
+def test_fused_mlp_backward_gives_identical_gradients(monkeypatch):
+    # the MLP as one Function (SwiGLU backward in the down projection's dX GEMM
+    # epilogue, [dg | du] written over the kept [g | u]) against gate/up and down
+    # as two Functions with the SwiGLU backward as an elementwise pass
+    from auspex_soup_demo_b200.kernels import make_triton_chunked_loss_function
+    from auspex_soup_demo_b200.kernels import swiglu as sw
+
+    apply()
+    monkeypatch.setattr(sw, "RECOMPUTE", False)
+    g = torch.Generator().manual_seed(13)
+    ids = torch.randint(0, 2048, (2, 200), generator=g).cuda()
+    labels = qlora.causal_labels(ids)
+    fn = make_triton_chunked_loss_function()
+    out = {}
+    for fused in (True, False):
+        monkeypatch.setattr(qlora, "FUSE_MLP_BACKWARD", fused)
+        model = _small_model_grouped(10, True)
+        model.train()
+        out[fused] = _grads(model, ids, labels, fn)
+    (l1, g1), (l2, g2) = out[True], out[False]
+    assert l1 == l2, (l1, l2)
+    assert g1.keys() == g2.keys()
+    for k in g1:
+        assert torch.equal(g1[k], g2[k]), k
+
+
 @pytest.mark.parametrize("n,n_scaled,wd", [(4096 * 37, 4096 * 5, 0.0), (100003, 77, 0.01)])
 def test_adamw_flat_matches_torch_adamw(n, n_scaled, wd):
     # the fused flat-buffer AdamW (vector path for n % 4 == 0, scalar otherwise)

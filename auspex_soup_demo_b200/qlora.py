@@ -524,10 +524,12 @@ def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tens
             for j in range(len(group.members))):
         torch.addmm(group.gradA, dxa.t(), x2, alpha=group.scaling, out_dtype=torch.float32, out=group.gradA)
         gA_done = True
-    # interleaved rows: one product G = dy^T xa [N, R], member j's gradient is its
-    # row blocks and rank columns of G
+    # one product G = dy^T xa [N, R] reads dy once for all members' B gradients
+    # (member j's gradient is its output rows - row blocks when interleaved - and
+    # rank columns of G); one accumulating product per member would re-read dy and
+    # costs cuBLAS ~14 us each at 8192 tokens even for the 4 MB k / v gradients
     G = None
-    if group.interleaved and any(need_params[2 * j + 1] for j in range(len(group.members))):
+    if any(need_params[2 * j + 1] for j in range(len(group.members))):
         G = torch.mm(dy.t(), xa, out_dtype=torch.float32)
     for j, mem in enumerate(group.members):
         r0, r1 = group.rank_off[j], group.rank_off[j + 1]
@@ -537,7 +539,10 @@ def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tens
             gA = _accumulate_grad(mem.lora_A, dxa[:, r0:r1].t(), x2, mem.scaling)
         if need_params[2 * j + 1]:
             if G is not None:
-                part = group._il_view(G, group.r_total)[:, j, :, r0:r1]
+                if group.interleaved:
+                    part = group._il_view(G, group.r_total)[:, j, :, r0:r1]
+                else:
+                    part = G[o0:o1, r0:r1]
                 g = mem.lora_B.grad
                 if g is not None and g.is_cuda and g.dtype == torch.float32 and g.is_contiguous():
                     g.view(part.shape).add_(part)

@@ -638,9 +638,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 }
 
 // ------------------------------------------------------------ backward ----
-// D[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d] (fp32), one warp per row,
-// and nl2[b, h, q] = -lse[b, h, q] * log2(e) (the exponent offset of P in base
-// 2); rows padded like lse ([B, H, S_pad]). dO and O are [B, S, H, D] contiguous.
+// D[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d] (fp32) and nl2[b, h, q] =
+// -lse[b, h, q] * log2(e) (the exponent offset of P in base 2); rows padded
+// like lse ([B, H, S_pad]). dO and O are [B, S, H, D] contiguous. Sixteen lanes
+// per row (16 bytes each), rows taken in the output's (b, h, q) order so the
+// stores are contiguous, four rows per half-warp with all loads issued first.
+constexpr int kDotRows = 4;
 __global__ void __launch_bounds__(256) attn_bwd_dot_kernel(const bf16* __restrict__ dO,
                                                            const bf16* __restrict__ O,
                                                            const float* __restrict__ lse, int B,
@@ -648,28 +651,45 @@ __global__ void __launch_bounds__(256) attn_bwd_dot_kernel(const bf16* __restric
                                                            float* __restrict__ nl2) {
   pdl_wait();
   pdl_trigger();
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);  // (b, q, h) row-major
-  const int lane = threadIdx.x & 31;
-  if (row >= (int64_t)B * S * H) return;
-  const uint2 a = *reinterpret_cast<const uint2*>(dO + row * kHeadDim + lane * 4);
-  const uint2 c = *reinterpret_cast<const uint2*>(O + row * kHeadDim + lane * 4);
-  const __nv_bfloat162* ap = reinterpret_cast<const __nv_bfloat162*>(&a);
-  const __nv_bfloat162* cp = reinterpret_cast<const __nv_bfloat162*>(&c);
-  float acc = 0.f;
+  const int64_t nrows = (int64_t)B * H * S;
+  const int sub = threadIdx.x & 15;
+  const int64_t half = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int64_t nhalves = ((int64_t)gridDim.x * blockDim.x) >> 4;
+  const int64_t s_pad = (int64_t)(S + kTile - 1) / kTile * kTile;
+  for (int64_t base = half * kDotRows; base < nrows; base += nhalves * kDotRows) {
+    uint4 a[kDotRows], c[kDotRows];
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const float2 x = __bfloat1622float2(ap[i]), y = __bfloat1622float2(cp[i]);
-    acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
-  }
-  acc = warp_sum(acc);
-  if (lane == 0) {
-    const int h = (int)(row % H);
-    const int64_t bq = row / H;
-    const int q = (int)(bq % S), b = (int)(bq / S);
-    const int64_t s_pad = (int64_t)(S + kTile - 1) / kTile * kTile;
-    const int64_t v = ((int64_t)b * H + h) * s_pad + q;
-    Dv[v] = acc;
-    nl2[v] = -lse[v] * kLog2e;
+    for (int u = 0; u < kDotRows; ++u) {
+      const int64_t i = base + u;  // (b, h, q) row-major
+      if (i < nrows) {
+        const int q = (int)(i % S);
+        const int64_t bh = i / S;
+        const int h = (int)(bh % H), b = (int)(bh / H);
+        const int64_t row = ((int64_t)b * S + q) * H + h;
+        a[u] = *reinterpret_cast<const uint4*>(dO + row * kHeadDim + sub * 8);
+        c[u] = *reinterpret_cast<const uint4*>(O + row * kHeadDim + sub * 8);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kDotRows; ++u) {
+      const int64_t i = base + u;
+      const __nv_bfloat162* ap = reinterpret_cast<const __nv_bfloat162*>(&a[u]);
+      const __nv_bfloat162* cp = reinterpret_cast<const __nv_bfloat162*>(&c[u]);
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 x = __bfloat1622float2(ap[e]), y = __bfloat1622float2(cp[e]);
+        acc = fmaf(x.x, y.x, fmaf(x.y, y.y, acc));
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (sub == 0 && i < nrows) {
+        const int q = (int)(i % S);
+        const int64_t v = (i / S) * s_pad + q;
+        Dv[v] = acc;
+        nl2[v] = -lse[v] * kLog2e;
+      }
+    }
   }
 }
 
@@ -1349,6 +1369,7 @@ __global__ void __launch_bounds__(256) attn_bwd_group_sum_kernel(const float* __
     const int s = (int)(t % S);
     const int b = (int)(t / S);
     float4 ak = make_float4(0.f, 0.f, 0.f, 0.f), av = ak;
+#pragma unroll 6
     for (int g = 0; g < rep; ++g) {
       const int64_t src = (((int64_t)b * H + hk * rep + g) * S + s) * kHeadDim + d4 * 4;
       const float4 x = *reinterpret_cast<const float4*>(dk_part + src);
@@ -1539,7 +1560,9 @@ int soup_attention_bwd(const void* q, const int64_t* q_strides, const void* k,
   cudaStream_t st = as_stream(stream);
   const int B = (int)batch, H = (int)heads, Hk = (int)kv_heads, S = (int)seq;
   const int64_t rows = (int64_t)B * S * H;
-  if ((rc = cuda_status(launch_pdl(attn_bwd_dot_kernel, dim3((unsigned)((rows + 7) / 8)), dim3(256),
+  int dot_blocks = (int)((rows + 16 * kDotRows - 1) / (16 * kDotRows));  // 16 half-warps per block
+  if (dot_blocks > 16 * num_sms()) dot_blocks = 16 * num_sms();
+  if ((rc = cuda_status(launch_pdl(attn_bwd_dot_kernel, dim3((unsigned)dot_blocks), dim3(256),
                                    0, st, static_cast<const bf16*>(dout),
                                    static_cast<const bf16*>(out), lse, B, H, S, dvec, nl2))))
     return rc;

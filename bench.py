@@ -430,6 +430,61 @@ def measure_qlora(args, R: Ranks, batch: int, seq: int, with_extras: bool = True
     return res
 
 
+def time_mlp_backward(m: int, dev, reps: int = 20, hidden: int = 1536, inter: int = 8960,
+                      r: int = 16):
+    """The MLP backward's first step at m tokens (Qwen2.5-1.5B shapes): down_proj's
+    input-gradient GEMM dh = dout W + dxa As with the SwiGLU backward in its
+    epilogue ([dg | du] written over [g | u], soup_gemm_bf16_lora_dswiglu) against
+    the same GEMM storing dh (soup_gemm_bf16_lora) followed by the elementwise
+    SwiGLU backward. CUDA events, reps back-to-back launches each."""
+    from auspex_soup_demo_b200 import qlora
+    from auspex_soup_demo_b200.kernels.swiglu import swiglu_backward
+
+    g = torch.Generator(device=dev).manual_seed(6)
+    d = torch.randn(m, hidden, device=dev, generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(hidden, inter, device=dev, generator=g)).to(torch.bfloat16)
+    dxa = torch.randn(m, r, device=dev, generator=g).to(torch.bfloat16)
+    As = (0.02 * torch.randn(r, inter, device=dev, generator=g)).to(torch.bfloat16)
+    y = torch.randn(m, 2 * inter, device=dev, generator=g).to(torch.bfloat16)
+    dh = torch.empty(m, inter, device=dev, dtype=torch.bfloat16)
+    dy = torch.empty_like(y)
+    y2, d2 = y.view(-1, 256), dy.view(-1, 256)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    t_gemm = timed(lambda: qlora.lora_gemm(d, w, True, dxa, As, dh))
+    t_ew = timed(lambda: swiglu_backward(dh.view(-1, 128), y2[:, :128], y2[:, 128:],
+                                         dg=d2[:, :128], du=d2[:, 128:]))
+    yy = y.clone()
+    t_fused = timed(lambda: qlora.dswiglu_gemm(d, w, dxa, As, yy))
+    flop = 2.0 * m * inter * (hidden + r)
+    peak, _, src = _peaks()
+    sus_peak, sus_src = _sustained_peak()
+    return {"kernel": "soup::tc::gemm_pair_kernel<EpiDSwiGLU> (down dX + rank-16 k-block, SwiGLU "
+                      "backward in the epilogue, [dg | du] over [g | u])",
+            "shape": f"M {m} x N {inter} x K {hidden} + rank {r}",
+            "ms_fused": round(t_fused, 4), "ms_unfused_gemm": round(t_gemm, 4),
+            "ms_unfused_swiglu_bwd": round(t_ew, 4),
+            "saving_ms": round(t_gemm + t_ew - t_fused, 4),
+            "achieved": round(flop / (t_fused * 1e-3) / 1e12, 1), "peak": peak,
+            "frac": round(flop / (t_fused * 1e-3) / 1e12 / peak, 4),
+            "frac_of_sustained": round(flop / (t_fused * 1e-3) / 1e12 / sus_peak, 4),
+            "peak_source": f"{src} bf16_tflops (burst); sustained {sus_src}",
+            "epilogue_bytes": 4 * m * inter * 2}
+
+
 def time_gate_up_gemm(group, m: int, dev, reps: int = 20, recompute: bool = False):
     """CUDA-event duration of the gate/up GEMM + SwiGLU epilogue launch at m tokens,
     the QLoRA step's largest kernel, in the modes the step runs: the forward that
@@ -1078,6 +1133,10 @@ def run_section(args):
         att = measure_attention(args, R, args.batch, args.seq or QLORA_SEQ)
         res = {"metric": "causal GQA attention forward + backward TFLOP/s",
                "value": att["soup_fwd_bwd"]["tflops"], "unit": "TFLOP/s", "dtype": "bf16", **att}
+    elif args.workload == "mlp_bwd":
+        mb = time_mlp_backward(args.batch * (args.seq or QLORA_SEQ), R.dev, reps=max(args.steps, 1))
+        res = {"metric": "down dX GEMM + SwiGLU backward epilogue TFLOP/s", "value": mb["achieved"],
+               "unit": "TFLOP/s", "dtype": "bf16", **mb}
     elif args.workload == "gateup":
         from auspex_soup_demo_b200 import qlora
 
@@ -1106,12 +1165,14 @@ def main():
                     help="default line: skip the nested ce / mem_ops / ce_vp / qlora_s512 results")
     ap.add_argument("--workload", default="step",
                     choices=["step", "qlora", "ce", "rmsnorm", "swiglu", "rope", "ce_vp", "gateup",
-                             "attention"],
+                             "attention", "mlp_bwd"],
                     help="step (default): the QLoRA train step with the other results nested; "
                          "qlora: the step alone; ce: the fused head CE; rmsnorm/swiglu/rope: one "
                          "memory-bound op's HBM GB/s; ce_vp: the vocab-parallel CE over all ranks; "
                          "gateup: the step's gate/up GEMM with the SwiGLU epilogue alone; attention: "
-                         "this library's attention against torch SDPA at the step's shape")
+                         "this library's attention against torch SDPA at the step's shape; mlp_bwd: "
+                         "down_proj's dX GEMM with the SwiGLU backward in its epilogue against the "
+                         "unfused pair")
     ap.add_argument("--sustained-steps", type=int, default=500,
                     help="ce: extra back-to-back steps timed under the power cap (0: skip)")
     ap.add_argument("--tokens", type=int, default=65536, help="ce_vp: tokens per step")

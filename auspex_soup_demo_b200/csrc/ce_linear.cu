@@ -377,85 +377,91 @@ struct EpiDSwiGLU {
     int64_t ldy;
     int M, N;
   };
-  // Lane l handles rows 8 i + l / 4 (i = 0..3), columns 8 (l % 4) .. + 7 of a 32 x 32
-  // chunk: g / u are read and dg / du written with 16-byte accesses in that
-  // layout, and only dh (one row per lane from TMEM) goes through shared memory.
-  // The g / u of a warp's next chunk are in flight while it works on this one.
-  struct Carry {
-    uint4 g[4], u[4];
-  };
+  // A warp owns 32 accumulator rows (its TMEM lane quarter) x its group's columns,
+  // which lie in one interleave block of 128. Rows are handled in two halves of
+  // 16: dh of the half goes through the warp's staging block as bf16 (16 rows x
+  // 128 columns = 4 KB), then each lane takes 8 consecutive columns of a row, so
+  // every load / store instruction covers 2 rows x 256 contiguous bytes of g, u,
+  // dg and du (long DRAM bursts; the same rows' g and u are 128 columns apart).
+  static constexpr int kPass = 4;  // passes (2 rows each) whose loads are issued together
   static __device__ __forceinline__ int gcol_of(int icol) { return (icol >> 7) * 256 + (icol & 127); }
-  static __device__ __forceinline__ void load(const Params& p, int lane, int row0, int icol, Carry& c) {
-    if (icol >= p.N) return;
-    const bf16* base = p.y + gcol_of(icol) + 8 * (lane & 3);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int grow = row0 + 8 * i + (lane >> 2);
-      const bool in = grow < p.M;
-      c.g[i] = in ? *reinterpret_cast<const uint4*>(base + (int64_t)grow * p.ldy) : make_uint4(0, 0, 0, 0);
-      c.u[i] = in ? *reinterpret_cast<const uint4*>(base + (int64_t)grow * p.ldy + 128)
-                  : make_uint4(0, 0, 0, 0);
-    }
-  }
-  static __device__ __forceinline__ void prefetch(const Params& p, int row_base, int nt, int quarter,
-                                                  int lane, int group, int ngroups, Carry& c) {
-    load(p, lane, row_base + quarter * 32, nt * BN + group * (BN / 32 / ngroups) * 32, c);
-  }
-  static __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float2 t = __bfloat1622float2(h[q]);
-      f[2 * q] = t.x;
-      f[2 * q + 1] = t.y;
-    }
-  }
   static __device__ __forceinline__ void tile(const Params& p, const CUtensorMap* tmc, int row_base, int nt,
                                               int ks, int quarter, int lane, uint32_t taddr,
-                                              uint8_t* stage, int group, int ngroups, Carry& carry) {
-    const int row0 = row_base + quarter * 32;
-    const int nch = BN / 32 / ngroups;
-    const int c8 = lane & 3;
-#pragma unroll 1
-    for (int cc = group * nch; cc < (group + 1) * nch; ++cc) {
-      const int icol = nt * BN + cc * 32;
-      float d[32];
-      tmem_ld32(taddr + cc * 32, d);
-      if (icol >= p.N) continue;
-      // dh rounded to bf16, as the unfused GEMM would store it
-#pragma unroll
-      for (int j = 0; j < 32; ++j) d[j] = __bfloat162float(__float2bfloat16_rn(d[j]));
-      stage_row(stage, lane, d, 1.f);
-      __syncwarp();
-      uint4 og[4], ou[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = 8 * i + (lane >> 2);
-        const float4 a = *reinterpret_cast<const float4*>(stage + stage_off(r, 2 * c8));
-        const float4 b = *reinterpret_cast<const float4*>(stage + stage_off(r, 2 * c8 + 1));
-        const float dv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        float gv[8], uv[8];
-        unpack8(carry.g[i], gv);
-        unpack8(carry.u[i], uv);
-        float dg[8], du[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) swiglu_bwd_f(dv[q], gv[q], uv[q], dg[q], du[q]);
-        og[i] = make_uint4(pack_bf16x2(dg[0], dg[1]), pack_bf16x2(dg[2], dg[3]),
-                           pack_bf16x2(dg[4], dg[5]), pack_bf16x2(dg[6], dg[7]));
-        ou[i] = make_uint4(pack_bf16x2(du[0], du[1]), pack_bf16x2(du[2], du[3]),
-                           pack_bf16x2(du[4], du[5]), pack_bf16x2(du[6], du[7]));
+                                              uint8_t* stage, int group, int ngroups) {
+    const int nch = BN / 32 / ngroups;   // 32-column chunks of this warp (4 with 8 warps)
+    const int c0 = group * nch;
+    const int icol0 = nt * BN + c0 * 32;  // first intermediate column of the warp
+    if (icol0 >= p.N) {
+      for (int cc = c0; cc < c0 + nch; ++cc) {  // the accumulator is read in every case
+        float d[32];
+        tmem_ld32(taddr + cc * 32, d);
       }
-      __syncwarp();  // the stage is rewritten by the next chunk
-      if (cc + 1 < (group + 1) * nch) load(p, lane, row0, icol + 32, carry);
-      bf16* base = p.y + gcol_of(icol) + 8 * c8;
+      return;
+    }
+    const int width = nch * 32;          // <= 128, within one interleave block
+    const int gc0 = gcol_of(icol0);
+    const int row0 = row_base + quarter * 32;
+    uint16_t* sh = reinterpret_cast<uint16_t*>(stage);  // [16][width] bf16
+#pragma unroll 1
+    for (int hr = 0; hr < 2; ++hr) {
+#pragma unroll 1
+      for (int cc = 0; cc < nch; ++cc) {
+        float d[32];
+        tmem_ld32(taddr + (c0 + cc) * 32, d);
+        if ((lane >> 4) == hr) {
+          uint32_t wv[16];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int grow = row0 + 8 * i + (lane >> 2);
-        if (grow < p.M) {
-          *reinterpret_cast<uint4*>(base + (int64_t)grow * p.ldy) = og[i];
-          *reinterpret_cast<uint4*>(base + (int64_t)grow * p.ldy + 128) = ou[i];
+          for (int j = 0; j < 16; ++j) wv[j] = pack_bf16x2(d[2 * j], d[2 * j + 1]);
+          uint4* dst = reinterpret_cast<uint4*>(sh + (lane & 15) * width + cc * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(wv[4 * q], wv[4 * q + 1], wv[4 * q + 2], wv[4 * q + 3]);
         }
       }
+      __syncwarp();
+      const int lpr = width / 8;            // lanes per row (16 for 128 columns)
+      const int rpp = 32 / lpr;             // rows per pass
+      const int npass = 16 / rpp;
+      const int cl = lane % lpr, rl = lane / lpr;
+#pragma unroll 1
+      for (int p0 = 0; p0 < npass; p0 += kPass) {
+        uint4 gv[kPass], uv[kPass];
+#pragma unroll
+        for (int k = 0; k < kPass; ++k) {
+          const int r = (p0 + k) * rpp + rl;  // row within the half
+          const int grow = row0 + hr * 16 + r;
+          if (p0 + k < npass && grow < p.M) {
+            const bf16* src = p.y + (int64_t)grow * p.ldy + gc0 + 8 * cl;
+            gv[k] = *reinterpret_cast<const uint4*>(src);
+            uv[k] = *reinterpret_cast<const uint4*>(src + 128);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < kPass; ++k) {
+          const int r = (p0 + k) * rpp + rl;
+          const int grow = row0 + hr * 16 + r;
+          if (p0 + k >= npass || grow >= p.M) continue;
+          const uint4 dv4 = *reinterpret_cast<const uint4*>(sh + r * width + 8 * cl);
+          const __nv_bfloat162* dh2 = reinterpret_cast<const __nv_bfloat162*>(&dv4);
+          const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[k]);
+          const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv[k]);
+          uint32_t og[4], ou[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 dd = __bfloat1622float2(dh2[q]), gg = __bfloat1622float2(g2[q]),
+                         uu = __bfloat1622float2(u2[q]);
+            float dg0, du0, dg1, du1;
+            swiglu_bwd_f(dd.x, gg.x, uu.x, dg0, du0);
+            swiglu_bwd_f(dd.y, gg.y, uu.y, dg1, du1);
+            og[q] = pack_bf16x2(dg0, dg1);
+            ou[q] = pack_bf16x2(du0, du1);
+          }
+          bf16* dst = p.y + (int64_t)grow * p.ldy + gc0 + 8 * cl;
+          *reinterpret_cast<uint4*>(dst) = make_uint4(og[0], og[1], og[2], og[3]);
+          *reinterpret_cast<uint4*>(dst + 128) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
+        }
+      }
+      __syncwarp();  // the staging block is rewritten by the next half
     }
   }
 };

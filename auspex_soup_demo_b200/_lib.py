@@ -103,6 +103,10 @@ _SIGNATURES = {
     "soup_gemm_bf16_lora": (c_int, [c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_vp, c_i64, c_vp, c_i64,
                                     c_i64, c_vp, c_vp, c_i64, c_int, c_i64, c_i64, c_i64, c_f, c_int,
                                     c_vp]),
+    "soup_lora_rank_gemm": (c_int, [c_vp, c_i64, c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64,
+                                    c_vp, c_i64, c_vp, c_i64, c_int, c_f, c_vp]),
+    "soup_lora_rank_grad_group": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
+                                          c_vp, c_vp, c_vp, c_vp, c_f, c_vp]),
 }
 
 _lib = None

@@ -25,6 +25,7 @@ step that surround the fused ops:
 
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Iterable, Optional
 
@@ -151,6 +152,88 @@ def lora_gemm(a: torch.Tensor, b: torch.Tensor, b_mn_major: bool, a2: torch.Tens
     return out
 
 
+def rank_gemm(a: torch.Tensor, b: torch.Tensor, a_mn_major: bool = False, c=None, ct=None, g=None,
+              g_trans: bool = False, alpha: float = 1.0) -> None:
+    """soup_lora_rank_gemm: C = op(a) b^T for a narrow b [n, K] (n <= 64), with
+    op(a) = a [M, K] or, with a_mn_major, a^T for a stored [K, M]. Writes
+    c = bf16(alpha C) [M, n], ct = its transpose [n, M] and/or g += alpha C
+    (fp32; g_trans: g^T += alpha C)."""
+    k, m = a.shape if a_mn_major else a.shape[::-1]
+    n = b.shape[0]
+    _lib.call("soup_lora_rank_gemm", a.device, a.data_ptr(), a.stride(0), int(a_mn_major), b.data_ptr(),
+              b.stride(0), m, n, k, _lib.ptr(c), 0 if c is None else c.stride(0), _lib.ptr(ct),
+              0 if ct is None else ct.stride(0), _lib.ptr(g), 0 if g is None else g.stride(0), int(g_trans),
+              float(alpha), _lib.stream_of(a))
+
+
+def rank_grad_group(dy: torch.Tensor, xaT: torch.Tensor, row_off, col_off, grads, interleaved: bool,
+                    alpha: float = 1.0) -> None:
+    """soup_lora_rank_grad_group: the members' gB += alpha dy^T xa in one pass over
+    dy [T, N] (member j: rows [row_off[j], row_off[j+1]) of N - 128-row blocks in
+    turn when interleaved - and rank columns [col_off[j], col_off[j+1]) of xaT [R, T])."""
+    k, m = dy.shape
+    nm = len(grads)
+    ptrs = (ctypes.c_void_p * nm)(*[g.data_ptr() for g in grads])
+    _lib.call("soup_lora_rank_grad_group", dy.device, dy.data_ptr(), dy.stride(0), xaT.data_ptr(),
+              xaT.stride(0), m, xaT.shape[0], k, nm, int(interleaved), _lib.i64_array(list(row_off)),
+              _lib.i64_array(list(col_off)), ptrs, _lib.i64_array([g.stride(0) for g in grads]),
+              float(alpha), _lib.stream_of(dy))
+
+
+#: Run the rank-r products of the LoRA linears (x As^T, dy B and the gradient
+#: products dxa^T x, dy^T xa) on soup_lora_rank_gemm instead of cuBLAS. Off by
+#: default: measured on B200 inside the captured Qwen2.5-1.5B step at 8192
+#: tokens, cuBLAS runs the 25 MB products in 5-6 us (the kernel 7.5-11 us) and
+#: streams the 150-300 MB ones at 6.4 TB/s (the kernel 5 TB/s); the kernel wins
+#: only the gradient products of the rank-16 linears (9.7-10.8 us against
+#: 12.6-12.9), and the step is 1.3 % slower with it on.
+RANK_KERNELS = False
+
+
+def _rank_ok(*ts) -> bool:
+    if not RANK_KERNELS:
+        return False
+    for t in ts:
+        if (t is None or not t.is_cuda or t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1
+                or t.stride(0) % 8 or t.data_ptr() % 16):
+            return False
+    return True
+
+
+def _grad_ok(g: Optional[torch.Tensor]) -> bool:
+    return g is not None and g.is_cuda and g.dtype == torch.float32 and g.is_contiguous()
+
+
+def _rank_product(a: torch.Tensor, bt: torch.Tensor):
+    """(a @ bt^T [M, R], its transpose [R, M] or None): one soup_lora_rank_gemm
+    writing both when the operands allow, else cuBLAS."""
+    m, r = a.shape[0], bt.shape[0]
+    if r <= 64 and m % 8 == 0 and _rank_ok(a, bt):
+        c = torch.empty(m, r, device=a.device, dtype=a.dtype)
+        ct = torch.empty(r, m, device=a.device, dtype=a.dtype)
+        rank_gemm(a, bt, c=c, ct=ct)
+        return c, ct
+    return a @ bt.t(), None
+
+
+def _lora_grads(A, B, x2, dy2, xa, xaT, dxa, dxaT, s, need_a: bool, need_b: bool):
+    """(gA, gB) of one LoRA linear: accumulated in place into fp32 .grad buffers
+    (None returned) by soup_lora_rank_gemm when the transposed rank products
+    exist, else through _accumulate_grad."""
+    gA = gB = None
+    if need_a:
+        if dxaT is not None and _grad_ok(A.grad) and _rank_ok(x2):
+            rank_gemm(x2, dxaT, a_mn_major=True, g=A.grad, g_trans=True, alpha=s)
+        else:
+            gA = _accumulate_grad(A, dxa.t(), x2, s)
+    if need_b:
+        if xaT is not None and _grad_ok(B.grad) and _rank_ok(dy2):
+            rank_gemm(dy2, xaT, a_mn_major=True, g=B.grad)
+        else:
+            gB = _accumulate_grad(B, dy2.t(), xa, 1.0)
+    return gA, gB
+
+
 class _LoRALinearFn(torch.autograd.Function):
     """y = x W^T (+ b) + (x As^T) B^T for a frozen base weight W and LoRA factors
     A [r, in], B [out, r], with As = s A (s = alpha / r).
@@ -166,10 +249,10 @@ class _LoRALinearFn(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, x, A, B, As16, B16, scaling, weight_fn, bias):
+    def forward(ctx, x, A, B, As16, B16, scaling, weight_fn, bias, Bt16=None):
         w = weight_fn(x.dtype)
         x2 = x.reshape(-1, x.shape[-1])
-        xa = x2 @ As16.t()
+        xa, xaT = _rank_product(x2, As16)
         m, n = x2.shape[0], w.shape[0]
         if _fused_ok(x2.shape[1], x2, w, xa, B16, bias.view(1, -1) if bias is not None else None):
             y2 = lora_gemm(x2, w, False, xa, B16, torch.empty(m, n, device=x.device, dtype=x.dtype), bias)
@@ -177,7 +260,7 @@ class _LoRALinearFn(torch.autograd.Function):
         else:
             y = F.linear(x, w, bias)
             y.view(-1, n).addmm_(xa, B16.t())
-        ctx.save_for_backward(x, xa, As16, B16)
+        ctx.save_for_backward(x, xa, As16, B16, xaT, Bt16)
         ctx.params = (A, B)
         ctx.scaling = scaling
         ctx.weight_fn = weight_fn
@@ -186,15 +269,18 @@ class _LoRALinearFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dy):
-        x, xa, As16, B16 = ctx.saved_tensors
+        x, xa, As16, B16, xaT, Bt16 = ctx.saved_tensors
         A, B = ctx.params
         s = ctx.scaling
         dy2 = dy.reshape(-1, dy.shape[-1])
         if dy2.stride(1) != 1:
             dy2 = dy2.contiguous()
         x2 = x.reshape(-1, x.shape[-1])
-        dxa = dy2 @ B16
-        dx = gA = gB = None
+        if xaT is not None:
+            dxa, dxaT = _rank_product(dy2, Bt16 if Bt16 is not None else B16.t().contiguous())
+        else:
+            dxa, dxaT = dy2 @ B16, None
+        dx = None
         if ctx.needs_input_grad[0]:
             w = ctx.w if ctx.w is not None and ctx.w.dtype == dy.dtype else ctx.weight_fn(dy.dtype)
             ctx.w = None
@@ -205,11 +291,9 @@ class _LoRALinearFn(torch.autograd.Function):
                 dx2 = dy2 @ w
                 dx2.addmm_(dxa, As16)
             dx = dx2.view(x.shape)
-        if ctx.needs_input_grad[1]:
-            gA = _accumulate_grad(A, dxa.t(), x2, s)
-        if ctx.needs_input_grad[2]:
-            gB = _accumulate_grad(B, dy2.t(), xa, 1.0)
-        return dx, gA, gB, None, None, None, None, None
+        gA, gB = _lora_grads(A, B, x2, dy2, xa, xaT, dxa, dxaT, s, ctx.needs_input_grad[1],
+                             ctx.needs_input_grad[2])
+        return dx, gA, gB, None, None, None, None, None, None
 
 
 class _LoRABase(torch.nn.Module):
@@ -235,6 +319,7 @@ class _LoRABase(torch.nn.Module):
         self.scaling = alpha / r
         self.lora_As16 = None
         self.lora_B16 = None
+        self.lora_Bt16 = None  # B16 transposed [r, out], refreshed with it (or None)
         self.lora_group = None
 
     def base_weight(self, dtype) -> torch.Tensor:
@@ -246,13 +331,14 @@ class _LoRABase(torch.nn.Module):
             out = grp.member_output(self, x)
             if out is not None:
                 return out
-        as16, b16 = self.lora_As16, self.lora_B16
+        as16, b16, bt16 = self.lora_As16, self.lora_B16, self.lora_Bt16
         if as16 is None or as16.dtype != x.dtype:
             as16 = (self.lora_A.detach() * self.scaling).to(x.dtype)
             b16 = self.lora_B.detach().to(x.dtype)
+            bt16 = None
         bias = None if self.bias is None else self.bias.to(x.dtype)
         return _LoRALinearFn.apply(x, self.lora_A, self.lora_B, as16, b16, self.scaling,
-                                   self.base_weight, bias)
+                                   self.base_weight, bias, bt16)
 
 
 class LoRANF4Linear(_LoRABase):
@@ -370,6 +456,7 @@ class LoRAProjectionGroup:
         # after every optimiser step) and the fp32 gradient view of the stacked A
         self.As16 = None
         self.Bblk16 = None
+        self.BblkT16 = None  # Bblk16 transposed [R, N], refreshed with it
         self.gradA = None
         self._stash = None
         for m in self.members:
@@ -433,6 +520,13 @@ class LoRAProjectionGroup:
             else:
                 Bblk[self.out_off[j]:self.out_off[j + 1], r0:r1] = m.lora_B.detach().to(dtype)
         return As, Bblk
+
+    def factors_t(self, Bblk: torch.Tensor) -> torch.Tensor:
+        """Bblk^T [R, N]: the owner's refreshed copy when Bblk is its buffer."""
+        t = self.BblkT16
+        if t is not None and self.Bblk16 is not None and Bblk.data_ptr() == self.Bblk16.data_ptr():
+            return t
+        return Bblk.t().contiguous()
 
     def out_features_of(self, j: int) -> int:
         return self.outs[j]
@@ -503,11 +597,17 @@ def _group_gemm(group: LoRAProjectionGroup, x2: torch.Tensor, w: torch.Tensor, A
 
 
 def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tensor, xa: torch.Tensor,
-                    w: torch.Tensor, As16, Bblk, need_dx: bool, need_params):
+                    w: torch.Tensor, As16, Bblk, need_dx: bool, need_params, xaT=None):
     """dx (or None) and the LoRA gradients for a group GEMM's output gradient
     dy [M, N]. Gradients go straight into fp32 ``.grad`` buffers where the
-    parameters have them (None is returned for those)."""
-    dxa = dy @ Bblk
+    parameters have them (None is returned for those). With xaT (= xa^T from
+    the forward's soup_lora_rank_gemm) the rank products run on that kernel:
+    dxa and dxa^T in one pass over dy, gA into the stacked A gradient, and
+    every member's gB in one more pass over dy."""
+    if xaT is not None:
+        dxa, dxaT = _rank_product(dy, group.factors_t(Bblk))
+    else:
+        dxa, dxaT = dy @ Bblk, None
     dx = None
     if need_dx:
         m, n = dy.shape[0], w.shape[1]
@@ -522,14 +622,24 @@ def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tens
             need_params[2 * j] and group.members[j].lora_A.grad is not None
             and group.members[j].lora_A.grad.data_ptr() == group.gradA[group.rank_off[j]].data_ptr()
             for j in range(len(group.members))):
-        torch.addmm(group.gradA, dxa.t(), x2, alpha=group.scaling, out_dtype=torch.float32, out=group.gradA)
+        if dxaT is not None and _rank_ok(x2) and _grad_ok(group.gradA):
+            rank_gemm(x2, dxaT, a_mn_major=True, g=group.gradA, g_trans=True, alpha=group.scaling)
+        else:
+            torch.addmm(group.gradA, dxa.t(), x2, alpha=group.scaling, out_dtype=torch.float32, out=group.gradA)
         gA_done = True
+    gB_done = False
+    nm = len(group.members)
+    if (xaT is not None and nm <= 4 and _rank_ok(dy) and xaT.shape[0] <= 64
+            and all(need_params[2 * j + 1] and _grad_ok(group.members[j].lora_B.grad) for j in range(nm))):
+        rank_grad_group(dy, xaT, group.out_off, group.rank_off, [mm.lora_B.grad for mm in group.members],
+                        group.interleaved)
+        gB_done = True
     # one product G = dy^T xa [N, R] reads dy once for all members' B gradients
     # (member j's gradient is its output rows - row blocks when interleaved - and
     # rank columns of G); one accumulating product per member would re-read dy and
     # costs cuBLAS ~14 us each at 8192 tokens even for the 4 MB k / v gradients
     G = None
-    if any(need_params[2 * j + 1] for j in range(len(group.members))):
+    if not gB_done and any(need_params[2 * j + 1] for j in range(len(group.members))):
         G = torch.mm(dy.t(), xa, out_dtype=torch.float32)
     for j, mem in enumerate(group.members):
         r0, r1 = group.rank_off[j], group.rank_off[j + 1]
@@ -537,7 +647,7 @@ def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tens
         gA = gB = None
         if need_params[2 * j] and not gA_done:
             gA = _accumulate_grad(mem.lora_A, dxa[:, r0:r1].t(), x2, mem.scaling)
-        if need_params[2 * j + 1]:
+        if need_params[2 * j + 1] and not gB_done:
             if G is not None:
                 if group.interleaved:
                     part = group._il_view(G, group.r_total)[:, j, :, r0:r1]
@@ -563,8 +673,9 @@ class _LoRAGroupFn(torch.autograd.Function):
         x2 = x.reshape(-1, k)
         w = group.base_weight(x.dtype)
         As16, Bblk = group.factors(x.dtype)
-        y, xa = _group_gemm(group, x2, w, As16, Bblk)
-        ctx.save_for_backward(x2, xa, As16, Bblk)
+        xa, xaT = _rank_product(x2, As16)
+        y, xa = _group_gemm(group, x2, w, As16, Bblk, xa)
+        ctx.save_for_backward(x2, xa, As16, Bblk, xaT)
         ctx.w = _keep(w)
         ctx.group = group
         ctx.lead = x.shape[:-1]
@@ -574,7 +685,7 @@ class _LoRAGroupFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, *douts):
-        x2, xa, As16, Bblk = ctx.saved_tensors
+        x2, xa, As16, Bblk, xaT = ctx.saved_tensors
         group = ctx.group
         m = x2.shape[0]
         parts = [d.reshape(m, n) if d is not None else torch.zeros(m, n, device=x2.device, dtype=x2.dtype)
@@ -585,7 +696,7 @@ class _LoRAGroupFn(torch.autograd.Function):
             w = ctx.w if ctx.w is not None and ctx.w.dtype == dy.dtype else group.base_weight(dy.dtype)
         ctx.w = None
         dx, grads = _group_backward(group, dy, x2, xa, w, As16, Bblk, ctx.needs_input_grad[0],
-                                    ctx.needs_input_grad[2:])
+                                    ctx.needs_input_grad[2:], xaT)
         if dx is not None:
             dx = dx.view(*ctx.lead, x2.shape[1])
         return (dx, None, *grads)
@@ -654,7 +765,7 @@ class _LoRAGateUpFn(torch.autograd.Function):
         bias = None if group.bias is None else group.bias.to(x2.dtype)
         h = torch.empty(m, inter, device=x.device, dtype=x.dtype)
         y = None
-        xa = x2 @ As16.t()
+        xa, xaT = _rank_product(x2, As16)
         if _swiglu_fused_ok(group, x2, w, xa, Bblk, bias, h):
             if not recompute:
                 y = torch.empty(m, group.n_total, device=x.device, dtype=x.dtype)
@@ -666,9 +777,9 @@ class _LoRAGateUpFn(torch.autograd.Function):
         ctx.recompute = recompute
         ctx.w = _keep(w)
         if recompute:
-            ctx.save_for_backward(x2, xa, As16, Bblk)
+            ctx.save_for_backward(x2, xa, As16, Bblk, xaT)
         else:
-            ctx.save_for_backward(x2, xa, As16, Bblk, y)
+            ctx.save_for_backward(x2, xa, As16, Bblk, xaT, y)
         ctx.group = group
         ctx.lead = x.shape[:-1]
         return h.view(*x.shape[:-1], inter)
@@ -679,7 +790,7 @@ class _LoRAGateUpFn(torch.autograd.Function):
 
         group = ctx.group
         saved = ctx.saved_tensors
-        x2, xa, As16, Bblk = saved[:4]
+        x2, xa, As16, Bblk, xaT = saved[:5]
         inter = group.outs[0]
         w = ctx.w if ctx.w is not None and ctx.w.dtype == x2.dtype else group.base_weight(x2.dtype)
         ctx.w = None
@@ -696,12 +807,12 @@ class _LoRAGateUpFn(torch.autograd.Function):
             if ctx.recompute:
                 y, _ = _group_gemm(group, x2, w, As16, Bblk, xa)
             else:
-                y = saved[4]
+                y = saved[5]
             g, u = _gu_views(group, y)
             dg, du = _gu_views(group, dy)
             swiglu_backward(dh2.view(g.shape[0], g.shape[1]), g, u, dg=dg, du=du)
         dx, grads = _group_backward(group, dy, x2, xa, w, As16, Bblk, ctx.needs_input_grad[0],
-                                    ctx.needs_input_grad[3:])
+                                    ctx.needs_input_grad[3:], xaT)
         if dx is not None:
             dx = dx.view(*ctx.lead, x2.shape[1])
         return (dx, None, None, *grads)
@@ -737,7 +848,7 @@ class _LoRAMLPFn(torch.autograd.Function):
         bias = None if group.bias is None else group.bias.to(x2.dtype)
         h = torch.empty(m, inter, device=x.device, dtype=x.dtype)
         y = torch.empty(m, group.n_total, device=x.device, dtype=x.dtype)
-        xa = x2 @ As16.t()
+        xa, xaT = _rank_product(x2, As16)
         if _swiglu_fused_ok(group, x2, w, xa, Bblk, bias, h, y):
             swiglu_gemm(x2, w, xa, Bblk, bias, 0, h, y)
         else:
@@ -747,13 +858,14 @@ class _LoRAMLPFn(torch.autograd.Function):
             g, u = _gu_views(group, y)
             swiglu_forward(g, u, out=h.view(g.shape[0], g.shape[1]))
         # down: as _LoRALinearFn.forward
-        as16_d, b16_d = down.lora_As16, down.lora_B16
+        as16_d, b16_d, bt16_d = down.lora_As16, down.lora_B16, down.lora_Bt16
         if as16_d is None or as16_d.dtype != x.dtype:
             as16_d = (down.lora_A.detach() * down.scaling).to(x.dtype)
             b16_d = down.lora_B.detach().to(x.dtype)
+            bt16_d = None
         bias_d = None if down.bias is None else down.bias.to(x.dtype)
         w_d = down.base_weight(x.dtype)
-        xa_d = h @ as16_d.t()
+        xa_d, xa_dT = _rank_product(h, as16_d)
         n_out = w_d.shape[0]
         if _fused_ok(inter, h, w_d, xa_d, b16_d, bias_d.view(1, -1) if bias_d is not None else None):
             out = lora_gemm(h, w_d, False, xa_d, b16_d,
@@ -761,7 +873,7 @@ class _LoRAMLPFn(torch.autograd.Function):
         else:
             out = F.linear(h, w_d, bias_d)
             out.addmm_(xa_d, b16_d.t())
-        ctx.save_for_backward(x2, xa, As16, Bblk, y, h, xa_d, as16_d, b16_d)
+        ctx.save_for_backward(x2, xa, As16, Bblk, y, h, xa_d, as16_d, b16_d, xaT, xa_dT, bt16_d)
         ctx.w = _keep(w)
         ctx.w_d = _keep(w_d)
         ctx.group = group
@@ -773,7 +885,7 @@ class _LoRAMLPFn(torch.autograd.Function):
     def backward(ctx, dout):
         from .kernels.swiglu import swiglu_backward
 
-        x2, xa, As16, Bblk, y, h, xa_d, as16_d, b16_d = ctx.saved_tensors
+        x2, xa, As16, Bblk, y, h, xa_d, as16_d, b16_d, xaT, xa_dT, bt16_d = ctx.saved_tensors
         group, down = ctx.group, ctx.down
         d2 = dout.reshape(-1, dout.shape[-1])
         if d2.stride(1) != 1 or d2.stride(0) != d2.shape[1]:
@@ -783,7 +895,10 @@ class _LoRAMLPFn(torch.autograd.Function):
         w_d = ctx.w_d if ctx.w_d is not None and ctx.w_d.dtype == x2.dtype else down.base_weight(x2.dtype)
         w = ctx.w if ctx.w is not None and ctx.w.dtype == x2.dtype else group.base_weight(x2.dtype)
         ctx.w = ctx.w_d = None
-        dxa_d = d2 @ b16_d
+        if xa_dT is not None:
+            dxa_d, dxa_dT = _rank_product(d2, bt16_d if bt16_d is not None else b16_d.t().contiguous())
+        else:
+            dxa_d, dxa_dT = d2 @ b16_d, None
         if _fused_ok(d2.shape[1], d2, w_d, dxa_d, as16_d, y):
             dswiglu_gemm(d2, w_d, dxa_d, as16_d, y)
             dy = y  # [dg | du] over [g | u]
@@ -794,13 +909,10 @@ class _LoRAMLPFn(torch.autograd.Function):
             g, u = _gu_views(group, y)
             dg, du = _gu_views(group, dy)
             swiglu_backward(dh.view(g.shape[0], g.shape[1]), g, u, dg=dg, du=du)
-        gA_d = gB_d = None
-        if ctx.needs_input_grad[3]:
-            gA_d = _accumulate_grad(down.lora_A, dxa_d.t(), h, down.scaling)
-        if ctx.needs_input_grad[4]:
-            gB_d = _accumulate_grad(down.lora_B, d2.t(), xa_d, 1.0)
+        gA_d, gB_d = _lora_grads(down.lora_A, down.lora_B, h, d2, xa_d, xa_dT, dxa_d, dxa_dT, down.scaling,
+                                 ctx.needs_input_grad[3], ctx.needs_input_grad[4])
         dx, grads = _group_backward(group, dy, x2, xa, w, As16, Bblk, ctx.needs_input_grad[0],
-                                    ctx.needs_input_grad[5:])
+                                    ctx.needs_input_grad[5:], xaT)
         if dx is not None:
             dx = dx.view(*ctx.lead, x2.shape[1])
         return (dx, None, None, gA_d, gB_d, *grads)
@@ -964,12 +1076,14 @@ class QLoRATrainer:
                 views16[id(p)] = self.flat_param16[off:off + n].view_as(p)
             off += n
         self._bblk_copies = []
+        self._t_copies = []
         if self.flat_param16 is not None:
             for m in lora:
                 if id(m.lora_B) in views16:
                     m.lora_As16 = views16[id(m.lora_A)]
                     m.lora_B16 = views16[id(m.lora_B)]
             self._setup_groups(lora, offsets)
+            self._setup_bt(lora, offsets)
             self._refresh_param16()
         on_cuda = self.params[0].is_cuda
         # AdamW (HF Trainer defaults: betas 0.9 / 0.999, eps 1e-8, weight decay 0).
@@ -1075,8 +1189,11 @@ class QLoRATrainer:
         for key, items in kinds.items():
             g0 = items[0][0]
             buf = torch.zeros(len(items), g0.n_total, g0.r_total, dtype=self.flat_param16.dtype, device=dev)
+            buf_t = torch.zeros(len(items), g0.r_total, g0.n_total, dtype=self.flat_param16.dtype, device=dev)
             for l, (g, _) in enumerate(items):
                 g.Bblk16 = buf[l]
+                g.BblkT16 = buf_t[l]
+            self._t_copies.append((buf_t, buf.transpose(1, 2)))
             L, R = len(items), g0.r_total
             for j in range(len(g0.members)):
                 n_j, r_j = g0.outs[j], g0.ranks[j]
@@ -1101,6 +1218,30 @@ class QLoRATrainer:
                         src = self.flat_param16[off:off + n_j * r_j].view(src_shape)
                         self._bblk_copies.append((dst_all[l], src))
 
+    def _setup_bt(self, lora, offsets):
+        """Transposed 16-bit B copies [r, out] of the ungrouped LoRA linears (the
+        operand of dxa = dy B in soup_lora_rank_gemm): one [layers, r, out] buffer
+        per shape, refreshed by one strided copy when the factors sit at a fixed
+        stride in the flat buffer."""
+        kinds = {}
+        for m in lora:
+            if m.lora_group is None and m.lora_B16 is not None and id(m.lora_B) in offsets:
+                kinds.setdefault((m.out_features, m.lora_B.shape[1]), []).append(m)
+        dev = self.flat_param.device
+        for (n, r), mods in kinds.items():
+            L = len(mods)
+            buf = torch.empty(L, r, n, dtype=self.flat_param16.dtype, device=dev)
+            for l, m in enumerate(mods):
+                m.lora_Bt16 = buf[l]
+            offs = [offsets[id(m.lora_B)] for m in mods]
+            stride = offs[1] - offs[0] if L > 1 else n * r
+            if all(offs[l] == offs[0] + l * stride for l in range(L)):
+                src = self.flat_param16.as_strided((L, n, r), (stride, r, 1), offs[0])
+                self._t_copies.append((buf, src.transpose(1, 2)))
+            else:
+                for l, m in enumerate(mods):
+                    self._t_copies.append((buf[l], m.lora_B16.t()))
+
     def _refresh_param16(self):
         if self.flat_param16 is not None:
             na = self.n_a
@@ -1111,6 +1252,9 @@ class QLoRATrainer:
     def _refresh_bblk(self):
         for dst, src in self._bblk_copies:
             dst.copy_(src)
+        if RANK_KERNELS:  # after the block-diagonal copies they read
+            for dst, src in self._t_copies:
+                dst.copy_(src)
 
     def capture(self, input_ids: torch.Tensor, labels: torch.Tensor, denominator: float,
                 warmup: int = 3):

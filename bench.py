@@ -322,6 +322,7 @@ def measure_qlora(args, R: Ranks, batch: int, seq: int, with_extras: bool = True
     # (8.2 GB for 28 layers) of the B200's 180 GB and saves one gate/up GEMM per layer.
     from auspex_soup_demo_b200.kernels import swiglu as _swiglu
     _swiglu.RECOMPUTE = bool(args.recompute)
+    qlora.RANK_KERNELS = bool(getattr(args, "rank_kernels", False))
     dev = R.dev
     model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=args.layers,
                                                             attention=args.attention),
@@ -483,6 +484,65 @@ def time_mlp_backward(m: int, dev, reps: int = 20, hidden: int = 1536, inter: in
             "frac_of_sustained": round(flop / (t_fused * 1e-3) / 1e12 / sus_peak, 4),
             "peak_source": f"{src} bf16_tflops (burst); sustained {sus_src}",
             "epilogue_bytes": 4 * m * inter * 2}
+
+
+def time_rank_products(m: int, dev, reps: int = 20):
+    """The four rank-r products of each Qwen2.5-1.5B LoRA linear at m tokens (xa =
+    x (sA)^T, dxa = dy B, gA += s dxa^T x, gB += dy^T xa) on soup_lora_rank_gemm
+    against cuBLAS. Each product is captured reps times in a CUDA graph, replayed
+    5 times (microseconds per product, CUDA events)."""
+    from auspex_soup_demo_b200 import qlora
+
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev).manual_seed(8)
+
+    def timed(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del graph
+        return round(e0.elapsed_time(e1) / (5 * reps) * 1e3, 2)
+
+    def rnd(*shape):
+        return torch.randn(*shape, device=dev, generator=g).to(torch.bfloat16)
+
+    out = {}
+    for name, k_in, n_out, r in (("qkv", 1536, 2048, 48), ("o", 1536, 1536, 16),
+                                 ("gate_up", 1536, 17920, 32), ("down", 8960, 1536, 16)):
+        x, dy, a, bt = rnd(m, k_in), rnd(m, n_out), 0.05 * rnd(r, k_in), 0.05 * rnd(r, n_out)
+        b = bt.t().contiguous()
+        xa, dxa = rnd(m, r), rnd(m, r)
+        xat, dxat = xa.t().contiguous(), dxa.t().contiguous()
+        c = torch.empty(m, r, device=dev, dtype=torch.bfloat16)
+        ct = torch.empty(r, m, device=dev, dtype=torch.bfloat16)
+        ga = torch.zeros(r, k_in, device=dev)
+        gb = torch.zeros(n_out, r, device=dev)
+        out[name] = {
+            "xa_us": [timed(lambda: qlora.rank_gemm(x, a, c=c, ct=ct)), timed(lambda: x @ a.t())],
+            "dxa_us": [timed(lambda: qlora.rank_gemm(dy, bt, c=c, ct=ct)), timed(lambda: dy @ b)],
+            "gA_us": [timed(lambda: qlora.rank_gemm(x, dxat, a_mn_major=True, g=ga, g_trans=True, alpha=2.0)),
+                      timed(lambda: torch.addmm(ga, dxa.t(), x, alpha=2.0, out_dtype=torch.float32, out=ga))],
+            "gB_us": [timed(lambda: qlora.rank_gemm(dy, xat, a_mn_major=True, g=gb)),
+                      timed(lambda: torch.addmm(gb, dy.t(), xa, out_dtype=torch.float32, out=gb))],
+        }
+    return {"shape": f"{m} tokens; [kernel, cuBLAS] microseconds per product", "products": out}
 
 
 def time_gate_up_gemm(group, m: int, dev, reps: int = 20, recompute: bool = False):
@@ -1064,6 +1124,7 @@ def run_step(args):
                    "lora": "r16 a32 q/k/v/o/gate/up/down", "lora_params": q["lora_params"],
                    "base": "NF4 blocksize 64, dequantised per use", "optimizer": "AdamW 2e-4",
                    "mlp_recompute": bool(args.recompute), "attention": args.attention,
+                   "rank_products": "soup_lora_rank_gemm" if args.rank_kernels else "cuBLAS",
                    "parallelism": f"dp{R.world}" + (" (one NCCL all-reduce of the flat fp32 LoRA "
                                                     "gradient per step)" if R.world > 1 else ""),
                    "l2": "weights and activations far larger than L2"},
@@ -1137,6 +1198,12 @@ def run_section(args):
         mb = time_mlp_backward(args.batch * (args.seq or QLORA_SEQ), R.dev, reps=max(args.steps, 1))
         res = {"metric": "down dX GEMM + SwiGLU backward epilogue TFLOP/s", "value": mb["achieved"],
                "unit": "TFLOP/s", "dtype": "bf16", **mb}
+    elif args.workload == "rank":
+        rk = time_rank_products(args.batch * (args.seq or QLORA_SEQ), R.dev, reps=max(args.steps, 1))
+        kern = sum(v[0] for p in rk["products"].values() for v in p.values())
+        cub = sum(v[1] for p in rk["products"].values() for v in p.values())
+        res = {"metric": "LoRA rank products per layer, kernel / cuBLAS time", "value": round(kern / cub, 3),
+               "unit": "ratio", "higher_is_better": False, "dtype": "bf16", **rk}
     elif args.workload == "gateup":
         from auspex_soup_demo_b200 import qlora
 
@@ -1165,14 +1232,15 @@ def main():
                     help="default line: skip the nested ce / mem_ops / ce_vp / qlora_s512 results")
     ap.add_argument("--workload", default="step",
                     choices=["step", "qlora", "ce", "rmsnorm", "swiglu", "rope", "ce_vp", "gateup",
-                             "attention", "mlp_bwd"],
+                             "attention", "mlp_bwd", "rank"],
                     help="step (default): the QLoRA train step with the other results nested; "
                          "qlora: the step alone; ce: the fused head CE; rmsnorm/swiglu/rope: one "
                          "memory-bound op's HBM GB/s; ce_vp: the vocab-parallel CE over all ranks; "
                          "gateup: the step's gate/up GEMM with the SwiGLU epilogue alone; attention: "
                          "this library's attention against torch SDPA at the step's shape; mlp_bwd: "
                          "down_proj's dX GEMM with the SwiGLU backward in its epilogue against the "
-                         "unfused pair")
+                         "unfused pair; rank: the LoRA rank products on soup_lora_rank_gemm against "
+                         "cuBLAS")
     ap.add_argument("--sustained-steps", type=int, default=500,
                     help="ce: extra back-to-back steps timed under the power cap (0: skip)")
     ap.add_argument("--tokens", type=int, default=65536, help="ce_vp: tokens per step")
@@ -1189,6 +1257,9 @@ def main():
     ap.add_argument("--recompute", action="store_true",
                     help="step/qlora: recompute gate/up in the MLP backward, as the reference does "
                          "(default: keep [g | u] from the forward; same results, more memory)")
+    ap.add_argument("--rank-kernels", action="store_true",
+                    help="step/qlora: LoRA rank products on soup_lora_rank_gemm (default: cuBLAS, "
+                         "faster in the step)")
     ap.add_argument("--profile", action="store_true",
                     help="step/qlora: after the timed region, print a per-kernel device-time table "
                          "of two steps (torch.profiler, CUDA activity) to stderr")

@@ -342,6 +342,37 @@ int soup_gemm_bf16_lora_dswiglu(const void* a, int64_t lda, const void* b, int64
                                 int64_t r, void* y, int64_t ldy, int64_t m, int64_t inter,
                                 int64_t k, void* stream);
 
+/* ---- Rank-r products of the LoRA linears (n <= 64) ---------------------------
+ * C[m, n] = sum_k A(m, k) B(n, k) on the tensor cores, fp32 accumulation.
+ * A: a_mn_major = 0 stored [m, k] (lda >= k), 1 stored [k, m] (lda >= m);
+ * B: stored [n, k] (ldb >= k); bf16, rows 16-byte aligned. Outputs, any of:
+ *   c  != NULL: c[i * ldc + j]  = bf16(alpha * C[i, j])
+ *   ct != NULL: ct[j * ldct + i] = bf16(alpha * C[i, j])   (the transpose)
+ *   g  != NULL: fp32 g[i * ldg + j] += alpha * C[i, j]
+ *               (g_transposed: g[j * ldg + i] += alpha * C[i, j])
+ * The four products of a LoRA linear y = x W^T + s (x A^T) B^T are
+ *   xa = x (sA)^T (a = x, b = sA; ct = xa^T for gB), dxa = dy B (a = dy,
+ *   b = B^T; ct = dxa^T for gA), gA += s dxa^T x (a = x MN-major, b = dxa^T,
+ *   g = A.grad transposed), gB += dy^T xa (a = dy MN-major, b = xa^T, g = B.grad).
+ * Deterministic (fixed summation order). No counterpart in the reference:
+ * there these are four GEMMs of peft's LoRA Linear (lora_A, lora_B and their
+ * autograd) over the bitsandbytes 4-bit base layer. */
+int soup_lora_rank_gemm(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb,
+                        int64_t m, int64_t n, int64_t k, void* c, int64_t ldc, void* ct, int64_t ldct,
+                        float* g, int64_t ldg, int g_transposed, float alpha, void* stream);
+
+/* gB of the members of a projection group in one pass over dy: C = dy^T xa with
+ * a = dy stored [k = tokens, m = the group's output rows] (MN-major) and
+ * b = xa^T [n = stacked rank, k]; member j (0 <= j < nmem <= 4) owns rows
+ * [row_off[j], row_off[j+1]) of C (interleaved != 0: 128-row blocks taken in
+ * turn, block t belonging to member t % nmem, each member's rows a multiple of
+ * 128) and rank columns [col_off[j], col_off[j+1]), and receives
+ * g[j][local row * ldg[j] + col - col_off[j]] += alpha * C[row, col]. */
+int soup_lora_rank_grad_group(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t m, int64_t n,
+                              int64_t k, int nmem, int interleaved, const int64_t* row_off,
+                              const int64_t* col_off, float* const* g, const int64_t* ldg, float alpha,
+                              void* stream);
+
 /* ---- AdamW over flat fp32 buffers (the QLoRA step's optimiser) ------------
  * One pass over n elements: param, exp_avg, exp_avg_sq updated in place from
  * grad with torch.optim.AdamW's decoupled weight decay; `step` is a device

@@ -423,16 +423,16 @@ int rank_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, 
 
 bool rank_tma_ok(const void* p, int64_t ld) { return aligned16(p) && ld > 0 && (ld * 2) % 16 == 0; }
 
-// ks = CTAs per cluster (1..16): the largest for which the grid stays within
-// three CTAs per SM, all m_tiles clusters are resident at once (the device's
-// limit for clusters of that size with this kernel's shared memory) and every
-// CTA keeps at least two k-blocks.
+// ks = CTAs per cluster (1..16): as many as one wave of resident CTAs allows
+// (2-3 per SM, by the kernel's shared memory), at least four k-blocks per CTA,
+// and a cluster size the device can hold with this kernel's shared memory.
 template <bool A_MN, int NP>
 int rank_launch(const CUtensorMap& ma, const CUtensorMap& mb, RankArgs args, int m_tiles, cudaStream_t stream) {
   using L = RankSmem<NP>;
   static_assert(L::kBytes <= 232448, "rank product shared memory exceeds 227 KB");
   auto kern = rank_gemm_kernel<A_MN, NP>;
   static bool attr_done[64] = {false};
+  static int per_sm[64] = {0};           // resident CTAs per SM
   static int max_clusters[64][17] = {};  // by cluster size; -1: none fits
   int dev = 0;
   cudaGetDevice(&dev);
@@ -464,32 +464,38 @@ int rank_launch(const CUtensorMap& ma, const CUtensorMap& mb, RankArgs args, int
       // clusters of up to 16 CTAs (the occupancy query below says which fit)
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
         cudaGetLastError();
+      // by shared memory (228 KB per SM, 1 KB of it reserved per CTA), at most 3
+      int smem_sm = 0;
+      if (cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess) {
+        cudaGetLastError();
+        smem_sm = L::kBytes;
+      }
+      const int n = smem_sm / (L::kBytes + 1024);
+      per_sm[dev] = n < 1 ? 1 : n > 3 ? 3 : n;
       attr_done[dev] = true;
     }
   }
-  int ks = 1;
-  for (int c = 16; c > 1; --c) {
-    if (m_tiles * c > 3 * sms || args.kb_total < 2 * c) continue;
-    int fit;
-    {
-      std::lock_guard<std::mutex> lock(cache_mutex());
-      if (max_clusters[dev][c] == 0) {
-        int n = 0;
-        attr[0].val.clusterDim.x = c;
-        cfg.gridDim = dim3(c * (sms / c));
-        cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-        if (e != cudaSuccess) {
-          cudaGetLastError();
-          n = 0;
-        }
-        max_clusters[dev][c] = n > 0 ? n : -1;
+  // one wave of resident CTAs (2-3 per SM, by this kernel's shared memory), at
+  // least four k-blocks per CTA, clusters of up to 16 where the device can hold
+  // one of that size with this kernel
+  int ks = per_sm[dev] * sms / (m_tiles > 0 ? m_tiles : 1);
+  if (ks > 16) ks = 16;
+  if (ks > args.kb_total / 4) ks = args.kb_total / 4;
+  if (ks < 1) ks = 1;
+  for (; ks > 1; --ks) {
+    std::lock_guard<std::mutex> lock(cache_mutex());
+    if (max_clusters[dev][ks] == 0) {
+      int n = 0;
+      attr[0].val.clusterDim.x = ks;
+      cfg.gridDim = dim3(ks * (sms / ks));
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
       }
-      fit = max_clusters[dev][c];
+      max_clusters[dev][ks] = n > 0 ? n : -1;
     }
-    if (fit >= m_tiles) {
-      ks = c;
-      break;
-    }
+    if (max_clusters[dev][ks] > 0) break;
   }
   args.ks = ks;
   attr[0].val.clusterDim.x = ks;

@@ -91,6 +91,9 @@ _SIGNATURES = {
                                    c_sz, c_vp]),
     "soup_nf4_quantize": (c_int, [c_vp, c_i64, c_int, c_int, ctypes.POINTER(c_f), c_vp, c_vp, c_vp]),
     "soup_nf4_dequant": (c_int, [c_vp, c_vp, c_i64, c_int, ctypes.POINTER(c_f), c_vp, c_int, c_vp]),
+    "soup_gemm_stream_k_workspace_bytes": (c_sz, []),
+    "soup_gemm_set_stream_k_workspace": (c_int, [c_vp, c_sz]),
+    "soup_gemm_set_stream_k_min_saved": (c_int, [c_int]),
     "soup_gemm_bf16": (c_int, [c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_vp, c_i64, c_int, c_i64,
                                c_i64, c_i64, c_f, c_int, c_vp]),
     "soup_gemm_bf16_lora_swiglu": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64,
@@ -164,9 +167,66 @@ def call(fn: str, device: torch.device, *args) -> None:
     f = getattr(lib(), fn)
     if device.index is not None and device.index != torch.cuda.current_device():
         with torch.cuda.device(device):
+            if fn in _GEMM_ENTRY_POINTS:
+                _ensure_stream_k()
             check(fn, f(*args))
     else:
+        if fn in _GEMM_ENTRY_POINTS:
+            _ensure_stream_k()
         check(fn, f(*args))
+
+
+# --------------------------------------------------------------------------
+# Stream-K scratch of the tcgen05 GEMMs: one zero-filled buffer per device,
+# registered with the library before the first GEMM on that device (the
+# kernels leave it zero-filled). SOUP_STREAM_K=0 in the environment, or
+# set_stream_k(False), runs every GEMM's last wave as a partial wave instead.
+# Launches on one device share the buffer, so GEMMs of this library must not
+# run concurrently on unordered streams of one device.
+# --------------------------------------------------------------------------
+STREAM_K = os.environ.get("SOUP_STREAM_K", "1") != "0"
+_GEMM_ENTRY_POINTS = {
+    "soup_gemm_bf16", "soup_gemm_bf16_lora", "soup_gemm_bf16_lora_swiglu",
+    "soup_gemm_bf16_lora_dswiglu", "soup_ce_linear", "soup_ce_linear_dweight",
+    "soup_ce_vp_forward", "soup_ce_vp_backward",
+}
+_sk_buffers = {}  # device index -> registered buffer
+
+
+def _ensure_stream_k() -> None:
+    """Register the current device's stream-K buffer, once. Skipped while a
+    CUDA graph is being captured (the zero-fill would become part of the
+    graph): launches then run without the stream-K tail."""
+    idx = torch.cuda.current_device()
+    if idx in _sk_buffers or not STREAM_K:
+        return
+    if torch.cuda.is_current_stream_capturing():
+        return
+    with _lock:
+        if idx in _sk_buffers:
+            return
+        nbytes = int(lib().soup_gemm_stream_k_workspace_bytes())
+        buf = torch.zeros(nbytes, dtype=torch.uint8, device=torch.device("cuda", idx))
+        torch.cuda.synchronize(idx)  # zero before any stream's first GEMM reads it
+        check("soup_gemm_set_stream_k_workspace",
+              lib().soup_gemm_set_stream_k_workspace(buf.data_ptr(), nbytes))
+        _sk_buffers[idx] = buf
+
+
+def set_stream_k(enabled: bool) -> None:
+    """Turn the GEMMs' stream-K tail on or off for later launches (devices with
+    a registered buffer; the others get one on their next GEMM when enabled).
+    Synchronises those devices first."""
+    global STREAM_K
+    STREAM_K = bool(enabled)
+    for idx, buf in list(_sk_buffers.items()):
+        with torch.cuda.device(idx):
+            torch.cuda.synchronize(idx)
+            if enabled:
+                check("soup_gemm_set_stream_k_workspace",
+                      lib().soup_gemm_set_stream_k_workspace(buf.data_ptr(), buf.numel()))
+            else:
+                check("soup_gemm_set_stream_k_workspace", lib().soup_gemm_set_stream_k_workspace(None, 0))
 
 
 def ptr(t) -> int:

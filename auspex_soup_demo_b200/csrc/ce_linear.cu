@@ -26,6 +26,8 @@
 #include <stdio.h>
 #include <stdlib.h>
 
+#include <atomic>
+
 #include "soup_common.cuh"
 #include "tc_gemm.cuh"
 
@@ -267,6 +269,7 @@ __device__ __forceinline__ void stage_block_bf16(uint8_t* stage, int lane, const
 //   mode 1: dh from h [M, N/2]; dg, du -> y [M, N] at the tile's g / u columns
 template <int BN>
 struct EpiSwiGLU {
+  static constexpr bool kHalves = true;  // a warp reads g chunks and the u chunks BN/2 further
   struct Params {
     int mode;
     bf16* h;  // mode 0: output h; mode 1: input dh
@@ -826,6 +829,67 @@ static int launch_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb, cons
   return launch_status();
 }
 
+// ---- stream-K scratch, one per device (soup_gemm_set_stream_k_workspace) ----
+// Layout, fixed for a device: ready flags [slots][kSlotFlags] int (zero
+// between launches), padded to 256 bytes, then the fp32 partial slots
+// [slots][kSlotFloats], slots = half the SM count (one per CTA pair). Every
+// launch uses the same offsets, so no launch's partials land where another
+// launch's flags live.
+using SkL = SkLayout<kBN, kEpiWarps>;
+// A stream-K tail has on average at most this many k parts per tile.
+constexpr int kSkMaxParts = 3;
+struct SkWorkspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+static SkWorkspace g_sk_ws[64];
+
+static size_t sk_flag_bytes(int slots) {
+  return ((size_t)slots * SkL::kSlotFlags * sizeof(int) + 255) & ~(size_t)255;
+}
+static size_t sk_bytes(int slots) {
+  return sk_flag_bytes(slots) + (size_t)slots * SkL::kSlotFloats * sizeof(float);
+}
+
+// k blocks a stream-K tail must save over a whole tile
+// (soup_gemm_set_stream_k_min_saved)
+constexpr int kSkMinSavedDefault = 24;
+static std::atomic<int> g_sk_min_saved{kSkMinSavedDefault};
+static int sk_min_saved() { return g_sk_min_saved.load(std::memory_order_relaxed); }
+
+// Fills in sched's stream-K fields when the current device has a workspace,
+// the launch has one k split and is no diagnostic, and the tiles do not fill
+// whole waves of `max_cl` clusters; returns the number of clusters to launch.
+static int plan_stream_k(Sched& sched, int max_cl, int dev) {
+  const int tiles = sched.m_tiles * sched.n_tiles;
+  const int whole = tiles < max_cl ? tiles : max_cl;
+  if (sched.splits != 1 || sched.withhold >= 0 || tiles % max_cl == 0) return whole;
+  SkWorkspace ws;
+  {
+    std::lock_guard<std::mutex> lock(cache_mutex());
+    ws = g_sk_ws[dev];
+  }
+  if (!ws.ptr) return whole;
+  const int sk = tiles > max_cl ? tiles % max_cl : tiles;
+  const long long iters = (long long)sk * sched.kb_total;
+  long long skc = max_cl;
+  if (skc > (long long)sk * kSkMaxParts) skc = (long long)sk * kSkMaxParts;
+  if (skc > iters) skc = iters;
+  const int slots = num_sms() / 2;
+  // the kernel computes segment bounds in 32-bit integers
+  if (skc <= sk || skc > slots || sk_bytes(slots) > ws.bytes || (iters + 1) * (skc + 1) >= (1ll << 31))
+    return whole;
+  // worth it only if a segment is much shorter than a tile: a finishing pair
+  // waits for the partials and adds them after its last MMA (measured at 5-7 us
+  // per launch on B200, the time of ~20 k blocks of a 256 x 256 tile)
+  if ((iters + skc - 1) / skc + sk_min_saved() > sched.kb_total) return whole;
+  sched.sk_tiles = sk;
+  sched.sk_clusters = (int)skc;
+  sched.sk_flag = static_cast<int*>(ws.ptr);
+  sched.sk_part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws.ptr) + sk_flag_bytes(slots));
+  return tiles > max_cl ? max_cl : (int)skc;
+}
+
 template <bool A_MN, bool B_MN, class Epi>
 static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma2,
                             const CUtensorMap& mb2, const CUtensorMap& mc, Sched sched,
@@ -874,7 +938,8 @@ static int launch_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const 
     max_cl = max_clusters[dev];
   }
   const int units = sched.m_tiles * sched.n_tiles * sched.splits;
-  const int clusters = units < max_cl ? units : max_cl;
+  const int clusters = sched.splits == 1 ? plan_stream_k(sched, max_cl, dev)
+                                         : (units < max_cl ? units : max_cl);
   cfg.gridDim = dim3(2 * clusters);
   return cuda_status(cudaLaunchKernelEx(&cfg, kern, ma, mb, ma2, mb2, mc, sched, ep, err));
 }
@@ -1779,6 +1844,35 @@ int soup_set_stage_events(void** events, int n) {
   }
   for (int i = 0; i < 8; ++i) g_stage_events[i] = (i < n) ? static_cast<cudaEvent_t>(events[i]) : nullptr;
   g_n_stage_events = n;
+  return SOUP_OK;
+}
+
+size_t soup_gemm_stream_k_workspace_bytes(void) {
+  const int sms = num_sms();
+  return sms >= 2 ? sk_bytes(sms / 2) : 0;
+}
+
+int soup_gemm_set_stream_k_workspace(void* ws, size_t bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= 64 || (ws && reinterpret_cast<uintptr_t>(ws) % 256 != 0)) {
+    set_last_error("soup_gemm_set_stream_k_workspace: workspace must be 256-byte aligned");
+    return SOUP_ERR_INVALID;
+  }
+  if (ws && bytes < soup_gemm_stream_k_workspace_bytes()) {
+    set_last_error("soup_gemm_set_stream_k_workspace: smaller than soup_gemm_stream_k_workspace_bytes()");
+    return SOUP_ERR_WORKSPACE;
+  }
+  std::lock_guard<std::mutex> lock(cache_mutex());
+  g_sk_ws[dev].ptr = ws;
+  g_sk_ws[dev].bytes = ws ? bytes : 0;
+  return SOUP_OK;
+}
+
+int soup_gemm_set_stream_k_min_saved(int kblocks) {
+  if (kblocks < 0) kblocks = kSkMinSavedDefault;
+  g_sk_min_saved.store(kblocks, std::memory_order_relaxed);
   return SOUP_OK;
 }
 

@@ -42,6 +42,18 @@
 namespace soup {
 namespace tc {
 
+// An epilogue whose warps read, of a tile's 32-column chunks, half their run
+// in each half of the tile (not one contiguous run) declares
+//   static constexpr bool kHalves = true;
+template <class Epi, class = void>
+struct EpiHalves {
+  static constexpr bool value = false;
+};
+template <class Epi>
+struct EpiHalves<Epi, std::void_t<decltype(Epi::kHalves)>> {
+  static constexpr bool value = Epi::kHalves;
+};
+
 // An epilogue may declare `struct Carry` and
 //   static void prefetch(const Params&, int row_base, int nt, int quarter, int lane,
 //                        int group, int ngroups, Carry&);
@@ -69,6 +81,7 @@ constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
 constexpr int kErrWaitProducer = 0x101;
 constexpr int kErrWaitMma = 0x102;
 constexpr int kErrWaitEpilogue = 0x103;
+constexpr int kErrWaitPartial = 0x104;  // a stream-K partial never became ready
 
 // ------------------------------------------------------------ PTX wrappers --
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -188,6 +201,37 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// The inverse of tmem_ld32: thread t writes row (lane base + t), columns
+// [col, col+32); returns once the stores are complete.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  __syncwarp();
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// gpu-scope flag accesses between CTAs of one grid
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // Shared-memory matrix descriptor (sm_100 format): start address, leading
 // and stride byte offsets (16-byte units), version 1, 128-byte swizzle.
@@ -262,7 +306,121 @@ struct Sched {
     kb0 = ks * base + min(ks, rem);
     kb1 = kb0 + base + (ks < rem ? 1 : 0);
   }
+
+  // ---- stream-K tail (pair kernel only; splits == 1; 0 = off) ----
+  // The first m_tiles * n_tiles - sk_tiles tiles of the unit order go whole
+  // to the clusters, round-robin (a multiple of the cluster count). The k
+  // blocks of the last sk_tiles tiles, concatenated tile after tile, are cut
+  // into sk_clusters contiguous segments of equal length (+-1), one for each
+  // of the first sk_clusters clusters, which do them before their whole
+  // tiles. A segment covers the end of one tile and/or the start of the next.
+  // The cluster holding a tile's last k block finishes it: it adds the fp32
+  // partial accumulators of the tile's earlier parts, each left by the
+  // cluster that computed it in that cluster's slot of sk_part, in the order
+  // of k, then runs the epilogue. A cluster computes at most one such
+  // earlier part, so one slot per cluster suffices. sk_flag holds one ready
+  // flag per (slot, CTA of the pair, epilogue warp): set by the warp that
+  // wrote that piece of the slot, cleared by the warp that consumed it, so
+  // the flags are zero between launches.
+  int sk_tiles = 0;
+  int sk_clusters = 0;
+  float* sk_part = nullptr;
+  int* sk_flag = nullptr;
+
+  __device__ __forceinline__ void tile_of(int t, int& mt, int& nt) const {
+    if (order == 0) {
+      mt = t % m_tiles;
+      nt = t / m_tiles;
+    } else {
+      nt = t % n_tiles;
+      mt = t / n_tiles;
+    }
+  }
+  // concatenated stream-K k-iterations [g0, g1) of cluster c (the launcher
+  // keeps sk_tiles * kb_total * sk_clusters below 2^31: 32-bit math)
+  __device__ __forceinline__ void sk_segment(int c, int& g0, int& g1) const {
+    g0 = g1 = 0;
+    if (c >= sk_clusters) return;
+    const int s = sk_tiles * kb_total;
+    g0 = s * c / sk_clusters;
+    g1 = s * (c + 1) / sk_clusters;
+  }
+  // the cluster whose segment holds concatenated k-iteration g
+  __device__ __forceinline__ int sk_owner(int g) const {
+    return ((g + 1) * sk_clusters - 1) / (sk_tiles * kb_total);
+  }
+  __device__ __forceinline__ int sk_parts(int c) const {
+    int g0, g1;
+    sk_segment(c, g0, g1);
+    if (g1 <= g0) return 0;
+    return (g0 / kb_total != (g1 - 1) / kb_total) ? 2 : 1;
+  }
+  // number of units in cluster c's list (of n_clusters)
+  __device__ __forceinline__ int cluster_units(int c, int n_clusters) const {
+    if (sk_tiles == 0) return c < units() ? (units() - c + n_clusters - 1) / n_clusters : 0;
+    const int t_whole = m_tiles * n_tiles - sk_tiles;
+    const int n = c < t_whole ? (t_whole - c + n_clusters - 1) / n_clusters : 0;
+    return n + sk_parts(c);
+  }
 };
+
+// Role of a unit in a stream-K tail.
+constexpr int kRoleWhole = 0;   // the whole k range: epilogue as usual
+constexpr int kRolePart = 1;    // an earlier k part: fp32 partial into this cluster's slot
+constexpr int kRoleFinish = 2;  // the last k part: add the slots [fix_lo, fix_hi), then epilogue
+
+struct Unit {
+  int mt, nt, ks, kb0, kb1;
+  int role, fix_lo, fix_hi;
+};
+
+// Unit i of cluster c's list: its stream-K parts first (the start of the
+// later tile, then the end of the earlier one, so a cluster publishes its
+// partial before it waits for others'), then its whole tiles.
+__device__ __forceinline__ Unit sched_unit(const Sched& s, int c, int n_clusters, int i) {
+  Unit w;
+  w.role = kRoleWhole;
+  w.fix_lo = w.fix_hi = 0;
+  if (s.sk_tiles > 0) {
+    const int n_sk = s.sk_parts(c);
+    if (i < n_sk) {
+      int g0, g1;
+      s.sk_segment(c, g0, g1);
+      const int kb = s.kb_total;
+      const int t0 = g0 / kb;
+      int t, lo, hi;
+      if (n_sk == 2 && i == 0) {
+        t = t0 + 1;
+        lo = t * kb;
+        hi = g1;
+      } else if (n_sk == 2) {
+        t = t0;
+        lo = g0;
+        hi = (t0 + 1) * kb;
+      } else {
+        t = t0;
+        lo = g0;
+        hi = g1;
+      }
+      w.ks = 0;
+      w.kb0 = lo - t * kb;
+      w.kb1 = hi - t * kb;
+      s.tile_of(s.m_tiles * s.n_tiles - s.sk_tiles + t, w.mt, w.nt);
+      if (w.kb1 < s.kb_total) {
+        w.role = kRolePart;
+      } else if (w.kb0 > 0) {
+        w.role = kRoleFinish;
+        w.fix_lo = s.sk_owner(t * kb);
+        w.fix_hi = c;
+      }
+      return w;
+    }
+    i -= n_sk;
+  }
+  s.decode(c + i * n_clusters, w.mt, w.nt, w.ks);
+  s.k_range(w.ks, w.kb0, w.kb1);
+  return w;
+}
 
 // Per-epilogue-warp staging buffer: 32 rows x 32 fp32 (128 B per row); the
 // 16-byte granule q of row r is stored at granule q ^ (r & 7) (bank-conflict
@@ -605,8 +763,132 @@ __device__ __forceinline__ void tc_mma_bf16_pair(uint32_t tmem_d, uint64_t adesc
       : "memory");
 }
 
+// ---- stream-K partial accumulators (pair kernel) ----
+// A slot holds one tile's fp32 partial: per CTA of the pair and epilogue
+// warp, that warp's kChunks chunks of 32 rows x 32 columns, each chunk as 8
+// column groups of [32 lanes] float4 (so one store instruction of the warp
+// covers 512 contiguous bytes).
+template <int BN, int EPI_WARPS>
+struct SkLayout {
+  static constexpr int kGroups = EPI_WARPS / 4;
+  static constexpr int kChunks = BN / 32 / kGroups;
+  static constexpr int kWarpFloats = kChunks * 32 * 32;
+  static constexpr int kSlotFloats = 2 * EPI_WARPS * kWarpFloats;
+  static constexpr int kSlotFlags = 2 * EPI_WARPS;
+};
+// The i-th of the 32-column TMEM chunks that the epilogue warps of column
+// group `group` read: a contiguous run of chunks, or (HALVES) half a run in
+// each half of the tile, as EpiSwiGLU reads g and the u columns BN/2 further.
+// A warp completes exactly these chunks of a stream-K tile, so its epilogue
+// reads nothing another warp is still adding to.
+template <int BN, int EPI_WARPS, bool HALVES>
+__device__ __forceinline__ int sk_chunk(int group, int i) {
+  using SL = SkLayout<BN, EPI_WARPS>;
+  if constexpr (!HALVES) {
+    return group * SL::kChunks + i;
+  } else {
+    constexpr int h = SL::kChunks / 2;
+    return i < h ? group * h + i : BN / 64 + group * h + (i - h);
+  }
+}
+
+// An earlier k part of a stream-K tile: this warp's columns of the
+// accumulator go to the cluster's slot, then the warp's ready flag is set.
+template <int BN, int EPI_WARPS, bool HALVES>
+__device__ __forceinline__ void sk_put(const Sched& s, int slot, uint32_t rank, int e, int group,
+                                       int lane, uint32_t taddr) {
+  using SL = SkLayout<BN, EPI_WARPS>;
+  const int wi = static_cast<int>(rank) * EPI_WARPS + e;
+  float4* dst = reinterpret_cast<float4*>(s.sk_part + static_cast<size_t>(slot) * SL::kSlotFloats +
+                                          static_cast<size_t>(wi) * SL::kWarpFloats);
+#pragma unroll 1
+  for (int c = 0; c < SL::kChunks; ++c) {
+    float v[32];
+    tmem_ld32(taddr + sk_chunk<BN, EPI_WARPS, HALVES>(group, c) * 32, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      __stcg(dst + (c * 8 + j) * 32 + lane, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+  }
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) st_release_gpu(s.sk_flag + slot * SL::kSlotFlags + wi, 1);
+}
+
+// The last k part of a stream-K tile: wait (bounded) for the partials of
+// the tile's earlier parts, slots [w.fix_lo, w.fix_hi), add them to this
+// warp's columns of the accumulator in that order (a fixed order: results
+// do not vary from run to run) and clear their flags. false: the wait ran
+// out or the CTA is aborting.
+template <int BN, int EPI_WARPS, bool HALVES>
+__device__ __forceinline__ bool sk_fix(const Sched& s, const Unit& w, uint32_t rank, int e, int group,
+                                       int lane, uint32_t taddr, volatile int* abort_flag, int* err,
+                                       uint64_t limit_ns) {
+  using SL = SkLayout<BN, EPI_WARPS>;
+  const int wi = static_cast<int>(rank) * EPI_WARPS + e;
+  bool ok = true;
+  if (lane == 0) {
+    for (int slot = w.fix_lo; slot < w.fix_hi && ok; ++slot) {
+      const int* f = s.sk_flag + slot * SL::kSlotFlags + wi;
+      if (ld_acquire_gpu(f) != 0) continue;
+      const uint64_t t0 = globaltimer();
+      while (ld_acquire_gpu(f) == 0) {
+        if (*abort_flag) {
+          ok = false;
+          break;
+        }
+        if (globaltimer() - t0 > limit_ns) {
+          *abort_flag = 1;
+          atomicCAS(err, 0, kErrWaitPartial);
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  // lane 0 acquired every flag; the warp barrier orders the other lanes'
+  // loads below after those acquires
+  __syncwarp();
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  if (!ok) return false;
+  // (chunk, slot) pairs in order; the next pair's loads are issued as soon as
+  // the current one is added, so they overlap the TMEM store and load
+  const int ns = w.fix_hi - w.fix_lo;
+  const int npairs = SL::kChunks * ns;
+  const float* part = s.sk_part + static_cast<size_t>(wi) * SL::kWarpFloats;
+  auto load = [&](int p, float4 (&r)[8]) {
+    const int c = p / ns;
+    const float4* src = reinterpret_cast<const float4*>(
+        part + static_cast<size_t>(w.fix_lo + (p - c * ns)) * SL::kSlotFloats);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __ldcg(src + (c * 8 + j) * 32 + lane);
+  };
+  float4 cur[8];
+  load(0, cur);
+  float v[32];
+#pragma unroll 1
+  for (int p = 0; p < npairs; ++p) {
+    const int c = p / ns, si = p - c * ns;
+    const uint32_t ta = taddr + sk_chunk<BN, EPI_WARPS, HALVES>(group, c) * 32;
+    if (si == 0) tmem_ld32(ta, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[4 * j] += cur[j].x;
+      v[4 * j + 1] += cur[j].y;
+      v[4 * j + 2] += cur[j].z;
+      v[4 * j + 3] += cur[j].w;
+    }
+    if (p + 1 < npairs) load(p + 1, cur);  // in flight during this chunk's store and the next load
+    if (si == ns - 1) tmem_st32(ta, v);
+  }
+  __syncwarp();
+  if (lane == 0)
+    for (int slot = w.fix_lo; slot < w.fix_hi; ++slot) s.sk_flag[slot * SL::kSlotFlags + wi] = 0;
+  return true;
+}
+
 // Sched for this kernel counts m tiles of 2 x BM rows; the grid is
-// 2 x (number of clusters) with cluster dimension (2, 1, 1).
+// 2 x (number of clusters) with cluster dimension (2, 1, 1). With
+// sched.sk_tiles > 0 the tail tiles run as stream-K parts (see Sched).
 template <int BN, int STAGES, bool A_MN, bool B_MN, class Epi, int EPI_WARPS>
 __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -678,7 +960,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const int n_units = sched.units();
+  const int n_my = sched.cluster_units(cluster, n_clusters);
   const uint64_t wait_ns = sched.limit();
   const uint32_t idesc = sched.idesc(kIdesc);
   // Launched with programmatic dependent launch: the prologue above (barriers,
@@ -691,13 +973,11 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       // ------------------------------------------------ TMA producer ----
       uint32_t it = 0;
       bool ok = true;
-      for (int u = cluster; u < n_units && ok; u += n_clusters) {
-        int mt, nt, ks, kb0, kb1;
-        sched.decode(u, mt, nt, ks);
-        sched.k_range(ks, kb0, kb1);
-        const int a_row = mt * 2 * BM + static_cast<int>(rank) * BM;
-        const int b_row = nt * BN + static_cast<int>(rank) * BNH;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+      for (int i = 0; i < n_my && ok; ++i) {
+        const Unit w = sched_unit(sched, cluster, n_clusters, i);
+        const int a_row = w.mt * 2 * BM + static_cast<int>(rank) * BM;
+        const int b_row = w.nt * BN + static_cast<int>(rank) * BNH;
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!bounded_wait(empty_bar(s), ph ^ 1u, abort_flag, err, kErrWaitProducer, wait_ns)) {
@@ -748,10 +1028,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       uint32_t it = 0, lt = 0;
       bool ok = true;
       bool issued = false;
-      for (int u = cluster; u < n_units && ok; u += n_clusters, ++lt) {
-        int mt, nt, ks, kb0, kb1;
-        sched.decode(u, mt, nt, ks);
-        sched.k_range(ks, kb0, kb1);
+      for (int i = 0; i < n_my && ok; ++i, ++lt) {
+        const Unit w = sched_unit(sched, cluster, n_clusters, i);
+        const int kb0 = w.kb0, kb1 = w.kb1;
         const uint32_t acc = lt & 1u;
         const uint32_t acc_ph = (lt >> 1) & 1u;
         if (!bounded_wait<true>(tempty_bar(acc), acc_ph ^ 1u, abort_flag, err, kErrWaitMma, wait_ns)) {
@@ -802,12 +1081,13 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     uint8_t* stage = smem + L::kEpiOff + e * kEpiWarpBytes;
     typename EpiCarry<Epi>::type carry{};
     uint32_t lt = 0;
-    for (int u = cluster; u < n_units; u += n_clusters, ++lt) {
-      int mt, nt, ks;
-      sched.decode(u, mt, nt, ks);
+    constexpr bool kHalves = EpiHalves<Epi>::value;
+    for (int i = 0; i < n_my; ++i, ++lt) {
+      const Unit w = sched_unit(sched, cluster, n_clusters, i);
+      const int mt = w.mt, nt = w.nt, ks = w.ks;
       const int row_base = mt * 2 * BM + static_cast<int>(rank) * BM;
       if constexpr (EpiCarry<Epi>::kHas)
-        Epi::prefetch(ep, row_base, nt, quarter, lane, group, kGroups, carry);
+        if (w.role != kRolePart) Epi::prefetch(ep, row_base, nt, quarter, lane, group, kGroups, carry);
       const uint32_t acc = lt & 1u;
       const uint32_t acc_ph = (lt >> 1) & 1u;
       bool ok = true;
@@ -816,10 +1096,20 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + acc * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      if constexpr (EpiCarry<Epi>::kHas)
-        Epi::tile(ep, &tma_c, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups, carry);
-      else
-        Epi::tile(ep, &tma_c, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups);
+      if (w.role == kRolePart) {
+        // an earlier k part of a stream-K tile: the partial goes to this
+        // cluster's slot; the tile's finishing cluster runs the epilogue
+        sk_put<BN, EPI_WARPS, kHalves>(sched, cluster, rank, e, group, lane, taddr);
+      } else {
+        if (w.role == kRoleFinish &&
+            !sk_fix<BN, EPI_WARPS, kHalves>(sched, w, rank, e, group, lane, taddr, abort_flag, err, wait_ns))
+          break;
+        // the epilogue reads only the TMEM columns this warp has just completed
+        if constexpr (EpiCarry<Epi>::kHas)
+          Epi::tile(ep, &tma_c, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups, carry);
+        else
+          Epi::tile(ep, &tma_c, row_base, nt, ks, quarter, lane, taddr, stage, group, kGroups);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(tempty_bar(acc), 0));

@@ -100,13 +100,17 @@ def _accumulate_grad(param: torch.Tensor, m1: torch.Tensor, m2: torch.Tensor, al
     return (alpha * (m1.float() @ m2.float())).to(param.dtype)
 
 
-# Contractions longer than this stay on cuBLAS plus an accumulating rank-r
-# GEMM: measured on B200 at 2048 and 8192 tokens, the one-GEMM tcgen05 path
-# wins for every Qwen2.5-1.5B projection with K = 1536 (q/k/v/o, gate/up
-# forward, down backward) and loses for K = 8960 (down forward, gate/up
-# backward), where the output is narrow, the extra pass over it cheap, and
-# the persistent kernel's last wave of 256 x 256 tiles mostly idle.
+# Contractions longer than this (K = 8960: down forward, K = 17920: gate/up
+# backward) run on the tcgen05 GEMM only when their output has at least
+# LONG_K_MIN_WAVES waves of 256 x 256 tiles over the CTA pairs and the
+# GEMMs' stream-K tail is on (_lib.STREAM_K); otherwise on cuBLAS plus an
+# accumulating rank-r GEMM. Measured on B200 (CUDA graphs of 40 launches):
+# at 8192 tokens (192 tiles, 2.6 waves) the gate/up backward takes 322-331 us
+# against cuBLAS's 340-364 and the down forward 159-168 against 157-165; at
+# 2048 tokens (48 tiles) cuBLAS is faster (83 vs 88 us, 43 vs 50 us). Every
+# K = 1536 projection is faster on the tcgen05 GEMM at both sizes.
 FUSED_MAX_K = 4096
+LONG_K_MIN_WAVES = 2
 
 # Row-block size of the interleaved gate/up weight layout (half a GEMM tile).
 IL_BLOCK = 128
@@ -122,9 +126,17 @@ def _keep(w: torch.Tensor):
     return w if KEEP_BASE_WEIGHTS else None
 
 
-def _fused_ok(k: int, *ts: torch.Tensor) -> bool:
+def _fused_ok(k: int, *ts: torch.Tensor, n: Optional[int] = None) -> bool:
+    """The tcgen05 LoRA GEMM takes these operands: 16-byte aligned bf16 rows;
+    for K > FUSED_MAX_K also an output of ts[0].shape[0] x n wide enough (see
+    FUSED_MAX_K)."""
     if k > FUSED_MAX_K:
-        return False
+        if n is None or not _lib.STREAM_K or not ts or ts[0] is None or not ts[0].is_cuda:
+            return False
+        tiles = -(-ts[0].shape[0] // 256) * -(-n // 256)
+        pairs = torch.cuda.get_device_properties(ts[0].device).multi_processor_count // 2
+        if tiles < LONG_K_MIN_WAVES * pairs:
+            return False
     for t in ts:
         if t is None:
             continue
@@ -254,7 +266,7 @@ class _LoRALinearFn(torch.autograd.Function):
         x2 = x.reshape(-1, x.shape[-1])
         xa, xaT = _rank_product(x2, As16)
         m, n = x2.shape[0], w.shape[0]
-        if _fused_ok(x2.shape[1], x2, w, xa, B16, bias.view(1, -1) if bias is not None else None):
+        if _fused_ok(x2.shape[1], x2, w, xa, B16, bias.view(1, -1) if bias is not None else None, n=n):
             y2 = lora_gemm(x2, w, False, xa, B16, torch.empty(m, n, device=x.device, dtype=x.dtype), bias)
             y = y2.view(*x.shape[:-1], n)
         else:
@@ -285,7 +297,7 @@ class _LoRALinearFn(torch.autograd.Function):
             w = ctx.w if ctx.w is not None and ctx.w.dtype == dy.dtype else ctx.weight_fn(dy.dtype)
             ctx.w = None
             m, n = dy2.shape[0], w.shape[1]
-            if _fused_ok(dy2.shape[1], dy2, w, dxa, As16):
+            if _fused_ok(dy2.shape[1], dy2, w, dxa, As16, n=w.shape[1]):
                 dx2 = lora_gemm(dy2, w, True, dxa, As16, torch.empty(m, n, device=dy.device, dtype=dy.dtype))
             else:
                 dx2 = dy2 @ w
@@ -588,7 +600,7 @@ def _group_gemm(group: LoRAProjectionGroup, x2: torch.Tensor, w: torch.Tensor, A
     m = x2.shape[0]
     n = group.n_total
     bias = None if group.bias is None else group.bias.to(x2.dtype)
-    if _fused_ok(x2.shape[1], x2, w, xa, Bblk, bias.view(1, -1) if bias is not None else None):
+    if _fused_ok(x2.shape[1], x2, w, xa, Bblk, bias.view(1, -1) if bias is not None else None, n=n):
         y = lora_gemm(x2, w, False, xa, Bblk, torch.empty(m, n, device=x2.device, dtype=x2.dtype), bias)
     else:
         y = F.linear(x2, w, bias)
@@ -611,7 +623,7 @@ def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tens
     dx = None
     if need_dx:
         m, n = dy.shape[0], w.shape[1]
-        if _fused_ok(dy.shape[1], dy, w, dxa, As16):
+        if _fused_ok(dy.shape[1], dy, w, dxa, As16, n=w.shape[1]):
             dx = lora_gemm(dy, w, True, dxa, As16, torch.empty(m, n, device=dy.device, dtype=dy.dtype))
         else:
             dx = dy @ w
@@ -867,7 +879,8 @@ class _LoRAMLPFn(torch.autograd.Function):
         w_d = down.base_weight(x.dtype)
         xa_d, xa_dT = _rank_product(h, as16_d)
         n_out = w_d.shape[0]
-        if _fused_ok(inter, h, w_d, xa_d, b16_d, bias_d.view(1, -1) if bias_d is not None else None):
+        if _fused_ok(inter, h, w_d, xa_d, b16_d, bias_d.view(1, -1) if bias_d is not None else None,
+                     n=n_out):
             out = lora_gemm(h, w_d, False, xa_d, b16_d,
                             torch.empty(m, n_out, device=x.device, dtype=x.dtype), bias_d)
         else:

@@ -42,8 +42,9 @@ const char* soup_last_error(void);
  * Reads and clears it in one atomic step on the device (a code written
  * meanwhile by a kernel on another stream stays for the next read), then
  * synchronises the given stream. Codes: 0x101 producer, 0x102 MMA issuer,
- * 0x103 epilogue wait expired. No counterpart in the reference (its Triton
- * kernels have no device-side waits). */
+ * 0x103 epilogue wait expired, 0x104 a stream-K partial never became
+ * ready. No counterpart in the reference (its Triton kernels have no
+ * device-side waits). */
 int soup_device_error(void* stream, int* out_code);
 
 /* Time limit of every mbarrier wait inside the GEMM kernels launched after
@@ -267,6 +268,32 @@ int soup_nf4_quantize(const void* weight, int64_t n, int dtype, int blocksize, c
 /* out[i] = code16[index_i] * absmax[i / 64] in dtype (16-byte aligned buffers). */
 int soup_nf4_dequant(const uint8_t* packed, const float* absmax, int64_t n, int blocksize,
                      const float* code16, void* out, int dtype, void* stream);
+
+/* ---- Stream-K scratch of the tcgen05 GEMMs (this device) -------------------
+ * The pair GEMMs (every launch with one k split: the fused CE's logits and dW
+ * products, the QLoRA step's GEMMs below) run their last, partial wave as
+ * stream-K when the current device has a registered workspace and that
+ * saves enough: the k blocks of the tiles that do not fill a whole wave of
+ * CTA pairs are spread evenly over the pairs, and the pair holding a tile's
+ * last k block adds the other parts' fp32 partials (in a fixed order;
+ * results are reproducible) before the epilogue. Otherwise the tail runs as
+ * a partial wave.
+ * soup_gemm_stream_k_workspace_bytes: the size that covers every launch on
+ * the current device. soup_gemm_set_stream_k_workspace: registers `ws`
+ * (256-byte aligned, at least that size, zero-filled before the first
+ * launch; the kernels leave it zero-filled) for later launches on the
+ * current device, or none (NULL). Launches that use it must be ordered (one
+ * stream, or streams that wait on each other): they share its slots. A
+ * launch that ended with the device wait code 0x104 (soup_device_error) may
+ * leave it non-zero; zero it again before the next launch. No counterpart
+ * in the reference (its GEMMs are cuBLAS calls from PyTorch). */
+size_t soup_gemm_stream_k_workspace_bytes(void);
+int soup_gemm_set_stream_k_workspace(void* ws, size_t bytes);
+/* A launch runs its tail as stream-K only if that shortens its longest
+ * segment by at least `kblocks` k blocks of 64 against a whole tile (the
+ * finishing pairs' waits and adds cost about 20 on B200); negative: the
+ * default, 24. For tuning and tests; all devices, later launches. */
+int soup_gemm_set_stream_k_min_saved(int kblocks);
 
 /* ---- Plain tcgen05 GEMM (building block, exposed for tests) ---------------
  * C[m, n] = alpha * sum_k A(m, k) * B(n, k) (+ C if accumulate), bf16 inputs,

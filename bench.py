@@ -545,6 +545,87 @@ def time_rank_products(m: int, dev, reps: int = 20):
     return {"shape": f"{m} tokens; [kernel, cuBLAS] microseconds per product", "products": out}
 
 
+def time_projection_gemms(m: int, dev, reps: int = 40, rounds: int = 3):
+    """CUDA-event time (us) of the QLoRA projections' one-GEMM LoRA linears
+    (soup_gemm_bf16_lora: y = a op(b) + a2 op(b2)) at m tokens, with the
+    stream-K tail on (default threshold), forced on every tail
+    (soup_gemm_set_stream_k_min_saved(0)) and off, and of cuBLAS's GEMM plus its
+    accumulating rank-r GEMM. Each is a CUDA graph of `reps` launches replayed
+    5 times; the variants alternate `rounds` times (medians), since the GPU's
+    power-capped clock drifts over a run."""
+    import statistics
+
+    import torch.nn.functional as F
+
+    from auspex_soup_demo_b200 import _lib, qlora
+
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev).manual_seed(9)
+
+    def timed(fn):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(reps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del graph
+        return e0.elapsed_time(e1) / (5 * reps) * 1e3
+
+    def rnd(*shape):
+        return (0.5 * torch.randn(*shape, device=dev, generator=g)).to(torch.bfloat16)
+
+    lib = _lib.lib()
+    out = {}
+    # (name, K, N, rank, B stored [K, N] (the input-gradient GEMMs) or [N, K])
+    for name, k, n, r, mn in (("qkv_fwd", 1536, 2048, 48, False), ("qkv_dx", 2048, 1536, 48, True),
+                              ("o_fwd", 1536, 1536, 16, False), ("o_dx", 1536, 1536, 16, True),
+                              ("down_fwd", 8960, 1536, 16, False), ("gate_up_dx", 17920, 1536, 32, True)):
+        a, a2 = rnd(m, k), rnd(m, r)
+        b, b2 = (rnd(k, n), rnd(r, n)) if mn else (rnd(n, k), rnd(n, r))
+        c = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+
+        def ours():
+            qlora.lora_gemm(a, b, mn, a2, b2, c)
+
+        def cublas():
+            y = a @ b if mn else F.linear(a, b)
+            y.addmm_(a2, b2 if mn else b2.t())
+
+        t = {"tail_default": [], "tail_forced": [], "tail_off": [], "cublas": []}
+        try:
+            for _ in range(rounds):
+                for mode in t:
+                    _lib.set_stream_k(mode != "tail_off")
+                    lib.soup_gemm_set_stream_k_min_saved(0 if mode == "tail_forced" else -1)
+                    t[mode].append(timed(cublas if mode == "cublas" else ours))
+        finally:
+            _lib.set_stream_k(True)
+            lib.soup_gemm_set_stream_k_min_saved(-1)
+        flop = 2 * m * n * (k + r)
+        med = {mode: statistics.median(v) for mode, v in t.items()}
+        out[name] = {**{f"{mode}_us": round(v, 2) for mode, v in med.items()},
+                     "tflops_tail_default": round(flop / med["tail_default"] / 1e6, 1),
+                     "tflops_cublas": round(flop / med["cublas"] / 1e6, 1),
+                     "tiles": -(-m // 256) * -(-n // 256)}
+    return {"shape": f"{m} tokens; microseconds per launch (medians of {rounds} alternating rounds)",
+            "gemms": out}
+
+
 def time_gate_up_gemm(group, m: int, dev, reps: int = 20, recompute: bool = False):
     """CUDA-event duration of the gate/up GEMM + SwiGLU epilogue launch at m tokens,
     the QLoRA step's largest kernel, in the modes the step runs: the forward that
@@ -1204,6 +1285,13 @@ def run_section(args):
         cub = sum(v[1] for p in rk["products"].values() for v in p.values())
         res = {"metric": "LoRA rank products per layer, kernel / cuBLAS time", "value": round(kern / cub, 3),
                "unit": "ratio", "higher_is_better": False, "dtype": "bf16", **rk}
+    elif args.workload == "gemm":
+        pg = time_projection_gemms(args.batch * (args.seq or QLORA_SEQ), R.dev, reps=max(args.steps, 1))
+        ours = sum(v["tail_default_us"] for v in pg["gemms"].values())
+        cub = sum(v["cublas_us"] for v in pg["gemms"].values())
+        res = {"metric": "QLoRA projection GEMMs per layer, tcgen05 (stream-K tail) / cuBLAS time",
+               "value": round(ours / cub, 3), "unit": "ratio", "higher_is_better": False, "dtype": "bf16",
+               **pg}
     elif args.workload == "gateup":
         from auspex_soup_demo_b200 import qlora
 
@@ -1232,7 +1320,7 @@ def main():
                     help="default line: skip the nested ce / mem_ops / ce_vp / qlora_s512 results")
     ap.add_argument("--workload", default="step",
                     choices=["step", "qlora", "ce", "rmsnorm", "swiglu", "rope", "ce_vp", "gateup",
-                             "attention", "mlp_bwd", "rank"],
+                             "attention", "mlp_bwd", "rank", "gemm"],
                     help="step (default): the QLoRA train step with the other results nested; "
                          "qlora: the step alone; ce: the fused head CE; rmsnorm/swiglu/rope: one "
                          "memory-bound op's HBM GB/s; ce_vp: the vocab-parallel CE over all ranks; "
@@ -1240,7 +1328,8 @@ def main():
                          "this library's attention against torch SDPA at the step's shape; mlp_bwd: "
                          "down_proj's dX GEMM with the SwiGLU backward in its epilogue against the "
                          "unfused pair; rank: the LoRA rank products on soup_lora_rank_gemm against "
-                         "cuBLAS")
+                         "cuBLAS; gemm: the projections' LoRA GEMMs with the stream-K tail on, "
+                         "forced and off, against cuBLAS")
     ap.add_argument("--sustained-steps", type=int, default=500,
                     help="ce: extra back-to-back steps timed under the power cap (0: skip)")
     ap.add_argument("--tokens", type=int, default=65536, help="ce_vp: tokens per step")

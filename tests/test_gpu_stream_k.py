@@ -7,8 +7,8 @@ shapes below give every case of that split: fewer tiles than pairs (every
 tile in parts), whole waves plus a tail, tails whose tiles have only a few k
 blocks (a tile in several short parts), the rank-r k-block of the LoRA GEMM
 inside a part, ragged edges, fp32 and bf16 (TMA-store) outputs, accumulate,
-and the SwiGLU epilogue (whose warps read two separate column runs of a
-tile). Each result is checked against an fp32 matmul, against the same launch
+the SwiGLU epilogue (whose warps read two separate column runs of a tile),
+the fused CE's logits and dW epilogues and the fused MLP backward. Each result is checked against an fp32 matmul, against the same launch
 with the stream-K tail turned off, and for bitwise repeatability.
 """
 
@@ -44,14 +44,15 @@ def _both(fn):
     """fn() with the stream-K tail on (twice) and off; the device error word stays 0."""
     try:
         _lib.set_stream_k(True)
+        dev = torch.device("cuda")
         on1 = fn()
         on2 = fn()
         torch.cuda.synchronize()
-        assert _lib.device_error(on1.device) == 0
+        assert _lib.device_error(dev) == 0
         _lib.set_stream_k(False)
         off = fn()
         torch.cuda.synchronize()
-        assert _lib.device_error(off.device) == 0
+        assert _lib.device_error(dev) == 0
     finally:
         _lib.set_stream_k(True)
     return on1, on2, off
@@ -142,3 +143,59 @@ def test_stream_k_tail_swiglu_epilogue_equals_plain_gemm_plus_swiglu(m):
     y2 = plain.view(-1, 2 * qlora.IL_BLOCK)
     h_ref = swiglu_forward(y2[:, :qlora.IL_BLOCK], y2[:, qlora.IL_BLOCK:]).view(m, inter)
     assert torch.equal(h, h_ref)
+
+
+def test_stream_k_tail_fused_ce_logits_and_dweight():
+    """The fused head CE with every GEMM tail forced to stream-K (the logits GEMM's
+    online-softmax epilogue, the dW GEMM) against the same call with the tail off:
+    per-token losses and entropies within fp32 accumulation error, hits equal,
+    dhidden and dW at cosine >= 0.9999 (the fp32 sums differ only in order)."""
+    from auspex_soup_demo_b200.kernels.chunked_ce import fused_linear_cross_entropy
+
+    n, v, d = 1000, 33000, 1536  # logits 4 x 129 tiles, dW 129 x 6 tiles: both leave a partial wave
+    g = torch.Generator(device="cuda").manual_seed(21)
+    h = torch.randn(n, d, device="cuda", generator=g).to(torch.bfloat16)
+    w = (0.02 * torch.randn(v, d, device="cuda", generator=g)).to(torch.bfloat16)
+    t = torch.randint(0, v, (n,), device="cuda", generator=g)
+    t[::10] = -100
+
+    def run():
+        return fused_linear_cross_entropy(h, w, t, denominator=float((t != -100).sum()), compute_dw=True)
+
+    on1, on2, off = _both(run)
+    for a, b in zip(on1, on2):
+        assert torch.equal(a, b)
+    loss_on, ent_on, hit_on, _, dh_on, dw_on = on1
+    loss_off, ent_off, hit_off, _, dh_off, dw_off = off
+    assert (loss_on - loss_off).abs().max().item() <= 1e-4 * loss_off.abs().max().item()
+    assert (ent_on - ent_off).abs().max().item() <= 1e-4 * ent_off.abs().max().item()
+    assert torch.equal(hit_on, hit_off)
+    cos = torch.nn.functional.cosine_similarity
+    assert cos(dh_on.float().flatten(), dh_off.float().flatten(), dim=0).item() >= 0.9999
+    assert cos(dw_on.float().flatten(), dw_off.float().flatten(), dim=0).item() >= 0.9999
+
+
+def test_stream_k_tail_fused_mlp_backward_epilogue():
+    """The down projection's dX GEMM with the SwiGLU backward in its epilogue, tail
+    forced to stream-K, against the same GEMM with a plain epilogue (also forced)
+    followed by the SwiGLU backward kernel: bit-identical [dg | du]."""
+    from auspex_soup_demo_b200.kernels.swiglu import swiglu_backward
+
+    m, inter, k, r = 2048, 2048, 1536, 16  # 8 x 8 tiles < 74 CTA pairs: every tile in k parts
+    g = torch.Generator(device="cuda").manual_seed(33)
+    d = torch.randn(m, k, device="cuda", generator=g).bfloat16()
+    w = (0.05 * torch.randn(k, inter, device="cuda", generator=g)).bfloat16()
+    dxa = torch.randn(m, r, device="cuda", generator=g).bfloat16()
+    As = (0.05 * torch.randn(r, inter, device="cuda", generator=g)).bfloat16()
+    y = torch.randn(m, 2 * inter, device="cuda", generator=g).bfloat16()
+    _lib.set_stream_k(True)
+    dh = qlora.lora_gemm(d, w, True, dxa, As, torch.empty(m, inter, device="cuda", dtype=torch.bfloat16))
+    y2 = y.view(-1, 256)
+    dy_ref = torch.empty_like(y)
+    d2 = dy_ref.view(-1, 256)
+    swiglu_backward(dh.view(-1, 128), y2[:, :128], y2[:, 128:], dg=d2[:, :128], du=d2[:, 128:])
+    yy = y.clone()
+    qlora.dswiglu_gemm(d, w, dxa, As, yy)
+    torch.cuda.synchronize()
+    assert _lib.device_error(torch.device("cuda")) == 0
+    assert torch.equal(yy, dy_ref)

@@ -108,6 +108,9 @@ _SIGNATURES = {
                                     c_vp]),
     "soup_lora_rank_gemm": (c_int, [c_vp, c_i64, c_int, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64,
                                     c_vp, c_i64, c_vp, c_i64, c_int, c_f, c_vp]),
+    "soup_lora_rank_dual_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64]),
+    "soup_lora_rank_dual": (c_int, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64,
+                                    c_vp, c_i64, c_vp, c_sz, c_vp]),
     "soup_lora_rank_grad_group": (c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_int,
                                           c_vp, c_vp, c_vp, c_vp, c_f, c_vp]),
 }

@@ -377,6 +377,252 @@ __global__ void __launch_bounds__(kRankThreads, 3)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Both rank products of one output gradient in one pass over it:
+//   dxa = dy Bt^T   [m, r]   (dy K-major, Bt [r, n])
+//   G   = dy^T Xt^T [n, r]   (dy MN-major, Xt = xa^T [r, m])
+// A CTA owns rt x ct tiles of 128 x 128 of dy (rows x columns). Each
+// tile is loaded once (two TMA boxes of 128 rows x 64 columns, 128-byte
+// swizzle) and feeds two MMAs: as the K-major A of its row tile's dxa
+// accumulator (K = its 128 columns) and, the same bytes read as an MN-major
+// operand, as the A of its column tile's G accumulator (M = its 128 columns,
+// K = its 128 rows). The rt + ct accumulators (NP fp32 columns each) share
+// the 512 TMEM columns; the launcher picks rt and ct for the shape. The CTA leaves its fp32 partials in a workspace,
+// dxa per column block and G per row block, and dual_reduce_kernel sums them
+// in block order (bitwise reproducible).
+template <int NP>
+struct DualSmem {
+  static constexpr int kMaxAcc = 512 / NP;          // rt + ct accumulators fit in TMEM
+  static constexpr int kDyBytes = 128 * 128 * 2;    // one 128 x 128 tile of dy
+  static constexpr int kFacBytes = NP * 64 * 2;     // one box of a factor: NP rows x 64
+  static constexpr int kStage = kDyBytes + 4 * kFacBytes;  // dy, Bt (2 boxes), Xt (2 boxes)
+  static constexpr int kStages = 4 * kStage + 2048 <= 232448 ? 4 : 3;
+  static constexpr int kBar = kStages * kStage;
+  static constexpr int kNumBars = 2 * kStages + 1;  // full[S], empty[S], acc_full
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kUsed = kMisc + 16;
+  static constexpr int kBytes = kUsed + 1024;  // + alignment slack
+};
+
+struct DualArgs {
+  int m, n;           // dy [m, n]
+  int mt, nt;         // 128-row and 128-column tiles of dy
+  int rt, ct;         // row and column tiles per CTA (rt + ct <= 512 / NP)
+  int rb, cb;         // CTA blocks along rows and columns (grid = rb * cb)
+  uint64_t wait_ns;
+  float* ws_dxa;      // [cb][m][NP]: dxa partial of each column block
+  float* ws_g;        // [rb][n][NP]: G partial of each row block
+};
+
+template <int NP>
+__global__ void __launch_bounds__(kRankThreads, 1)
+    dual_rank_kernel(const __grid_constant__ CUtensorMap tma_d, const __grid_constant__ CUtensorMap tma_bt,
+                     const __grid_constant__ CUtensorMap tma_xt, const DualArgs a, int* err) {
+  using L = DualSmem<NP>;
+  const int RT = a.rt, CT = a.ct;
+  constexpr int S = L::kStages;
+  constexpr uint32_t kIdescK = idesc_bf16(NP, false, false, 128);
+  constexpr uint32_t kIdescMN = idesc_bf16(NP, true, false, 128);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  if ((uint32_t)(smem - smem_raw) + L::kUsed > rank_dynamic_smem()) {  // grid-uniform
+    if (threadIdx.x == 0) atomicCAS(err, 0, kErrRankSmem);
+    return;
+  }
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + L::kBar;
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (S + s); };
+  const uint32_t acc_bar = bar0 + 8u * (2 * S);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bi = blockIdx.x / a.cb, bj = blockIdx.x - (blockIdx.x / a.cb) * a.cb;
+  const int i_n = min(RT, a.mt - bi * RT), j_n = min(CT, a.nt - bj * CT);  // tiles inside dy
+  const uint64_t wait_ns = a.wait_ns ? a.wait_ns : kWaitNs;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < L::kNumBars; ++i) mbar_init(bar0 + 8u * i, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tma_prefetch_desc(&tma_d);
+    tma_prefetch_desc(&tma_bt);
+    tma_prefetch_desc(&tma_xt);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  pdl_wait();
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer ----
+      int it = 0;
+      bool ok = true;
+      for (int j = 0; j < j_n && ok; ++j) {
+        for (int i = 0; i < i_n; ++i, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!bounded_wait(empty_bar(s), ph ^ 1u, abort_flag, err, kErrRankProducer, wait_ns)) {
+            ok = false;
+            break;
+          }
+          const uint32_t d_dst = sbase + s * L::kStage;
+          const uint32_t bt_dst = d_dst + L::kDyBytes;
+          const uint32_t xt_dst = bt_dst + 2 * L::kFacBytes;
+          const int r0 = (bi * RT + i) * 128, c0 = (bj * CT + j) * 128;
+          mbar_arrive_expect_tx(full_bar(s), L::kStage);
+          tma_load_2d(d_dst, &tma_d, full_bar(s), c0, r0);
+          tma_load_2d(d_dst + 16384, &tma_d, full_bar(s), c0 + 64, r0);
+          tma_load_2d(bt_dst, &tma_bt, full_bar(s), c0, 0);
+          tma_load_2d(bt_dst + L::kFacBytes, &tma_bt, full_bar(s), c0 + 64, 0);
+          tma_load_2d(xt_dst, &tma_xt, full_bar(s), r0, 0);
+          tma_load_2d(xt_dst + L::kFacBytes, &tma_xt, full_bar(s), r0 + 64, 0);
+        }
+      }
+      // let the copies still in flight land before the CTA may leave (bounded)
+      const int n_wait = it < S ? it : S;
+      for (int q = 1; q <= n_wait; ++q) {
+        const int jj = it - q;
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(full_bar(jj % S), (jj / S) & 1u) && globaltimer() - t0 < wait_ns) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ----------------------------------------------- MMA issuer ----
+      int it = 0;
+      bool ok = true, issued = false;
+      for (int j = 0; j < j_n && ok; ++j) {
+        for (int i = 0; i < i_n; ++i, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!bounded_wait(full_bar(s), ph, abort_flag, err, kErrRankMma, wait_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_addr = sbase + s * L::kStage;
+          const uint32_t bt_addr = d_addr + L::kDyBytes;
+          const uint32_t xt_addr = bt_addr + 2 * L::kFacBytes;
+          // dxa(row tile i) += dy tile . Bt^T over the tile's 128 columns
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = smem_desc_sw128(d_addr + h * 16384 + kk * 32, 16, 1024);
+              const uint64_t bd = smem_desc_sw128(bt_addr + h * L::kFacBytes + kk * 32, 16, 1024);
+              tc_mma_bf16(tmem + i * NP, ad, bd, kIdescK, (j > 0 || h > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          // G(column tile j) += dy tile^T . Xt^T over the tile's 128 rows: the
+          // same bytes as an MN-major operand (64-column boxes 16 KB apart)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = smem_desc_sw128(d_addr + kk * 2048, 16384, 1024);
+            const uint64_t bd = smem_desc_sw128(xt_addr + (kk >> 2) * L::kFacBytes + (kk & 3) * 32, 16, 1024);
+            tc_mma_bf16(tmem + (RT + j) * NP, ad, bd, kIdescMN, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued = true;
+          tc_commit(empty_bar(s));
+        }
+      }
+      if (issued) {
+        tc_commit(acc_bar);
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(acc_bar, 0) && globaltimer() - t0 < wait_ns) {
+        }
+      } else {
+        mbar_arrive(acc_bar);
+      }
+    }
+  } else {
+    // ------------------------------------------------------ epilogue ----
+    const int quarter = warp & 3;
+    bool ok = true;
+    if (lane == 0) ok = bounded_wait(acc_bar, 0, abort_flag, err, kErrRankEpilogue, wait_ns);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    tc_fence_after();
+    if (ok && !*abort_flag) {
+      const uint32_t tl = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+      for (int t = 0; t < i_n + j_n; ++t) {
+        const bool is_dxa = t < i_n;
+        const int tile = is_dxa ? t : t - i_n;
+        float v[NP];
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < NP; c += 16)
+          tmem_ld16_nowait(tl + (is_dxa ? tile : RT + tile) * NP + c, v + c);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        const int row = ((is_dxa ? bi * RT : bj * CT) + tile) * 128 + quarter * 32 + lane;
+        if (row >= (is_dxa ? a.m : a.n)) continue;
+        float* dst = is_dxa ? a.ws_dxa + ((int64_t)bj * a.m + row) * NP
+                            : a.ws_g + ((int64_t)bi * a.n + row) * NP;
+#pragma unroll
+        for (int c = 0; c < NP; c += 4)
+          *reinterpret_cast<float4*>(dst + c) = make_float4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+  }
+}
+
+// dxa[m, :r] (bf16) = sum over the column blocks of ws_dxa; G[n, :r] (fp32) =
+// sum over the row blocks of ws_g; block order, four columns per thread.
+__global__ void __launch_bounds__(256) dual_reduce_kernel(const float* __restrict__ ws_dxa,
+                                                          const float* __restrict__ ws_g, int m, int n, int r,
+                                                          int np, int rb, int cb, bf16* __restrict__ dxa,
+                                                          int64_t lddxa, float* __restrict__ g, int64_t ldg) {
+  pdl_wait();
+  const int q = np / 4;
+  const int64_t n1 = (int64_t)m * q, total = n1 + (int64_t)n * q;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const bool is_dxa = idx < n1;
+    const int64_t e = is_dxa ? idx : idx - n1;
+    const int64_t row = e / q;
+    const int col = static_cast<int>(e - row * q) * 4;
+    if (col >= r) continue;
+    const int blocks = is_dxa ? cb : rb;
+    const int rows = is_dxa ? m : n;
+    const float* src = (is_dxa ? ws_dxa : ws_g) + row * np + col;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int b = 0; b < blocks; ++b) {
+      const float4 p = *reinterpret_cast<const float4*>(src + (int64_t)b * rows * np);
+      s.x += p.x;
+      s.y += p.y;
+      s.z += p.z;
+      s.w += p.w;
+    }
+    const float v[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (col + c >= r) break;
+      if (is_dxa) dxa[row * lddxa + col + c] = __float2bfloat16_rn(v[c]);
+      else g[row * ldg + col + c] = v[c];
+    }
+  }
+  pdl_trigger();
+}
+
 }  // namespace
 }  // namespace soup
 
@@ -548,10 +794,142 @@ int rank_prepare(const void* a, int64_t lda, int a_mn_major, const void* b, int6
   return SOUP_OK;
 }
 
+template <int NP>
+int dual_launch(const CUtensorMap& md, const CUtensorMap& mbt, const CUtensorMap& mxt, DualArgs args, int r,
+                bf16* dxa, int64_t lddxa, float* g, int64_t ldg, cudaStream_t stream) {
+  using L = DualSmem<NP>;
+  static_assert(L::kBytes <= 232448, "dual rank product shared memory exceeds 227 KB");
+  auto kern = dual_rank_kernel<NP>;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cuda_status(cudaErrorInvalidDevice);
+  int* err = device_err_ptr();
+  if (!err) {
+    set_last_error("device error word unavailable");
+    return SOUP_ERR_CUDA;
+  }
+  {
+    std::lock_guard<std::mutex> lock(cache_mutex());
+    if (!attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+      if (e != cudaSuccess) return cuda_status(e);
+      attr_done[dev] = true;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.blockDim = dim3(kRankThreads);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(args.rb * args.cb);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, md, mbt, mxt, args, err);
+  if (e != cudaSuccess) return cuda_status(e);
+  const int64_t items = ((int64_t)args.m + args.n) * (NP / 4);
+  int64_t blocks = (items + 255) / 256;
+  const int64_t cap = 4ll * num_sms();
+  if (blocks > cap) blocks = cap;
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, dual_reduce_kernel, static_cast<const float*>(args.ws_dxa),
+                                        static_cast<const float*>(args.ws_g), args.m, args.n, r, NP, args.rb,
+                                        args.cb, dxa, lddxa, g, ldg));
+}
+
+// accumulator width of the dual kernel: 16, 32 or 64 columns (TMEM offsets
+// i * NP stay multiples of NP)
+int dual_np(int64_t r) { return r <= 16 ? 16 : r <= 32 ? 32 : 64; }
+
+// Row and column tiles per CTA (rt + ct <= 512 / np accumulators): the
+// estimate is the slowest SM's share of dy (whole waves of CTAs, each
+// streaming rt x ct tiles at ~40 GB/s) plus the partials' HBM round trip.
+void dual_blocking(int64_t m, int64_t n, int np, int sms, int* rt, int* ct) {
+  const int64_t mt = (m + 127) / 128, nt = (n + 127) / 128;
+  double best = 1e30;
+  *rt = *ct = 1;
+  for (int a = 1; a < 512 / np; ++a) {
+    for (int b = 1; a + b <= 512 / np; ++b) {
+      if (a > mt || b > nt) continue;
+      const int64_t rb = (mt + a - 1) / a, cb = (nt + b - 1) / b;
+      const int64_t waves = (rb * cb + sms - 1) / sms;
+      const double t = waves * (double)a * b * 32768.0 / 40e9 + (double)(cb * m + rb * n) * np * 8.0 / 6e12;
+      if (t < best) {
+        best = t;
+        *rt = a;
+        *ct = b;
+      }
+    }
+  }
+}
+
 }  // namespace
 }  // namespace soup
 
 extern "C" {
+
+size_t soup_lora_rank_dual_workspace_bytes(int64_t m, int64_t n, int64_t r) {
+  using namespace soup;
+  if (m <= 0 || n <= 0 || r <= 0 || r > kRankMaxN || m > (1 << 30) || n > (1 << 30)) return 0;
+  int rt, ct;
+  dual_blocking(m, n, dual_np(r), num_sms(), &rt, &ct);
+  const int64_t rb = ((m + 127) / 128 + rt - 1) / rt, cb = ((n + 127) / 128 + ct - 1) / ct;
+  return (size_t)((cb * m + rb * n) * dual_np(r) * 4);
+}
+
+int soup_lora_rank_dual(const void* dy, int64_t lddy, const void* bt, int64_t ldbt, const void* xt,
+                        int64_t ldxt, int64_t m, int64_t n, int64_t r, void* dxa, int64_t lddxa, float* g,
+                        int64_t ldg, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace soup;
+  if (!dy || !bt || !xt || !dxa || !g || m <= 0 || n <= 0 || r <= 0 || r > kRankMaxN || m > (1 << 30) ||
+      n > (1 << 30)) {
+    set_last_error("soup_lora_rank_dual: bad arguments (r must be 1..64)");
+    return SOUP_ERR_INVALID;
+  }
+  if (lddy < n || ldbt < n || ldxt < m || lddxa < r || ldg < r) {
+    set_last_error("soup_lora_rank_dual: leading dimension too small");
+    return SOUP_ERR_INVALID;
+  }
+  if (!rank_tma_ok(dy, lddy) || !rank_tma_ok(bt, ldbt) || !rank_tma_ok(xt, ldxt)) {
+    set_last_error("soup_lora_rank_dual: operands need 16-byte aligned rows");
+    return SOUP_ERR_UNSUPPORTED;
+  }
+  const size_t need = soup_lora_rank_dual_workspace_bytes(m, n, r);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace)) {
+    set_last_error("soup_lora_rank_dual: workspace missing, unaligned or smaller than "
+                   "soup_lora_rank_dual_workspace_bytes()");
+    return SOUP_ERR_WORKSPACE;
+  }
+  const int np = dual_np(r);
+  CUtensorMap md, mbt, mxt;
+  int rc;
+  if ((rc = rank_map(&md, dy, (uint64_t)n, (uint64_t)m, (uint64_t)lddy, 128))) return rc;
+  if ((rc = rank_map(&mbt, bt, (uint64_t)n, (uint64_t)r, (uint64_t)ldbt, (uint32_t)np))) return rc;
+  if ((rc = rank_map(&mxt, xt, (uint64_t)m, (uint64_t)r, (uint64_t)ldxt, (uint32_t)np))) return rc;
+  DualArgs args{};
+  dual_blocking(m, n, np, num_sms(), &args.rt, &args.ct);
+  args.m = (int)m;
+  args.n = (int)n;
+  args.mt = (int)((m + 127) / 128);
+  args.nt = (int)((n + 127) / 128);
+  args.rb = (args.mt + args.rt - 1) / args.rt;
+  args.cb = (args.nt + args.ct - 1) / args.ct;
+  args.wait_ns = wait_limit_ns();
+  args.ws_dxa = static_cast<float*>(workspace);
+  args.ws_g = args.ws_dxa + (int64_t)args.cb * m * np;
+  bf16* d = static_cast<bf16*>(dxa);
+  cudaStream_t st = as_stream(stream);
+  switch (np) {
+    case 16: return dual_launch<16>(md, mbt, mxt, args, (int)r, d, lddxa, g, ldg, st);
+    case 32: return dual_launch<32>(md, mbt, mxt, args, (int)r, d, lddxa, g, ldg, st);
+    default: return dual_launch<64>(md, mbt, mxt, args, (int)r, d, lddxa, g, ldg, st);
+  }
+}
+
 
 int soup_lora_rank_gemm(const void* a, int64_t lda, int a_mn_major, const void* b, int64_t ldb, int64_t m,
                         int64_t n, int64_t k, void* c, int64_t ldc, void* ct, int64_t ldct, float* g,

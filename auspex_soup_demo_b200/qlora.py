@@ -164,6 +164,42 @@ def lora_gemm(a: torch.Tensor, b: torch.Tensor, b_mn_major: bool, a2: torch.Tens
     return out
 
 
+# A group's output gradient at least this wide, with at least DUAL_MIN_ROWS
+# tokens, takes dxa and the B-gradient product from one pass of
+# soup_lora_rank_dual: measured on B200 at the gate/up gradient [8192, 17920]
+# (rank 32) 76 us against 86.5 us for cuBLAS's two products; at 2048 tokens
+# (31 vs 24 us) and for the q/k/v gradient [8192, 2048] (26 vs 18 us) cuBLAS
+# is faster.
+DUAL_RANK = True
+DUAL_MIN_COLS = 8192
+DUAL_MIN_ROWS = 4096
+
+
+def _dual_ok(group, dy: torch.Tensor, xa: torch.Tensor, need_params) -> bool:
+    return (DUAL_RANK and dy.is_cuda and dy.dtype == torch.bfloat16 and xa.dtype == torch.bfloat16
+            and dy.dim() == 2 and dy.shape[1] >= DUAL_MIN_COLS and dy.shape[0] >= DUAL_MIN_ROWS
+            and dy.shape[0] % 8 == 0 and dy.shape[1] % 8 == 0 and dy.stride(1) == 1 and dy.stride(0) % 8 == 0
+            and dy.data_ptr() % 16 == 0 and xa.shape[1] <= 64
+            and any(need_params[2 * j + 1] for j in range(len(group.members))))
+
+
+def rank_dual(dy: torch.Tensor, bt: torch.Tensor, xt: torch.Tensor):
+    """(dxa = dy bt^T [M, R] bf16, G = dy^T xt^T [N, R] fp32) in one pass over
+    dy [M, N] (soup_lora_rank_dual): a LoRA group's dxa = dy B and the product
+    whose blocks are its members' B gradients, for bt = B^T [R, N] and
+    xt = xa^T [R, M]."""
+    m, n = dy.shape
+    r = bt.shape[0]
+    dxa = torch.empty(m, r, device=dy.device, dtype=torch.bfloat16)
+    G = torch.empty(n, r, device=dy.device, dtype=torch.float32)
+    nbytes = int(_lib.lib().soup_lora_rank_dual_workspace_bytes(m, n, r))
+    ws = _lib.scratch(dy.device, nbytes)
+    _lib.call("soup_lora_rank_dual", dy.device, dy.data_ptr(), dy.stride(0), bt.data_ptr(), bt.stride(0),
+              xt.data_ptr(), xt.stride(0), m, n, r, dxa.data_ptr(), dxa.stride(0), G.data_ptr(), G.stride(0),
+              ws.data_ptr(), nbytes, _lib.stream_of(dy))
+    return dxa, G
+
+
 def rank_gemm(a: torch.Tensor, b: torch.Tensor, a_mn_major: bool = False, c=None, ct=None, g=None,
               g_trans: bool = False, alpha: float = 1.0) -> None:
     """soup_lora_rank_gemm: C = op(a) b^T for a narrow b [n, K] (n <= 64), with
@@ -616,8 +652,13 @@ def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tens
     the forward's soup_lora_rank_gemm) the rank products run on that kernel:
     dxa and dxa^T in one pass over dy, gA into the stacked A gradient, and
     every member's gB in one more pass over dy."""
+    G = None
     if xaT is not None:
         dxa, dxaT = _rank_product(dy, group.factors_t(Bblk))
+    elif _dual_ok(group, dy, xa, need_params):
+        # dxa and G = dy^T xa (the members' B gradients) in one pass over dy
+        dxa, G = rank_dual(dy, group.factors_t(Bblk), xa.t().contiguous())
+        dxaT = None
     else:
         dxa, dxaT = dy @ Bblk, None
     dx = None
@@ -650,8 +691,7 @@ def _group_backward(group: LoRAProjectionGroup, dy: torch.Tensor, x2: torch.Tens
     # (member j's gradient is its output rows - row blocks when interleaved - and
     # rank columns of G); one accumulating product per member would re-read dy and
     # costs cuBLAS ~14 us each at 8192 tokens even for the 4 MB k / v gradients
-    G = None
-    if not gB_done and any(need_params[2 * j + 1] for j in range(len(group.members))):
+    if G is None and not gB_done and any(need_params[2 * j + 1] for j in range(len(group.members))):
         G = torch.mm(dy.t(), xa, out_dtype=torch.float32)
     for j, mem in enumerate(group.members):
         r0, r1 = group.rank_off[j], group.rank_off[j + 1]
@@ -1265,7 +1305,9 @@ class QLoRATrainer:
     def _refresh_bblk(self):
         for dst, src in self._bblk_copies:
             dst.copy_(src)
-        if RANK_KERNELS:  # after the block-diagonal copies they read
+        # the transposed copies: operands of the rank kernels and of the dual
+        # product (after the block-diagonal copies they read)
+        if RANK_KERNELS or DUAL_RANK:
             for dst, src in self._t_copies:
                 dst.copy_(src)
 

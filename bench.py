@@ -323,6 +323,7 @@ def measure_qlora(args, R: Ranks, batch: int, seq: int, with_extras: bool = True
     from auspex_soup_demo_b200.kernels import swiglu as _swiglu
     _swiglu.RECOMPUTE = bool(args.recompute)
     qlora.RANK_KERNELS = bool(getattr(args, "rank_kernels", False))
+    qlora.DUAL_RANK = not bool(getattr(args, "no_dual_rank", False))
     dev = R.dev
     model = qlora.build_qwen2_qlora(qlora.qwen2_1p5b_config(num_layers=args.layers,
                                                             attention=args.attention),
@@ -542,7 +543,16 @@ def time_rank_products(m: int, dev, reps: int = 20):
             "gB_us": [timed(lambda: qlora.rank_gemm(dy, xat, a_mn_major=True, g=gb)),
                       timed(lambda: torch.addmm(gb, dy.t(), xa, out_dtype=torch.float32, out=gb))],
         }
-    return {"shape": f"{m} tokens; [kernel, cuBLAS] microseconds per product", "products": out}
+    # both products of the gate/up gradient in one pass (soup_lora_rank_dual) against cuBLAS's two
+    dy, bt = rnd(m, 17920), 0.05 * rnd(32, 17920)
+    xa = rnd(m, 32)
+    b = bt.t().contiguous()
+    xt = xa.t().contiguous()
+    dual = {"dxa_and_dyT_xa_us": [timed(lambda: qlora.rank_dual(dy, bt, xt)),
+                                  timed(lambda: (dy @ b, torch.mm(dy.t(), xa, out_dtype=torch.float32)))],
+            "shape": f"dy [{m}, 17920], rank 32"}
+    return {"shape": f"{m} tokens; [kernel, cuBLAS] microseconds per product", "products": out,
+            "dual": dual}
 
 
 def time_projection_gemms(m: int, dev, reps: int = 40, rounds: int = 3):
@@ -1205,7 +1215,9 @@ def run_step(args):
                    "lora": "r16 a32 q/k/v/o/gate/up/down", "lora_params": q["lora_params"],
                    "base": "NF4 blocksize 64, dequantised per use", "optimizer": "AdamW 2e-4",
                    "mlp_recompute": bool(args.recompute), "attention": args.attention,
-                   "rank_products": "soup_lora_rank_gemm" if args.rank_kernels else "cuBLAS",
+                   "rank_products": "soup_lora_rank_gemm" if args.rank_kernels else
+                                    ("cuBLAS; gate/up dxa + dy^T xa on soup_lora_rank_dual at >= 4096 tokens"
+                                     if not args.no_dual_rank else "cuBLAS"),
                    "parallelism": f"dp{R.world}" + (" (one NCCL all-reduce of the flat fp32 LoRA "
                                                     "gradient per step)" if R.world > 1 else ""),
                    "l2": "weights and activations far larger than L2"},
@@ -1346,6 +1358,9 @@ def main():
     ap.add_argument("--recompute", action="store_true",
                     help="step/qlora: recompute gate/up in the MLP backward, as the reference does "
                          "(default: keep [g | u] from the forward; same results, more memory)")
+    ap.add_argument("--no-dual-rank", action="store_true",
+                    help="step/qlora: the gate/up group's dxa and B-gradient products on cuBLAS instead "
+                         "of one soup_lora_rank_dual pass")
     ap.add_argument("--rank-kernels", action="store_true",
                     help="step/qlora: LoRA rank products on soup_lora_rank_gemm (default: cuBLAS, "
                          "faster in the step)")

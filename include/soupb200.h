@@ -400,6 +400,20 @@ int soup_lora_rank_grad_group(const void* a, int64_t lda, const void* b, int64_t
                               const int64_t* col_off, float* const* g, const int64_t* ldg, float alpha,
                               void* stream);
 
+/* Both rank products of one LoRA output gradient dy [m, n] in one pass over it
+ * (no reference counterpart; replaces peft's two products through cuBLAS,
+ * dxa = dy B and gB = dy^T xa, for the wide gate/up gradient):
+ *   dxa [m, r] bf16 = dy bt^T     bt = B^T [r, n] (row stride ldbt)
+ *   g   [n, r] fp32 = dy^T xt^T   xt = xa^T [r, m] (row stride ldxt), written (not added)
+ * r <= 64. Each 128 x 128 tile of dy is loaded once and feeds both tcgen05
+ * products; fp32 partials of each CTA block go to `workspace` (at least
+ * soup_lora_rank_dual_workspace_bytes(m, n, r), 16-byte aligned) and a second
+ * kernel sums them in a fixed order. */
+size_t soup_lora_rank_dual_workspace_bytes(int64_t m, int64_t n, int64_t r);
+int soup_lora_rank_dual(const void* dy, int64_t lddy, const void* bt, int64_t ldbt, const void* xt,
+                        int64_t ldxt, int64_t m, int64_t n, int64_t r, void* dxa, int64_t lddxa, float* g,
+                        int64_t ldg, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- AdamW over flat fp32 buffers (the QLoRA step's optimiser) ------------
  * One pass over n elements: param, exp_avg, exp_avg_sq updated in place from
  * grad with torch.optim.AdamW's decoupled weight decay; `step` is a device

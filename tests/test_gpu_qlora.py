@@ -447,3 +447,30 @@ def test_rank_kernels_give_matching_gradients(group, monkeypatch):
         assert abs(a - b) <= 1e-3 * abs(b), (l1, l2)
     worst = min(cosine(g1[k], g2[k]) for k in g2)
     assert worst > 0.9995, worst
+
+
+def test_dual_rank_product_gives_matching_gradients(monkeypatch):
+    # the gate/up group's dxa and B-gradient product from one pass over its
+    # output gradient (soup_lora_rank_dual) against cuBLAS's two products,
+    # through the trainer; the width limits are lowered so the small model's
+    # gate/up gradient [192, 1280] takes the kernel. dxa is rounded to bf16 after
+    # fp32 sums in a different order, as in the rank-kernel comparison above
+    apply()
+    monkeypatch.setattr(qlora, "DUAL_MIN_COLS", 1024)
+    monkeypatch.setattr(qlora, "DUAL_MIN_ROWS", 128)
+    g = torch.Generator().manual_seed(15)
+    ids = torch.randint(0, 2048, (2, 96), generator=g).cuda()
+    labels = qlora.causal_labels(ids)
+    den = float((labels != -100).sum())
+    out = {}
+    for dual in (True, False):
+        monkeypatch.setattr(qlora, "DUAL_RANK", dual)
+        trainer = qlora.QLoRATrainer(_small_model_grouped(16, True), lr=1e-3)
+        losses = [float(trainer.step(ids, labels, den)[0]) for _ in range(2)]
+        grads = {n: p.grad.clone() for n, p in trainer.model.named_parameters() if p.requires_grad}
+        out[dual] = (losses, grads)
+    (l1, g1), (l2, g2) = out[True], out[False]
+    for a, b in zip(l1, l2):
+        assert abs(a - b) <= 1e-3 * abs(b), (l1, l2)
+    worst = min(cosine(g1[k], g2[k]) for k in g2)
+    assert worst > 0.9995, worst

@@ -10,6 +10,8 @@ accumulations within 1e-4 relative to the largest magnitude.
 import pytest
 import torch
 
+from auspex_soup_demo_b200 import _lib
+
 pytestmark = pytest.mark.gpu
 
 
@@ -96,3 +98,40 @@ def test_rank_product_argument_errors():
     with pytest.raises(_lib.SoupError):  # no output
         qlora.rank_gemm(x, a)
     assert _lib.device_error(x.device) == 0
+
+
+@pytest.mark.parametrize("m,n,r", [(8192, 17920, 32), (1000, 3000, 16), (304, 704, 48), (2048, 4096, 64),
+                                   (136, 144, 8)])
+def test_rank_dual_matches_fp32(m, n, r):
+    """soup_lora_rank_dual: dxa = dy B and G = dy^T xa from one pass over dy,
+    against fp32 products of the same bf16 operands (dxa rounded once to bf16,
+    G in fp32), ragged edges and ranks 8-64; results bitwise repeatable."""
+    from auspex_soup_demo_b200 import qlora
+
+    # TMA operands: rows of dy, B^T and xa^T 16-byte aligned (m, n multiples of 8)
+    g = torch.Generator(device="cuda").manual_seed(m + n + r)
+    dy = torch.randn(m, n, device="cuda", generator=g).bfloat16()
+    B = (0.05 * torch.randn(n, r, device="cuda", generator=g)).bfloat16()
+    xa = torch.randn(m, r, device="cuda", generator=g).bfloat16()
+    bt, xt = B.t().contiguous(), xa.t().contiguous()
+    dxa, G = qlora.rank_dual(dy, bt, xt)
+    dxa2, G2 = qlora.rank_dual(dy, bt, xt)
+    torch.cuda.synchronize()
+    assert _lib.device_error(dy.device) == 0
+    assert torch.equal(dxa, dxa2) and torch.equal(G, G2)
+    ref_dxa = dy.float() @ B.float()
+    ref_G = dy.float().t() @ xa.float()
+    # bf16 output: within one rounding of the fp32 result (8e-3 of the largest entry)
+    assert (dxa.float() - ref_dxa).abs().max().item() <= 8e-3 * ref_dxa.abs().max().item()
+    tol = 1e-5 * max(1.0, (m / 1536) ** 0.5)
+    assert (G - ref_G).abs().max().item() <= tol * ref_G.abs().max().item()
+
+
+def test_rank_dual_rejects_unaligned_rows():
+    from auspex_soup_demo_b200 import qlora
+
+    dy = torch.zeros(300, 700, device="cuda", dtype=torch.bfloat16)
+    bt = torch.zeros(16, 700, device="cuda", dtype=torch.bfloat16)
+    xt = torch.zeros(16, 300, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(_lib.SoupError):
+        qlora.rank_dual(dy, bt, xt)

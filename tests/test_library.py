@@ -165,3 +165,32 @@ def test_wait_limit_setting_is_validated_on_the_host():
     assert lib.soup_set_wait_limit_ns(0) == _lib.SOUP_OK  # back to the 2 s default
     st = lib.soup_gemm_wait_expiry_check(None, None, None, 256, 256, 256, 1_000_000, None)
     assert st == _lib.SOUP_ERR_INVALID
+
+
+def test_stream_k_and_dual_rank_entry_points_validate_on_the_host():
+    lib = _lib.lib()
+    # stream-K scratch: one 256 KB fp32 slot per CTA pair plus the ready flags
+    # (the library assumes 148 SMs when no GPU is visible)
+    assert lib.soup_gemm_stream_k_workspace_bytes() >= 74 * 256 * 1024
+    assert lib.soup_gemm_set_stream_k_min_saved(-1) == _lib.SOUP_OK
+    fake = ctypes.c_void_p(256)  # never dereferenced: validation fails first
+    m, n, r = 8192, 17920, 32
+    ws = lib.soup_lora_rank_dual_workspace_bytes(m, n, r)
+    # 8 x 8 tiles of 128 x 128 per CTA: dxa partials of 18 column blocks, G partials of 8 row blocks
+    assert ws == (18 * m + 8 * n) * 32 * 4
+    assert lib.soup_lora_rank_dual_workspace_bytes(m, n, 65) == 0
+    args = [fake, n, fake, n, fake, m, m, n, r, fake, r, fake, r, fake, ws, None]
+
+    def call(**over):
+        a = list(args)
+        for i, v in over.items():
+            a[int(i[1:])] = v
+        return lib.soup_lora_rank_dual(*a)
+
+    assert call(a0=None) == _lib.SOUP_ERR_INVALID                 # no dy
+    assert call(a8=80, a10=80, a12=80) == _lib.SOUP_ERR_INVALID   # rank above 64
+    assert call(a1=n - 8) == _lib.SOUP_ERR_INVALID                # dy row stride shorter than a row
+    assert call(a5=m - 8) == _lib.SOUP_ERR_INVALID                # xa^T row stride shorter than a row
+    assert call(a1=n + 3) == _lib.SOUP_ERR_UNSUPPORTED            # rows not 16-byte aligned
+    assert call(a14=ws - 16) == _lib.SOUP_ERR_WORKSPACE           # workspace too small
+    assert call(a13=None) == _lib.SOUP_ERR_WORKSPACE              # no workspace

@@ -241,12 +241,19 @@ def i64_array(values):
 
 
 def device_error(device: torch.device) -> int:
-    """Read and clear the device error word (synchronises the current stream)."""
+    """Read and clear the device error word (synchronises the current stream).
+    After a GEMM wait error (codes 0x101-0x104) the device's stream-K buffer is
+    zeroed again, since an aborted launch may have left ready flags set."""
     out = c_int(0)
     with torch.cuda.device(device):
         check("soup_device_error",
               lib().soup_device_error(torch.cuda.current_stream(device).cuda_stream,
                                       ctypes.byref(out)))
+        idx = torch.cuda.current_device()
+        if 0x101 <= out.value <= 0x104 and _sk_buffers.get(idx) is not None:
+            torch.cuda.synchronize(idx)
+            _sk_buffers[idx].zero_()
+            torch.cuda.synchronize(idx)
     return out.value
 
 

@@ -104,5 +104,5 @@ def test_schedule_invariants_at_the_qlora_shapes():
 
 def test_schedule_invariants_for_random_shapes_with_every_tail_forced():
     rng = random.Random(0)
-    for _ in range(3000):
-        check(rng.randint(1, 2000), rng.randint(1, 300), min_saved=0)
+    for _ in range(400):
+        check(rng.randint(1, 600), rng.randint(1, 120), min_saved=0)
